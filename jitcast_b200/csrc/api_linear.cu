@@ -1,0 +1,174 @@
+// C-ABI entry points of the op-level GEMM: jc_linear (host buffers) and jc_linear_device
+// (HBM-resident buffers), with the epilogue flags of the reference's Kernels.gemm
+// (tornado/Kernels.java:50-102) and the operator of Ops.linear (cpu/Ops.java:33-51).
+#include <cstring>
+#include <string>
+
+#include "gemm.h"
+#include "kernels.cuh"
+#include "runtime.h"
+
+using namespace jc;
+
+namespace {
+
+enum Slot { kSlotA = 0, kSlotALo, kSlotW, kSlotWLo, kSlotAF32, kSlotWF32, kSlotBias, kSlotC };
+
+int op_of(jc_precision p) { return p == JC_BF16 ? kOpBF16 : p == JC_TF32 ? kOpTF32 : kOpSplit; }
+
+// Maps Kernels.gemm flags to an activation; false for flags this engine rejects.
+bool act_of(int flags, int* act, std::string* why) {
+  const int known = JC_BIAS | JC_ACCUMULATE | JC_SILU | JC_RELU | JC_GELU | JC_TWIN_ONLY;
+  if (flags & ~known) {
+    *why = "unknown flag bits " + std::to_string(flags & ~known);
+    return false;
+  }
+  if (flags & JC_TWIN_ONLY) {
+    *why = "JC_TWIN_ONLY writes only an FP16 twin of C and does not apply to an FP32 C";
+    return false;
+  }
+  const bool silu = flags & JC_SILU, relu = flags & JC_RELU, gelu = flags & JC_GELU;
+  if (gelu && (silu || relu)) {
+    *why = "JC_GELU cannot be combined with JC_SILU or JC_RELU";
+    return false;
+  }
+  *act = silu && relu ? kActSiluRelu : silu ? kActSilu : relu ? kActRelu : gelu ? kActGelu : kActNone;
+  return true;
+}
+
+bool valid_precision(int p) { return p == JC_FP32 || p == JC_TF32 || p == JC_BF16; }
+
+// Converts fp32 A [rows, cols] (pitch ld) into the operand buffers of slot pair (hi, lo),
+// K padded to a multiple of 64 elements.
+bool stage_operand(DeviceRt* rt, int op, const float* src, long long ld, long long rows, int cols, int slot_hi,
+                   int slot_lo, void** hi, void** lo, long long* ldp, cudaStream_t s) {
+  const long long kp = round_up(cols, 64);
+  const size_t esz = op == kOpBF16 ? 2 : 4;
+  *hi = scratch(rt, slot_hi, rows * kp * esz);
+  *lo = op == kOpSplit ? scratch(rt, slot_lo, rows * kp * esz) : nullptr;
+  if (!*hi || (op == kOpSplit && !*lo)) return false;
+  launch_convert(op, src, ld, *hi, *lo, kp, rows, cols, s);
+  *ldp = kp;
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* jc_version(void) { return "jitcast_b200 0.1.0 (sm_100a)"; }
+
+const char* jc_last_error(void) { return last_error(); }
+
+int jc_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+// Enqueues the GEMM on `s`; the caller holds rt->mu with the device current.
+static jc_status linear_locked(DeviceRt* rt, jc_precision precision, const float* a, long long lda, const float* w,
+                               long long ldw, const float* bias, float* c, long long ldc, int m, int n, int k,
+                               int flags, int act, cudaStream_t s) {
+  const int op = op_of(precision);
+  GemmArgs g{};
+  g.op = op;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  void *ahi, *alo, *whi, *wlo;
+  long long lda_p, ldw_p;
+  if (!stage_operand(rt, op, a, lda, m, k, kSlotA, kSlotALo, &ahi, &alo, &lda_p, s) ||
+      !stage_operand(rt, op, w, ldw, n, k, kSlotW, kSlotWLo, &whi, &wlo, &ldw_p, s))
+    return fail(JC_ERR_OOM, "scratch allocation failed");
+  g.a_hi = ahi;
+  g.a_lo = alo;
+  g.lda = lda_p;
+  g.w_hi = whi;
+  g.w_lo = wlo;
+  g.ldw = ldw_p;
+  g.ep = epi_default();
+  g.ep.act = act;
+  g.ep.bias_on = (flags & JC_BIAS) != 0;
+  g.ep.bias = bias;
+  g.ep.accumulate = (flags & JC_ACCUMULATE) != 0;
+  g.ep.c = c;
+  g.ep.ldc = ldc;
+  g.ep.cin = c;
+  g.ep.ldcin = ldc;
+  if (const char* msg = check_gemm(g)) return fail(JC_ERR_UNSUPPORTED_SHAPE, msg);
+  cudaError_t e = launch_gemm(g, s, rt->err);
+  if (e != cudaSuccess) return fail_cuda(e, "GEMM launch");
+  return JC_OK;
+}
+
+jc_status jc_linear_device(int device, jc_precision precision, const float* a, long long lda, const float* w,
+                           long long ldw, const float* bias, float* c, long long ldc, int m, int n, int k, int flags,
+                           void* stream) {
+  clear_error();
+  if (!valid_precision(precision)) return fail(JC_ERR_INVALID_ARG, "unknown precision");
+  if (m < 1 || n < 1 || k < 1) return fail(JC_ERR_INVALID_ARG, "m, n and k must be positive");
+  if (!a || !w || !c) return fail(JC_ERR_INVALID_ARG, "null buffer");
+  if ((flags & JC_BIAS) && !bias) return fail(JC_ERR_INVALID_ARG, "JC_BIAS without a bias");
+  if (lda < k || ldw < k || ldc < n) return fail(JC_ERR_INVALID_ARG, "leading dimension smaller than the row");
+  int act = 0;
+  std::string why;
+  if (!act_of(flags, &act, &why)) return fail(JC_ERR_INVALID_ARG, why);
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  return linear_locked(rt, precision, a, lda, w, ldw, bias, c, ldc, m, n, k, flags, act,
+                       static_cast<cudaStream_t>(stream));
+}
+
+jc_status jc_linear(int device, jc_precision precision, const float* a, const float* w, const float* bias, float* c,
+                    int m, int n, int k, int flags) {
+  clear_error();
+  if (!valid_precision(precision)) return fail(JC_ERR_INVALID_ARG, "unknown precision");
+  if (m < 1 || n < 1 || k < 1) return fail(JC_ERR_INVALID_ARG, "m, n and k must be positive");
+  if (!a || !w || !c) return fail(JC_ERR_INVALID_ARG, "null buffer");
+  if ((flags & JC_BIAS) && !bias) return fail(JC_ERR_INVALID_ARG, "JC_BIAS without a bias");
+  int act = 0;
+  std::string why;
+  if (!act_of(flags, &act, &why)) return fail(JC_ERR_INVALID_ARG, why);
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  float* da = static_cast<float*>(scratch(rt, kSlotAF32, sizeof(float) * (size_t)m * k));
+  float* dw = static_cast<float*>(scratch(rt, kSlotWF32, sizeof(float) * (size_t)n * k));
+  float* dc = static_cast<float*>(scratch(rt, kSlotC, sizeof(float) * (size_t)m * n));
+  float* db = (flags & JC_BIAS) ? static_cast<float*>(scratch(rt, kSlotBias, sizeof(float) * (size_t)n)) : nullptr;
+  if (!da || !dw || !dc || ((flags & JC_BIAS) && !db)) return fail(JC_ERR_OOM, "device buffers for jc_linear");
+  cudaStream_t s = rt->stream;
+  cudaError_t e = cudaMemcpyAsync(da, a, sizeof(float) * (size_t)m * k, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dw, w, sizeof(float) * (size_t)n * k, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess && db) e = cudaMemcpyAsync(db, bias, sizeof(float) * n, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess && (flags & JC_ACCUMULATE))
+    e = cudaMemcpyAsync(dc, c, sizeof(float) * (size_t)m * n, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return fail_cuda(e, "upload");
+  jc_status st = linear_locked(rt, precision, da, k, dw, k, db, dc, n, m, n, k, flags, act, s);
+  if (st != JC_OK) return st;
+  e = cudaMemcpyAsync(c, dc, sizeof(float) * (size_t)m * n, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return fail_cuda(e, "download");
+  return take_device_error(rt);
+}
+
+jc_status jc_device_sync(int device) {
+  clear_error();
+  std::string why;
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail_cuda(e, "device synchronize");
+  return take_device_error(rt);
+}
+
+}  // extern "C"

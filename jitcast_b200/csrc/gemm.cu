@@ -1,0 +1,629 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a with a fused epilogue.
+//
+//   C[m, n] (+)= act(rs[m]·(A[m, :]·W[n, :]) + b[n])      A [M, K], W [N, K], both K-major
+//
+// One CTA per SM walks output tiles of 128 × BN. Warp 0 streams A and W K-slices into a
+// ring of shared-memory stages with TMA (128-byte swizzle); warp 1 issues tcgen05.mma into
+// one of two TMEM accumulators (128 lanes × BN fp32 columns each); warps 2-5 drain the
+// other accumulator with tcgen05.ld and run the epilogue (bias, activation, residual add,
+// FP32 store, operand-typed copy for the next GEMM, SwiGLU pairing, RoPE, sigmoid gate)
+// straight from registers to HBM, so no separate elementwise kernel touches C.
+//
+// The semantics follow the reference's shared GEMM kernel (Kernels.gemm, Kernels.java:59-102):
+// bias, then SiLU or ReLU, then the accumulate of C; and its CPU operator Ops.linear
+// (Ops.java:33-51) for y = x·Wᵀ + b.
+#include "gemm.h"
+#include "ptx.cuh"
+
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <mutex>
+
+namespace jc {
+
+template <int BN_, int OPK_>
+struct Cfg {
+  static constexpr int BN = BN_;
+  static constexpr int OPK = OPK_;
+  static constexpr int BM = 128;
+  static constexpr int ESZ = OPK == kOpBF16 ? 2 : 4;
+  static constexpr int BK = 128 / ESZ;   // K elements per 128-byte swizzled row
+  static constexpr int UK = 32 / ESZ;    // K per tcgen05.mma (32 bytes)
+  static constexpr int NSUB = BK / UK;   // MMAs per stage per product
+  static constexpr int NOP = OPK == kOpSplit ? 2 : 1;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = NOP * (A_BYTES + B_BYTES);
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : 2u, BM, BN);
+  static_assert(STAGES >= 2, "too few stages");
+  static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
+};
+
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+
+// ---- epilogue helpers ---------------------------------------------------------------------
+__device__ __forceinline__ float apply_act(int act, float v) {
+  switch (act) {
+    case kActSilu: return silu_f(v);
+    case kActRelu: return fmaxf(v, 0.0f);
+    case kActGelu: return gelu_f(v);
+    case kActSigmoid: return sigmoid_f(v);
+    case kActSiluRelu: return fmaxf(silu_f(v), 0.0f);
+    default: return v;
+  }
+}
+
+__device__ __forceinline__ void add_bias(const EpiParams& p, int col0, int nv, float (&v)[32]) {
+  if (nv == 32 && p.vec_ok) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 b = __ldg(b4 + q);
+      v[4 * q] += b.x;
+      v[4 * q + 1] += b.y;
+      v[4 * q + 2] += b.z;
+      v[4 * q + 3] += b.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nv) v[j] += __ldg(p.bias + col0 + j);
+  }
+}
+
+// Writes 32 (or nv) fp32 values of one row to an fp32 buffer.
+__device__ __forceinline__ void store_f32(float* dst, int nv, bool vec, const float (&v)[32]) {
+  if (nv == 32 && vec) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nv) dst[j] = v[j];
+  }
+}
+
+__device__ __forceinline__ void store_bf16(__nv_bfloat16* dst, int nv, bool vec, const float (&v)[32]) {
+  if (nv == 32 && vec) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 u;
+      __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+      __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+      __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+      __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+      u.x = *reinterpret_cast<uint32_t*>(&t0);
+      u.y = *reinterpret_cast<uint32_t*>(&t1);
+      u.z = *reinterpret_cast<uint32_t*>(&t2);
+      u.w = *reinterpret_cast<uint32_t*>(&t3);
+      d4[q] = u;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nv) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+// The operand-typed copy of a row chunk (for the next GEMM's A).
+__device__ __forceinline__ void store_operand(const EpiParams& p, long long off, int nv, const float (&v)[32]) {
+  const bool vec = p.vec_ok != 0;
+  switch (p.o_kind) {
+    case kOutBF16:
+      store_bf16(static_cast<__nv_bfloat16*>(p.o_hi) + off, nv, vec, v);
+      break;
+    case kOutF32:
+      store_f32(static_cast<float*>(p.o_hi) + off, nv, vec, v);
+      break;
+    case kOutTF32: {
+      float t[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) t[j] = round_tf32(v[j]);
+      store_f32(static_cast<float*>(p.o_hi) + off, nv, vec, t);
+      break;
+    }
+    case kOutSplit: {
+      float hi[32], lo[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        hi[j] = round_tf32(v[j]);
+        lo[j] = v[j] - hi[j];
+      }
+      store_f32(static_cast<float*>(p.o_hi) + off, nv, vec, hi);
+      store_f32(static_cast<float*>(p.o_lo) + off, nv, vec, lo);
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+// Bias → activation → accumulate → stores, for one row's 32-column chunk.
+__device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int orow, int col0, int nv,
+                                                float (&v)[32], float& sq) {
+  if (p.row_scale) {
+    const float s = p.row_scale[row];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= s;
+  }
+  if (p.bias_on) add_bias(p, col0, nv, v);
+  if (p.act != kActNone) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = apply_act(p.act, v[j]);
+  }
+  if (p.accumulate) {
+    const float* src = p.cin + (long long)orow * p.ldcin + col0;
+    if (nv == 32 && p.vec_ok) {
+      const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 c = s4[q];
+        v[4 * q] += c.x;
+        v[4 * q + 1] += c.y;
+        v[4 * q + 2] += c.z;
+        v[4 * q + 3] += c.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < nv) v[j] += src[j];
+    }
+  }
+  if (p.c) store_f32(p.c + (long long)orow * p.ldc + col0, nv, p.vec_ok != 0, v);
+  if (p.o_kind != kOutNone) store_operand(p, (long long)orow * p.ldo + col0, nv, v);
+  if (p.rowsq) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nv) sq += v[j] * v[j];
+  }
+}
+
+__device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(taddr, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// One accumulator tile (rows m0.., columns n0..) → HBM, for the thread's row.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, int m0, int n0, uint32_t tbase,
+                                              int row_in_tile) {
+  const int row = m0 + row_in_tile;
+  const bool live = row < M;
+  const int orow = live ? (row / p.rg) * p.rg_stride + row % p.rg + p.rg_off : 0;
+  float sq = 0.0f;
+  if (p.mode == kEpiPlain) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col0 = n0 + 32 * c;
+      if (col0 >= N) break;  // warp-uniform
+      float v[32];
+      load_chunk(tbase + 32 * c, v);
+      if (live) epi_plain_chunk(p, row, orow, col0, min(32, N - col0), v, sq);
+    }
+  } else if (p.mode == kEpiSwiGLU) {
+    // tile columns (64u .. 64u+31) are the SiLU half of output columns (n0/2 + 32u ..), (64u+32 ..) the linear half
+#pragma unroll 1
+    for (int u = 0; u < BN / 64; ++u) {
+      const int col0 = n0 + 64 * u;
+      if (col0 >= N) break;
+      float a[32], b[32];
+      load_chunk(tbase + 64 * u, a);
+      load_chunk(tbase + 64 * u + 32, b);
+      if (live) {
+        if (p.bias_on) {
+          add_bias(p, col0, 32, a);
+          add_bias(p, col0 + 32, 32, b);
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) a[j] = silu_f(a[j]) * b[j];
+        const int ocol = col0 / 2;
+        store_operand(p, (long long)orow * p.ldo + ocol, min(32, N / 2 - ocol), a);
+      }
+    }
+  } else {  // kEpiQKV
+    const int hd = p.head_dim, half = hd / 2;
+    if (n0 >= p.n_split) {
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col0 = n0 + 32 * c;
+        if (col0 >= N) break;
+        float v[32];
+        load_chunk(tbase + 32 * c, v);
+        if (live) {
+          if (p.bias_on) add_bias(p, col0, min(32, N - col0), v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = sigmoid_f(v[j]);
+          const long long off = (long long)orow * p.ldg + (col0 - p.n_split);
+          const int nv = min(32, N - col0);
+          if (p.g_bf16)
+            store_bf16(static_cast<__nv_bfloat16*>(p.g_out) + off, nv, p.vec_ok != 0, v);
+          else
+            store_f32(static_cast<float*>(p.g_out) + off, nv, p.vec_ok != 0, v);
+        }
+      }
+    } else {
+      const int pos = live ? p.pos[row] : 0;
+#pragma unroll 1
+      for (int h0 = 0; h0 < BN; h0 += hd) {
+#pragma unroll 1
+        for (int s = 0; s < half; s += 32) {
+          const int ca = h0 + s, cb = h0 + half + s;
+          if (n0 + ca >= N) break;
+          float a[32], b[32];
+          load_chunk(tbase + ca, a);
+          load_chunk(tbase + cb, b);
+          if (!live) continue;
+          if (p.bias_on) {
+            add_bias(p, n0 + ca, 32, a);
+            add_bias(p, n0 + cb, 32, b);
+          }
+          if (n0 + ca < p.rope_cols) {
+            const float* tc = p.rope_table + (long long)pos * hd + s;
+            const float* ts = tc + half;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float cs = __ldg(tc + j), sn = __ldg(ts + j);
+              const float x = a[j], y = b[j];
+              a[j] = x * cs + -y * sn;
+              b[j] = y * cs + x * sn;
+            }
+          }
+          store_operand(p, (long long)orow * p.ldo + n0 + ca, 32, a);
+          store_operand(p, (long long)orow * p.ldo + n0 + cb, 32, b);
+        }
+      }
+    }
+  }
+  if (p.rowsq && live) atomicAdd(p.rowsq + orow, sq);
+}
+
+// ---- the kernel -----------------------------------------------------------------------------
+template <int BN, int OPK>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, int M,
+                   int N, int K, EpiParams ep, uint32_t* err) {
+  using C = Cfg<BN, OPK>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_blks = (M + C::BM - 1) / C::BM, n_blks = (N + BN - 1) / BN;
+  const int tiles = m_blks * n_blks;
+  const int kblks = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (OPK == kOpSplit) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
+        for (int kb = 0; kb < kblks; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1) || *abort_flag) {
+            atomicOr(err, kErrTimeoutEmpty);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(full + stage, C::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, full + stage, kb * C::BK, m0);
+          tma_load_2d(sb, &tmB, full + stage, kb * C::BK, n0);
+          if (OPK == kOpSplit) {
+            tma_load_2d(sb + C::B_BYTES, &tmA2, full + stage, kb * C::BK, m0);
+            tma_load_2d(sb + C::B_BYTES + C::A_BYTES, &tmB2, full + stage, kb * C::BK, n0);
+          }
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // let the copies still in flight land before the CTA's shared memory goes away
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < C::STAGES && i < issued; ++i) {
+          if (--s < 0) {
+            s = C::STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(full + s, ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag) {
+          atomicOr(err, kErrTimeoutAccFree);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < kblks; ++kb) {
+          if (!mbar_wait(full + stage, phase) || *abort_flag) {
+            atomicOr(err, kErrTimeoutFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::NSUB; ++k) {
+            const uint64_t ad = sdesc_k_sw128(sa + 32 * k);
+            const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if (OPK == kOpBF16) {
+              umma_bf16(d, ad, bd, C::IDESC, acc);
+            } else if (OPK == kOpTF32) {
+              umma_tf32(d, ad, bd, C::IDESC, acc);
+            } else {
+              const uint64_t ad2 = sdesc_k_sw128(sb + C::B_BYTES + 32 * k);
+              const uint64_t bd2 = sdesc_k_sw128(sb + C::B_BYTES + C::A_BYTES + 32 * k);
+              umma_tf32(d, ad2, bd, C::IDESC, acc);  // lo·hi
+              umma_tf32(d, ad, bd2, C::IDESC, 1u);   // hi·lo
+              umma_tf32(d, ad, bd, C::IDESC, 1u);    // hi·hi
+            }
+          }
+          umma_commit(empty + stage);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(acc_full + buf);
+      }
+      // every MMA this thread issued has completed once `drain` flips
+      umma_commit(drain);
+      mbar_wait(drain, 0);
+    }
+  } else {
+    // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const bool got = mbar_wait(acc_full + buf, aph);
+      const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
+      if (!all) {
+        if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+      epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile);
+      tc_fence_before();
+      mbar_arrive(acc_empty + buf);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A 2-D K-major tensor map: `rows` rows of `k` elements, `ld` elements apart; box = 128 bytes × box_rows.
+static bool make_map(CUtensorMap* map, const void* base, int op, long long rows, long long k, long long ld,
+                     int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return false;
+  const int esz = op == kOpBF16 ? 2 : 4;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * esz)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, op == kOpBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+EpiParams epi_default() {
+  EpiParams p{};
+  p.rg = 1 << 30;
+  p.rg_stride = 1 << 30;
+  p.rg_off = 0;
+  p.vec_ok = 0;
+  return p;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+const char* check_gemm(const GemmArgs& g) {
+  if (g.M < 1 || g.N < 1 || g.K < 1) return "M, N and K must be positive";
+  if (g.op < kOpBF16 || g.op > kOpSplit) return "unknown operand kind";
+  const int esz = g.op == kOpBF16 ? 2 : 4;
+  if (!g.a_hi || !g.w_hi) return "null operand";
+  if (g.op == kOpSplit && (!g.a_lo || !g.w_lo)) return "split operands need hi and lo buffers";
+  if (!aligned16(g.a_hi) || !aligned16(g.w_hi) || (g.a_lo && !aligned16(g.a_lo)) || (g.w_lo && !aligned16(g.w_lo)))
+    return "operand base addresses must be 16-byte aligned";
+  if ((g.lda * esz) % 16 != 0 || (g.ldw * esz) % 16 != 0) return "operand row pitch must be a multiple of 16 bytes";
+  if (g.lda < g.K || g.ldw < g.K) return "leading dimension smaller than K";
+  const EpiParams& e = g.ep;
+  if (e.mode == kEpiSwiGLU && (g.N % 64 != 0)) return "SwiGLU GEMM needs N % 64 == 0";
+  if (e.mode == kEpiQKV) {
+    if (e.head_dim % 64 != 0) return "fused RoPE needs head_dim % 64 == 0";
+    if (e.n_split % 256 != 0 || e.rope_cols % e.head_dim != 0) return "fused q|k|v|gate layout";
+    if (!e.pos || !e.rope_table) return "fused RoPE needs positions and a table";
+  }
+  if (e.accumulate && !e.cin) return "accumulate without C input";
+  if (e.bias_on && !e.bias) return "bias flag without bias";
+  if (e.rg < 1) return "row group must be positive";
+  return nullptr;
+}
+
+template <int BN, int OPK>
+static cudaError_t launch_cfg(const GemmArgs& g, cudaStream_t stream, uint32_t* err, int num_sms) {
+  using C = Cfg<BN, OPK>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, OPK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
+  CUtensorMap ma, mb, ma2, mb2;
+  if (!make_map(&ma, g.a_hi, OPK, g.M, g.K, g.lda, C::BM) || !make_map(&mb, g.w_hi, OPK, g.N, g.K, g.ldw, BN))
+    return cudaErrorInvalidValue;
+  if (OPK == kOpSplit) {
+    if (!make_map(&ma2, g.a_lo, OPK, g.M, g.K, g.lda, C::BM) || !make_map(&mb2, g.w_lo, OPK, g.N, g.K, g.ldw, BN))
+      return cudaErrorInvalidValue;
+  } else {
+    ma2 = ma;
+    mb2 = mb;
+  }
+  const int tiles = ((g.M + C::BM - 1) / C::BM) * ((g.N + BN - 1) / BN);
+  const int grid = tiles < num_sms ? tiles : num_sms;
+  gemm_tc_kernel<BN, OPK><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, ma2, mb2, g.M, g.N, g.K, g.ep, err);
+  return cudaGetLastError();
+}
+
+static int sm_count() {
+  static int count[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!count[dev & 63]) {
+    int c = 0;
+    cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
+    count[dev & 63] = c > 0 ? c : 148;
+  }
+  return count[dev & 63];
+}
+
+// The widest tile that still gives every SM a tile, else the narrowest.
+static int choose_bn(const GemmArgs& g, int num_sms) {
+  if (g.bn) return g.bn;
+  const int m_blks = (g.M + 127) / 128;
+  int need = 64;
+  if (g.ep.mode == kEpiQKV) need = 256;  // the gate split sits on a 256-column boundary
+  for (int bn : {256, 128}) {
+    if (bn < need) break;
+    const long long tiles = (long long)m_blks * ((g.N + bn - 1) / bn);
+    if (tiles >= num_sms) return bn;
+  }
+  if (g.N <= 64 && need <= 64) return 64;
+  if (need > 128) return 256;
+  return g.N <= 128 || (long long)m_blks * ((g.N + 127) / 128) >= num_sms / 2 ? 128 : 64;
+}
+
+// Whether every epilogue pointer and pitch allows 16-byte vector access.
+static int vector_ok(const EpiParams& e) {
+  auto ok = [](const void* p, long long ld, int esz) {
+    return p == nullptr || (aligned16(p) && (ld * esz) % 16 == 0);
+  };
+  const int oesz = e.o_kind == kOutBF16 ? 2 : 4;
+  return ok(e.c, e.ldc, 4) && ok(e.cin, e.ldcin, 4) && ok(e.bias, 0, 4) && ok(e.o_hi, e.ldo, oesz) &&
+         ok(e.o_lo, e.ldo, oesz) && ok(e.g_out, e.ldg, e.g_bf16 ? 2 : 4);
+}
+
+cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err) {
+  if (check_gemm(gin)) return cudaErrorInvalidValue;
+  GemmArgs g = gin;
+  g.ep.vec_ok = vector_ok(g.ep);
+  const int sms = sm_count();
+  const int bn = choose_bn(g, sms);
+#define JC_LAUNCH(BN_)                                                  \
+  switch (g.op) {                                                       \
+    case kOpBF16: return launch_cfg<BN_, kOpBF16>(g, stream, err, sms); \
+    case kOpTF32: return launch_cfg<BN_, kOpTF32>(g, stream, err, sms); \
+    default: return launch_cfg<BN_, kOpSplit>(g, stream, err, sms);     \
+  }
+  if (bn == 256) {
+    JC_LAUNCH(256)
+  } else if (bn == 128) {
+    JC_LAUNCH(128)
+  } else {
+    JC_LAUNCH(64)
+  }
+#undef JC_LAUNCH
+}
+
+}  // namespace jc

@@ -1,0 +1,102 @@
+// The tcgen05 GEMM engine's host-visible types: operand kinds, the fused-epilogue
+// parameters and the launch entry. C[m, n] (+)= act(A[m, :]·W[n, :] + b[n]) with A [M, K]
+// and W [N, K] both K-major (PyTorch [out, in] weights), the accumulator in TMEM.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace jc {
+
+// How GEMM operands are stored in HBM.
+enum OperandKind : int {
+  kOpBF16 = 0,   // bfloat16; tcgen05 kind::f16
+  kOpTF32 = 1,   // fp32 container rounded to TF32; kind::tf32
+  kOpSplit = 2,  // fp32 as a TF32 hi/lo pair; three kind::tf32 MMAs (hi·hi + hi·lo + lo·hi)
+};
+
+// How an epilogue writes its operand-typed copy of the result.
+enum OutKind : int {
+  kOutNone = 0,
+  kOutBF16 = 1,
+  kOutTF32 = 2,   // fp32, rounded to TF32
+  kOutSplit = 3,  // fp32 hi (TF32) and lo (residual) buffers
+  kOutF32 = 4,    // fp32, unrounded
+};
+
+// kActSiluRelu is the reference's SILU|RELU flag pair: ReLU(SiLU(v)).
+enum Activation : int { kActNone = 0, kActSilu = 1, kActRelu = 2, kActGelu = 3, kActSigmoid = 4, kActSiluRelu = 5 };
+
+enum EpiMode : int {
+  kEpiPlain = 0,
+  // Output columns come in 32-column pairs (silu half, linear half); writes N/2 columns of
+  // SiLU(first)·second to the operand output.
+  kEpiSwiGLU = 1,
+  // Fused q|k|v|gate projection: RoPE on columns < rope_cols (per head of head_dim, pairs
+  // e and e + head_dim/2), columns >= n_split go through a sigmoid to the gate output.
+  kEpiQKV = 2,
+};
+
+// Flags, as the reference's Kernels.gemm (BIAS=1, ACCUMULATE=2, SILU=4, RELU=16) plus GELU=32.
+constexpr int kFlagBias = 1;
+constexpr int kFlagAccumulate = 2;
+constexpr int kFlagSilu = 4;
+constexpr int kFlagTwinOnly = 8;
+constexpr int kFlagRelu = 16;
+constexpr int kFlagGelu = 32;
+
+struct EpiParams {
+  int mode;        // EpiMode
+  int act;         // Activation, applied after the bias
+  int bias_on;
+  int accumulate;  // C = C_in + act(...)
+  const float* bias;
+  float* c;        // fp32 output, row-remapped; may be null
+  long long ldc;
+  const float* cin;  // residual input for accumulate (usually == c)
+  long long ldcin;
+  void* o_hi;      // operand-typed output (OutKind); o_lo only for kOutSplit
+  void* o_lo;
+  long long ldo;
+  int o_kind;
+  // Row remap of the outputs: out_row = (r / rg) * rg_stride + r % rg + rg_off.
+  int rg, rg_stride, rg_off;
+  // kEpiQKV
+  int rope_cols, head_dim;
+  const int* pos;           // [M] index into rope_table rows
+  const float* rope_table;  // [positions, head_dim]: cos at e, sin at head_dim/2 + e
+  int n_split;
+  void* g_out;  // gate output (sigmoid), fp32 or bf16
+  long long ldg;
+  int g_bf16;
+  // Optional: Σ over the row of the fp32 output squared, atomically added per row.
+  float* rowsq;
+  // Optional: each output row scaled by row_scale[r] before the bias (a folded RMSNorm).
+  const float* row_scale;
+  int vec_ok;  // all output pointers / leading dims allow 16-byte vector access
+};
+
+struct GemmArgs {
+  int op;  // OperandKind
+  const void* a_hi;
+  const void* a_lo;
+  long long lda;  // elements
+  const void* w_hi;
+  const void* w_lo;
+  long long ldw;
+  int M, N, K;
+  int bn;  // 0 = choose
+  EpiParams ep;
+};
+
+// Returns a zero-initialised EpiParams with the identity row remap.
+EpiParams epi_default();
+
+// Launches one GEMM on `stream`. `err` is a device word the kernel ORs error bits into.
+// Returns cudaSuccess or the launch error; shape errors are reported as cudaErrorInvalidValue.
+cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream, uint32_t* err);
+
+// Checks the alignment and shape rules of launch_gemm; returns nullptr or a message.
+const char* check_gemm(const GemmArgs& g);
+
+}  // namespace jc

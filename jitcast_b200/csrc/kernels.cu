@@ -1,0 +1,101 @@
+// Memory-bound companion kernels: operand conversion (fp32 → bf16 / TF32 / TF32 hi-lo with
+// K padding), RMSNorm (optionally gathering the decoder tokens), and decoder-token fill.
+// Each is a grid-stride loop sized to the SM count; one warp owns one row where a row
+// reduction is needed.
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace jc {
+
+namespace {
+
+__device__ __forceinline__ void put(int kind, void* hi, void* lo, long long i, float v) {
+  switch (kind) {
+    case kOutBF16: static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v); break;
+    case kOutTF32: static_cast<float*>(hi)[i] = round_tf32(v); break;
+    case kOutSplit: {
+      const float h = round_tf32(v);
+      static_cast<float*>(hi)[i] = h;
+      static_cast<float*>(lo)[i] = v - h;
+      break;
+    }
+    default: static_cast<float*>(hi)[i] = v; break;
+  }
+}
+
+int out_kind_of(int op) { return op == kOpBF16 ? kOutBF16 : op == kOpTF32 ? kOutTF32 : kOutSplit; }
+
+__global__ void convert_kernel(int kind, const float* __restrict__ src, long long lds, void* hi, void* lo,
+                               long long ldd, long long rows, int cols) {
+  const long long total = rows * ldd;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / ldd;
+    const int c = static_cast<int>(i - r * ldd);
+    put(kind, hi, lo, i, c < cols ? src[r * lds + c] : 0.0f);
+  }
+}
+
+// One warp per output row.
+__global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w, int cols,
+                               float eps, int kind, void* hi, void* lo, long long ldy, long long rows, int grows,
+                               int gstride, int goff) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const long long src = grows > 0 ? (r / grows) * gstride + goff + r % grows : r;
+    const float* xr = x + src * ldx;
+    float ss = 0.0f;
+    for (int c = lane; c < cols; c += 32) ss += xr[c] * xr[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(ss) / cols + eps));
+    for (int c = lane; c < cols; c += 32) put(kind, hi, lo, r * ldy + c, xr[c] * inv * (w ? w[c] : 1.0f));
+  }
+}
+
+__global__ void fill_rows_kernel(float* x, long long ldx, const float* __restrict__ q, int cols, int rows, int enc,
+                                 int n) {
+  const int h = n - enc;
+  const long long total = (long long)rows * h * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int c = static_cast<int>(i % cols);
+    const long long t = i / cols;
+    const long long r = t / h;
+    const int tok = enc + static_cast<int>(t % h);
+    x[(r * n + tok) * ldx + c] = q[c];
+  }
+}
+
+int grid_for(long long work, int threads) {
+  long long b = (work + threads - 1) / threads;
+  const long long cap = 148LL * 16;
+  if (b > cap) b = cap;
+  return b < 1 ? 1 : static_cast<int>(b);
+}
+
+}  // namespace
+
+void launch_convert(int op, const float* src, long long lds, void* dst_hi, void* dst_lo, long long ldd,
+                    long long rows, int cols, cudaStream_t s) {
+  if (rows <= 0) return;
+  convert_kernel<<<grid_for(rows * ldd, 256), 256, 0, s>>>(out_kind_of(op), src, lds, dst_hi, dst_lo, ldd, rows,
+                                                           cols);
+}
+
+void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, float eps, int out_kind, void* y_hi,
+                    void* y_lo, long long ldy, long long rows, int gather_rows, int gather_stride, int gather_off,
+                    cudaStream_t s) {
+  if (rows <= 0) return;
+  rmsnorm_kernel<<<grid_for(rows * 32, 256), 256, 0, s>>>(x, ldx, w, cols, eps, out_kind, y_hi, y_lo, ldy, rows,
+                                                          gather_rows, gather_stride, gather_off);
+}
+
+void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int enc, int n, cudaStream_t s) {
+  const long long total = (long long)rows * (n - enc) * cols;
+  if (total <= 0) return;
+  fill_rows_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, ldx, q, cols, rows, enc, n);
+}
+
+}  // namespace jc

@@ -1,0 +1,27 @@
+// Launchers for the non-GEMM device kernels: operand conversion and packing, RMSNorm,
+// token assembly, attention and the small per-family companions.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "gemm.h"
+
+namespace jc {
+
+// dst[r, c] (operand kind `op`, row pitch ldd) = src[r, c] for c < cols, 0 for cols <= c < ldd.
+// src is fp32 with row pitch lds. For kOpSplit dst_lo receives the TF32 residual.
+void launch_convert(int op, const float* src, long long lds, void* dst_hi, void* dst_lo, long long ldd, long long rows,
+                    int cols, cudaStream_t s);
+
+// y[r, :] = x[r, :] · rsqrt(mean(x[r, :]²) + eps) · w  for rows r, written as operand kind `op`
+// (or fp32 for kOutF32). If gather_* is set, source row = (r / gather_rows) * gather_stride +
+// gather_off + r % gather_rows (selects the decoder tokens of each series row).
+void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, float eps, int out_kind, void* y_hi,
+                    void* y_lo, long long ldy, long long rows, int gather_rows, int gather_stride, int gather_off,
+                    cudaStream_t s);
+
+// x[(r·n + t), :] = q for every row r and decoder token t in [enc, n).
+void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int enc, int n, cudaStream_t s);
+
+}  // namespace jc

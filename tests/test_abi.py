@@ -1,0 +1,81 @@
+"""The C ABI without a GPU: the library loads, exports every entry point its header declares,
+and rejects bad arguments with the reference's fail-fast statuses before touching a device."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import jitcast_b200
+from jitcast_b200 import _lib
+
+HEADERS = sorted((Path(__file__).resolve().parent.parent / "include").glob("*.h"))
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(jc_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    assert "jc_linear" in declared_symbols()
+
+
+@pytest.mark.parametrize("name", declared_symbols())
+def test_library_exports(name):
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+
+
+def test_prototypes_cover_header():
+    missing = [n for n in declared_symbols() if n not in _lib.PROTOTYPES]
+    assert not missing, f"no ctypes prototype for {missing}"
+
+
+def test_version():
+    assert "sm_100a" in jitcast_b200.version()
+
+
+def _call_linear(**kw):
+    a = np.ones((4, 8), np.float32)
+    w = np.ones((3, 8), np.float32)
+    c = np.zeros((4, 3), np.float32)
+    args = dict(device=0, precision=_lib.BF16, a=a.ctypes.data, w=w.ctypes.data, bias=None, c=c.ctypes.data,
+                m=4, n=3, k=8, flags=0)
+    args.update(kw)
+    return _lib.lib().jc_linear(*args.values())
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(m=0), _lib.ERR_INVALID_ARG),
+    (dict(k=-1), _lib.ERR_INVALID_ARG),
+    (dict(precision=9), _lib.ERR_INVALID_ARG),
+    (dict(flags=_lib.BIAS), _lib.ERR_INVALID_ARG),        # bias flag without a bias
+    (dict(flags=_lib.TWIN_ONLY), _lib.ERR_INVALID_ARG),
+    (dict(flags=1 << 10), _lib.ERR_INVALID_ARG),
+    (dict(flags=_lib.GELU | _lib.SILU), _lib.ERR_INVALID_ARG),
+    (dict(a=None), _lib.ERR_INVALID_ARG),
+])
+def test_invalid_arguments(kw, status):
+    assert _call_linear(**kw) == status
+    assert _lib.last_error()
+
+
+def test_argument_errors_raise_value_error():
+    with pytest.raises(ValueError):
+        jitcast_b200.ops.gemm(np.ones((2, 3)), np.ones((4, 5)), None, None, 0)
+    with pytest.raises(jitcast_b200.JcArgumentError):
+        jitcast_b200.ops.gemm(np.ones((2, 3)), np.ones((4, 3)), None, None, _lib.TWIN_ONLY)
+
+
+def test_no_device_is_reported():
+    if _lib.lib().jc_device_count() > 0:
+        pytest.skip("a device is present")
+    st = _call_linear()
+    assert st == _lib.ERR_NO_DEVICE
+    assert "device" in _lib.last_error().lower()
