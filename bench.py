@@ -1,0 +1,318 @@
+"""Benchmark: Timestral-style forward passes on the B200 engine.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one forward pass of the whole box-scale batch (65,536 series by default, sharded evenly
+across the N ranks; each rank runs its series in chunks of up to 8,192 through one CUDA graph per
+chunk shape). Prints one JSON line on rank 0:
+
+* ``value``   series/s of the whole job, inputs already in HBM (jc_forward_timestral_device), device
+              time by CUDA events, max over ranks;
+* ``e2e``     the same metric through the host C-ABI call (jc_forward_timestral with host buffers,
+              host↔device copies inside the timed region);
+* ``roofline`` the dominant kernel (the tcgen05 GEMM) from a profiled forward on rank 0: algorithmic
+              FLOPs per launch ÷ its CUDA-event time, against the measured BF16 peak;
+* ``cpu_baseline`` the oracle (a C restatement of the reference's FP32 CPU forward; the reference is
+              Java and no JDK exists here) on a bounded sample, rank 0 at N = 1.
+
+``--impl reference`` times that CPU forward on the host cores instead (rank 0; other ranks exit).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "series forecasts/sec (Timestral-style config-3 model, box-scale batch of config 5)"
+UNIT = "series/s"
+
+
+def peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--series", type=int, default=65536, help="series per step, whole job")
+    ap.add_argument("--chunk", type=int, default=8192, help="series per forward call")
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--cpu-series", type=int, default=2, help="series in the CPU baseline sample")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def workload_config(args, world):
+    return {"workload": "config5: Timestral-style decoder (d 1024, 16 layers, 16 heads, SwiGLU 4096, patch 32, "
+                        "128 context tokens + 2 decoder tokens, 21 quantiles), random-init weights",
+            "series_per_step": args.series, "series_per_gpu": args.series // world, "chunk_series": args.chunk,
+            "context": 4096, "horizon_patches": 2, "tokens_per_series": 130, "precision": args.precision,
+            "parallelism": f"series-sharded x{world}, no collective",
+            "l2": "no flush: every forward's working set (GBs) is far larger than the 126 MB L2"}
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (self.out or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(cfg, weights, series: int):
+    """The oracle's CPU forward on `series` series of the same workload; returns (series/s, threads)."""
+    from jitcast_b200 import timestral as ts
+    from jitcast_b200 import workloads
+    from oracle import timestral as ots
+
+    x = workloads.sinusoid_noise(series, 4096, seed=12345)
+    b = ts.BlockInput(x, np.ones_like(x, bool), np.arange(series, dtype=np.int32), 2)
+    model = ots.Model(cfg, weights)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    model.predict_block(b, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return series / dt, threads
+
+
+def reference_arm(args, rank, world):
+    """The reference's CPU forward (C restatement) on the host cores, for the same metric."""
+    if rank != 0:
+        return 0
+    from jitcast_b200 import timestral as ts
+
+    cfg = ts.config3()
+    weights = ts.random_checkpoint(cfg, seed=0)
+    for _ in range(args.warmup):
+        cpu_sample(cfg, weights, 1)
+    vals, threads = [], 1
+    for _ in range(args.steps):
+        v, threads = cpu_sample(cfg, weights, args.cpu_series)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * args.cpu_series / value, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64-accumulate f32", "data": "synthetic",
+            "config": workload_config(args, world), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{args.cpu_series} series per step of the config-5 workload, "
+                                       "C restatement of CpuTimestral.predictBlock (no JDK on this image)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import ctypes
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from jitcast_b200 import _lib
+    from jitcast_b200 import timestral as ts
+    from jitcast_b200 import workloads
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+
+    cfg = ts.config3()
+    weights = ts.random_checkpoint(cfg, seed=0)
+    engine = ts.TimestralEngine(cfg, weights, devices=(local,), precision=args.precision)
+
+    per_rank = args.series // world
+    first = rank * per_rank
+    chunks = []
+    for c0 in range(first, first + per_rank, args.chunk):
+        n = min(args.chunk, first + per_rank - c0)
+        x = workloads.sinusoid_noise(n, 4096, seed=c0)  # chunk-seeded: the same series for every N
+        b = ts.BlockInput(x, np.ones_like(x, bool), np.arange(n, dtype=np.int32), 2)
+        lay = ts.BlockLayout.of(cfg, b)
+        prep = ts.BlockPrep.of(cfg, lay)
+        hin = ts.DeviceInputs.of(lay, prep)
+        d = {k: torch.from_numpy(np.ascontiguousarray(getattr(hin, k))).to(dev)
+             for k in ("tokens", "positions", "key_valid", "known", "role", "group_start", "group_end")}
+        raw = torch.empty(n * 2, cfg.patch_size * cfg.num_quantiles, device=dev)
+        blk = ts.Block(hin.rows, hin.encoder, hin.horizon, hin.context_patches, hin.covariates,
+                       *(d[k].data_ptr() for k in ("tokens", "positions", "key_valid", "known", "role",
+                                                   "group_start", "group_end")))
+        chunks.append((hin, d, raw, blk, n))
+    L = _lib.lib()
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+
+    def device_step():
+        for _, _, raw, blk, _ in chunks:
+            _lib.check(L.jc_forward_timestral_device(engine.handle, 0, ctypes.byref(blk), raw.data_ptr(),
+                                                     stream.cuda_stream))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        device_step()
+    torch.cuda.synchronize()
+    engine.sync()
+
+    barrier()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            device_step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    engine.sync()
+    barrier()
+    ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
+    value = args.series / (ms / 1000.0)
+
+    # end to end through the host C ABI: host buffers in, host raw outputs back, copies timed
+    for hin, _, _, _, _ in chunks[:1]:
+        engine.forward(hin)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    h2d = d2h = 0
+    for _ in range(args.steps):
+        for hin, _, _, _, n in chunks:
+            engine.forward(hin)
+            h2d += sum(getattr(hin, k).nbytes for k in ("tokens", "positions", "key_valid", "known", "role",
+                                                       "group_start", "group_end"))
+            d2h += n * 2 * cfg.patch_size * cfg.num_quantiles * 4
+    e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    barrier()
+
+    # kernel-class timings of one profiled forward (eager, CUDA events around every launch)
+    engine.set_option("profile", 1)
+    hin0, _, raw0, blk0, n0 = chunks[0]
+    _lib.check(L.jc_forward_timestral_device(engine.handle, 0, ctypes.byref(blk0), raw0.data_ptr(),
+                                             stream.cuda_stream))
+    torch.cuda.synchronize()
+    prof = engine.profile()
+    engine.set_option("profile", 0)
+    launches_per_forward = sum(v["launches"] for v in prof.values()) + 3  # + the 3 index-rebasing kernels
+    g = prof["gemm"]
+    gemm_ms = g["ms"] / g["launches"]
+    gemm_flops = g["flops"] / g["launches"]
+    pk, pk_kind = peaks()
+    peak_tf = pk.get("bf16_tflops_sustained", 1400.0)
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+    traffic = None
+    tf = ROOT / "profiles" / "gemm_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+
+    if rank != 0:
+        engine.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        v, threads = cpu_sample(cfg, weights, args.cpu_series)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{args.cpu_series} series of the config-5 workload through the C restatement of "
+                         "CpuTimestral.predictBlock (FP32, double accumulation; no JDK on this image)"}
+    total_gemm_share = g["ms"] / sum(v["ms"] for v in prof.values())
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
+            "config": workload_config(args, world),
+            "e2e": {"value": args.series / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
+                    "d2h_bytes_per_step": d2h // args.steps},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tf, "traffic": traffic,
+                         "kernel": "gemm_tc_kernel (tcgen05, all linear layers)",
+                         "peak_kind": f"{pk_kind} bf16 dense, sustained",
+                         "gemm_time_share": total_gemm_share},
+            "cpu_baseline": cpu, "clocks": clocks.summary(),
+            "gpu_launches": launches_per_forward * len(chunks) * args.steps,
+            "kernel_profile": {k: {"ms": v["ms"], "launches": v["launches"]} for k, v in prof.items()}}
+    print(json.dumps(line), flush=True)
+    engine.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

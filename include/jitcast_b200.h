@@ -10,6 +10,10 @@
  *   - cpu/Ops.java:33-51            Ops.linear (y = x·Wᵀ + b)                → jc_linear
  *   - tornado/Kernels.java:50-102   Kernels.gemm and its flags             → jc_linear, jc_linear_device
  *   - tornado/GemmMode.java:40-77   GemmMode (FP32 / TF32 / FP16 cuBLAS)   → jc_precision
+ *   - timestral/BlockForward.java:20-24 and timestral/tornado/TimestralForward.java:187-642
+ *       BlockForward.predictBlock's device forward (TimestralForward)   → jc_engine_create_timestral,
+ *                                                                          jc_forward_timestral
+ *   - tornado/PlanCache.java:40-162  per-shape plans, CUDA-graph replay → engine plans, jc_engine_set_option
  */
 #ifndef JITCAST_B200_H
 #define JITCAST_B200_H
@@ -85,9 +89,127 @@ jc_status jc_linear_device(int device, jc_precision precision, const float* a, l
                            long long ldw, const float* bias, float* c, long long ldc, int m, int n, int k, int flags,
                            void* stream);
 
+/*
+ * The GEMM on DEVICE operands already in the precision's storage format, with no conversion and
+ * no scratch memory (the form the engine's own layers use):
+ *   JC_BF16  a_hi [m, k] and w_hi [n, k] bfloat16; a_lo and w_lo unused (NULL)
+ *   JC_TF32  a_hi, w_hi FP32 holding TF32 values; a_lo, w_lo unused
+ *   JC_FP32  a_hi, w_hi TF32 parts and a_lo, w_lo FP32 remainders (x = hi + lo)
+ * lda and ldw are row pitches in elements (pitch × element size a multiple of 16 bytes, base
+ * addresses 16-byte aligned). bias, c and flags as jc_linear_device. Enqueued on `stream`.
+ * Replaces the reference's per-mode GEMM dispatch (timestral/tornado/TimestralForward.java:404-499).
+ */
+jc_status jc_gemm_device(int device, jc_precision precision, const void* a_hi, const void* a_lo, long long lda,
+                         const void* w_hi, const void* w_lo, long long ldw, const float* bias, float* c,
+                         long long ldc, int m, int n, int k, int flags, void* stream);
+
 /* Waits for all work on `device`, then returns and clears the device's kernel error word:
  * JC_ERR_TIMEOUT if a kernel's bounded wait gave up since the last call. */
 jc_status jc_device_sync(int device);
+
+/* ===================================================================================== */
+/* Engines: a model's weights resident on one or more GPUs, and its forward pass.          */
+/* ===================================================================================== */
+
+/* One checkpoint tensor from the caller (the reference maps model.safetensors with FFM,
+ * io/SafeTensors.java:49-70, and hands out MemorySegment views): FP32, row-major, contiguous. */
+typedef struct jc_tensor_view {
+  const char* name; /* checkpoint name, e.g. "transformer.layers.0.mlp.w3.weight" */
+  const float* data;
+  int ndim;
+  int64_t shape[4];
+} jc_tensor_view;
+
+typedef struct jc_engine jc_engine;
+
+/* Timestral layer kinds (block_schedule of timestral/TimestralConfig.java:173-182). */
+#define JC_LAYER_TIME 0
+#define JC_LAYER_VARIATE 1
+#define JC_LAYER_TIME_VARIATE 2
+#define JC_LAYER_VARIATE_TIME 3
+
+/* The TimestralConfig fields the forward pass uses (timestral/TimestralConfig.java:53-71). */
+typedef struct jc_timestral_desc {
+  int patch_size;
+  int d_model;
+  int num_heads;
+  int mlp_hidden_dim;
+  int num_layers;
+  const int32_t* layer_kinds; /* [num_layers] JC_LAYER_* */
+  int num_quantiles;
+  float rope_theta;
+  float rope_partial_factor;
+  float norm_eps;
+  int time_attn_gate;
+  int variate_attn_gate;
+} jc_timestral_desc;
+
+/*
+ * Creates a Timestral engine: binds `weights` by the checkpoint's names and shapes (every tensor
+ * exactly once, as timestral/TimestralWeights.java:83-115 does; an unknown, missing or misshapen
+ * tensor fails with JC_ERR_INVALID_ARG), rearranges and converts them to `precision` on each of
+ * the `n_devices` GPUs in `devices` (a full replica per GPU). The weights are copied; the
+ * caller's buffers may be released when the call returns. Head widths other than 32 or 64 fail
+ * with JC_ERR_UNSUPPORTED_SHAPE, as TimestralForward.java:163-166 rejects unsupported widths.
+ */
+jc_status jc_engine_create_timestral(const jc_timestral_desc* desc, const jc_tensor_view* weights, int n_weights,
+                                     const int* devices, int n_devices, jc_precision precision, jc_engine** out);
+
+/* One decode block's device-forward inputs: what TimestralForward.Plan.run uploads
+ * (timestral/tornado/TimestralForward.java:594-632), as BlockLayout and BlockPrep compute them. */
+typedef struct jc_timestral_block {
+  int rows;
+  int encoder;         /* encoder tokens per row (BlockLayout.encoderTokens) */
+  int horizon;         /* decoder tokens per row (BlockLayout.horizonPatches) */
+  int context_patches; /* BlockLayout.contextPatches */
+  int covariates;      /* BlockLayout.covariates */
+  const float* tokens;         /* [rows · encoder · 2P] BlockPrep.tokens */
+  const int32_t* positions;    /* [rows · (encoder + horizon)] BlockLayout.position */
+  const int32_t* key_valid;    /* [rows · encoder] BlockLayout.keyValid, 0/1 */
+  const int32_t* known;        /* [rows] BlockLayout.known, 0/1 */
+  const int32_t* role;         /* [rows] BlockLayout.role */
+  const int32_t* group_start;  /* [rows] first row of the row's series */
+  const int32_t* group_end;    /* [rows] one past its last row */
+} jc_timestral_block;
+
+/*
+ * The Timestral forward of one block on HOST buffers: raw_out [rows · horizon · P · Q] receives
+ * the quantile head's raw outputs (what TimestralForward.Plan.run downloads; the caller then runs
+ * BlockPrep.finish). Rows are sharded across the engine's GPUs in contiguous ranges that keep
+ * each series on one GPU; every GPU runs its shard as a CUDA graph and the results are gathered
+ * into raw_out. Rows of one series must be contiguous (JC_ERR_INVALID_ARG otherwise, as
+ * TimestralForward.java:616-619). Thread-safe; calls on one engine are serialised.
+ */
+jc_status jc_forward_timestral(jc_engine* engine, const jc_timestral_block* block, float* raw_out);
+
+/*
+ * The same forward on inputs already in HBM of the engine's GPU number `slot` (0-based index
+ * into the devices given at creation): every pointer of `block` and `raw_out` is a device
+ * pointer on that GPU. Enqueued on `stream` (cudaStream_t; NULL = the legacy default stream),
+ * returns without synchronising. Device-side errors surface on the next jc_engine_sync.
+ */
+jc_status jc_forward_timestral_device(jc_engine* engine, int slot, const jc_timestral_block* block, float* raw_out,
+                                      void* stream);
+
+/* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
+jc_status jc_engine_sync(jc_engine* engine);
+
+/*
+ * Engine options (the reference's -D properties, e.g. timestral.tornado.cudaGraph and
+ * timestral.tornado.plans in TimestralForward.java:146-160):
+ *   "cuda_graph"  1 (default) replay each shape as a captured CUDA graph, 0 run eagerly
+ *   "max_plans"   shape plans kept per GPU (default 8; least recently used evicted)
+ *   "profile"     1: run eagerly and time every kernel class with CUDA events (jc_engine_profile)
+ */
+jc_status jc_engine_set_option(jc_engine* engine, const char* key, long long value);
+
+/* Kernel-class timings collected while "profile" is 1, summed since the last read (then reset).
+ * names/ms/launches have room for `cap` entries; *count receives the number written. */
+jc_status jc_engine_profile(jc_engine* engine, int slot, const char** names, double* ms, long long* launches,
+                            double* flops, int cap, int* count);
+
+/* Frees the engine's device memory, graphs and streams. NULL is a no-op; returns JC_OK. */
+jc_status jc_engine_destroy(jc_engine* engine);
 
 #ifdef __cplusplus
 }

@@ -159,6 +159,48 @@ jc_status jc_linear(int device, jc_precision precision, const float* a, const fl
   return take_device_error(rt);
 }
 
+jc_status jc_gemm_device(int device, jc_precision precision, const void* a_hi, const void* a_lo, long long lda,
+                         const void* w_hi, const void* w_lo, long long ldw, const float* bias, float* c,
+                         long long ldc, int m, int n, int k, int flags, void* stream) {
+  clear_error();
+  if (!valid_precision(precision)) return fail(JC_ERR_INVALID_ARG, "unknown precision");
+  if (m < 1 || n < 1 || k < 1) return fail(JC_ERR_INVALID_ARG, "m, n and k must be positive");
+  if (!a_hi || !w_hi || !c) return fail(JC_ERR_INVALID_ARG, "null buffer");
+  if ((flags & JC_BIAS) && !bias) return fail(JC_ERR_INVALID_ARG, "JC_BIAS without a bias");
+  if (ldc < n) return fail(JC_ERR_INVALID_ARG, "ldc smaller than n");
+  int act = 0;
+  std::string why;
+  if (!act_of(flags, &act, &why)) return fail(JC_ERR_INVALID_ARG, why);
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  GemmArgs g{};
+  g.op = op_of(precision);
+  g.a_hi = a_hi;
+  g.a_lo = a_lo;
+  g.lda = lda;
+  g.w_hi = w_hi;
+  g.w_lo = w_lo;
+  g.ldw = ldw;
+  g.M = m;
+  g.N = n;
+  g.K = k;
+  g.ep = epi_default();
+  g.ep.act = act;
+  g.ep.bias_on = (flags & JC_BIAS) != 0;
+  g.ep.bias = bias;
+  g.ep.accumulate = (flags & JC_ACCUMULATE) != 0;
+  g.ep.c = c;
+  g.ep.ldc = ldc;
+  g.ep.cin = c;
+  g.ep.ldcin = ldc;
+  if (const char* msg = check_gemm(g)) return fail(JC_ERR_UNSUPPORTED_SHAPE, msg);
+  cudaError_t e = launch_gemm(g, static_cast<cudaStream_t>(stream), rt->err);
+  if (e != cudaSuccess) return fail_cuda(e, "GEMM launch");
+  return JC_OK;
+}
+
 jc_status jc_device_sync(int device) {
   clear_error();
   std::string why;

@@ -1,0 +1,34 @@
+// Attention companion kernels (time and variate attention with the block-layout masks).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "gemm.h"
+
+namespace jc {
+
+struct AttnArgs {
+  const void* qkv;  // [rows·n, ld_qkv]: q | k | v, heads-major (head h at columns h·dh within each part)
+  int qkv_bf16;     // qkv element type: bf16 (1) or fp32 (0)
+  long long ld_qkv;
+  const void* gate;  // [rows·n, ld_gate] sigmoid gate multiplied into the output, or null
+  int gate_bf16;
+  long long ld_gate;
+  void* out_hi;  // [rows·n, ld_out] in OutKind out_kind
+  void* out_lo;
+  long long ld_out;
+  int out_kind;
+  int rows, n, enc, ll, heads, head_dim, d;
+  float scale;  // applied to q·k
+  const int* key_valid;  // [rows·enc]
+  const int* known;      // [rows]
+  const int* role;       // [rows]
+  const int* group_start;
+  const int* group_end;
+  int covariates;
+};
+
+cudaError_t launch_time_attention(const AttnArgs& a, cudaStream_t s);
+cudaError_t launch_variate_attention(const AttnArgs& a, cudaStream_t s);
+
+}  // namespace jc

@@ -516,6 +516,17 @@ EpiParams epi_default() {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Tile widths (bit 0: 64, bit 1: 128, bit 2: 256) that keep heads and the gate split whole.
+static int qkv_tile_choices(const EpiParams& e) {
+  int bits = 0, i = 0;
+  for (int bn : {64, 128, 256}) {
+    const bool heads_ok = e.rope_cols == 0 || bn % e.head_dim == 0;
+    if (heads_ok && e.n_split % bn == 0) bits |= 1 << i;
+    ++i;
+  }
+  return bits;
+}
+
 const char* check_gemm(const GemmArgs& g) {
   if (g.M < 1 || g.N < 1 || g.K < 1) return "M, N and K must be positive";
   if (g.op < kOpBF16 || g.op > kOpSplit) return "unknown operand kind";
@@ -529,9 +540,12 @@ const char* check_gemm(const GemmArgs& g) {
   const EpiParams& e = g.ep;
   if (e.mode == kEpiSwiGLU && (g.N % 64 != 0)) return "SwiGLU GEMM needs N % 64 == 0";
   if (e.mode == kEpiQKV) {
-    if (e.head_dim % 64 != 0) return "fused RoPE needs head_dim % 64 == 0";
-    if (e.n_split % 256 != 0 || e.rope_cols % e.head_dim != 0) return "fused q|k|v|gate layout";
-    if (!e.pos || !e.rope_table) return "fused RoPE needs positions and a table";
+    if (e.rope_cols > 0 && (e.head_dim % 64 != 0 || e.rope_cols % e.head_dim != 0))
+      return "fused RoPE needs head_dim % 64 == 0 and whole heads";
+    if (e.rope_cols > 0 && (!e.pos || !e.rope_table)) return "fused RoPE needs positions and a table";
+    if (e.n_split % 64 != 0) return "the gate columns must start on a 64-column boundary";
+    if (g.N > e.n_split && !e.g_out) return "gate columns without a gate output";
+    if (qkv_tile_choices(e) == 0) return "no tile width fits the q|k|v|gate layout";
   }
   if (e.accumulate && !e.cin) return "accumulate without C input";
   if (e.bias_on && !e.bias) return "bias flag without bias";
@@ -582,16 +596,19 @@ static int sm_count() {
 static int choose_bn(const GemmArgs& g, int num_sms) {
   if (g.bn) return g.bn;
   const int m_blks = (g.M + 127) / 128;
-  int need = 64;
-  if (g.ep.mode == kEpiQKV) need = 256;  // the gate split sits on a 256-column boundary
-  for (int bn : {256, 128}) {
-    if (bn < need) break;
-    const long long tiles = (long long)m_blks * ((g.N + bn - 1) / bn);
-    if (tiles >= num_sms) return bn;
-  }
-  if (g.N <= 64 && need <= 64) return 64;
-  if (need > 128) return 256;
-  return g.N <= 128 || (long long)m_blks * ((g.N + 127) / 128) >= num_sms / 2 ? 128 : 64;
+  const int allowed = g.ep.mode == kEpiQKV ? qkv_tile_choices(g.ep) : 7;
+  const int widths[3] = {64, 128, 256};
+  // the widest allowed tile that still gives every SM a tile
+  for (int i = 2; i >= 0; --i)
+    if ((allowed >> i) & 1) {
+      const long long tiles = (long long)m_blks * ((g.N + widths[i] - 1) / widths[i]);
+      if (tiles >= num_sms) return widths[i];
+    }
+  // too few tiles for the grid: the narrowest allowed tile, unless N fits one 128-wide tile
+  if (g.N <= 128 && g.N > 64 && (allowed & 2)) return 128;
+  for (int i = 0; i < 3; ++i)
+    if ((allowed >> i) & 1) return widths[i];
+  return 256;
 }
 
 // Whether every epilogue pointer and pitch allows 16-byte vector access.

@@ -68,6 +68,11 @@ __global__ void fill_rows_kernel(float* x, long long ldx, const float* __restric
   }
 }
 
+__global__ void add_i32_kernel(const int* __restrict__ in, int* __restrict__ out, long long n, int add) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    out[i] = in[i] + add;
+}
+
 int grid_for(long long work, int threads) {
   long long b = (work + threads - 1) / threads;
   const long long cap = 148LL * 16;
@@ -96,6 +101,11 @@ void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int row
   const long long total = (long long)rows * (n - enc) * cols;
   if (total <= 0) return;
   fill_rows_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, ldx, q, cols, rows, enc, n);
+}
+
+void launch_add_i32(const int* in, int* out, long long n, int add, cudaStream_t s) {
+  if (n <= 0) return;
+  add_i32_kernel<<<grid_for(n, 256), 256, 0, s>>>(in, out, n, add);
 }
 
 }  // namespace jc

@@ -1,0 +1,681 @@
+// The Timestral forward on B200: weights bound by checkpoint name, rearranged and converted once
+// per GPU; one plan (activation buffers + CUDA graph) per block shape; every linear layer a
+// tcgen05 GEMM with its elementwise work fused into the epilogue:
+//
+//   patch embedding   hidden (bias, SiLU) → output (bias, written into the token rows of x)
+//                     → residual (bias, += x)
+//   per attention     RMSNorm → q|k|v|gate GEMM (RoPE on q and k, sigmoid on the gate)
+//                     → attention (gate multiplied in) → output GEMM (+= x)
+//   per MLP           RMSNorm → w12 GEMM (SwiGLU pairs) → w3 GEMM (+= x)
+//   head              RMSNorm of the decoder tokens → hidden (SiLU) → output → residual (+=)
+//
+// This replaces TimestralForward's task graph (timestral/tornado/TimestralForward.java:298-394),
+// its cuBLAS dispatch with separate bias/activation passes (:404-499) and the companion kernels of
+// TimestralKernels; the arithmetic is CpuTimestral.predictBlock's (timestral/cpu/CpuTimestral.java:
+// 127-188) between BlockPrep.of and BlockPrep.finish.
+#include <cmath>
+#include <cstring>
+#include <thread>
+
+#include "attention.cuh"
+#include "engine.h"
+#include "kernels.cuh"
+#include "runtime.h"
+
+namespace jc {
+namespace {
+
+struct TsAttn {
+  bool time = true, gated = true;
+  float* norm = nullptr;
+  DevLinear qkvg;  // [3d (+ d gate), d]: q|k|v heads-major, then the gate rows
+  DevLinear wo;
+};
+
+struct TsLayer {
+  std::vector<TsAttn> attns;
+  float* mlp_norm = nullptr;
+  DevLinear w12;  // [2F, d], SiLU and linear halves interleaved in 32-row groups
+  DevLinear w3;
+};
+
+struct TsWeights {
+  DevLinear emb_h, emb_o, emb_r;
+  float* forecast_query = nullptr;
+  std::vector<TsLayer> layers;
+  float* out_norm = nullptr;
+  DevLinear head_h, head_o, head_r;
+};
+
+struct TsPlan {
+  int rows = 0, enc = 0, h = 0, ll = 0, cov = 0;
+  DeviceMem mem;
+  float* tok_f32 = nullptr;
+  OpBuf tok, emb_h, hn, att, act, dec, head_h;
+  float* x = nullptr;
+  void* qkv = nullptr;
+  void* gate = nullptr;
+  float* raw = nullptr;
+  int *pos = nullptr, *key_valid = nullptr, *known = nullptr, *role = nullptr, *gs = nullptr, *ge = nullptr;
+  float* table = nullptr;
+  GraphRunner graph;
+  std::vector<int> h_pos, h_gs, h_ge;  // host staging of the transformed integer inputs
+};
+
+struct TsDevice : DeviceSlot {
+  TsWeights w;
+  std::list<std::unique_ptr<TsPlan>> plans;  // most recently used first
+  Profiler prof;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;  // chain a caller's stream to the engine stream
+  ~TsDevice() {
+    if (ev_in) cudaEventDestroy(ev_in);
+    if (ev_out) cudaEventDestroy(ev_out);
+  }
+};
+
+struct TimestralEngine : jc_engine {
+  int P = 0, d = 0, heads = 0, dh = 0, F = 0, Q = 0, rope_dim = 0;
+  float theta = 0, partial = 0, eps = 0;
+  int op = kOpBF16;
+  std::vector<int> kinds;
+  std::vector<float> inv_freq;
+  std::vector<std::unique_ptr<TsDevice>> devs;
+
+  int slots() const override { return static_cast<int>(devs.size()); }
+  DeviceSlot* slot(int i) override { return devs[i].get(); }
+  Profiler* profiler(int i) override { return &devs[i]->prof; }
+  void drop_plans() override {
+    for (auto& dv : devs) {
+      cudaSetDevice(dv->device);
+      cudaStreamSynchronize(dv->stream);
+      dv->plans.clear();
+    }
+  }
+
+  int qkv_out_kind() const { return op == kOpBF16 ? kOutBF16 : kOutF32; }
+  size_t qkv_esize() const { return op == kOpBF16 ? 2 : 4; }
+};
+
+// ---- weight binding and packing ---------------------------------------------------------------
+
+// TimestralWeights.qkv: row (s·heads + h)·dh + e of the result is stored row s·D + e·heads + h.
+std::vector<float> qkv_heads_major(const float* src, int d, int heads, int dh) {
+  std::vector<float> dst(static_cast<size_t>(3) * d * d);
+  for (int s = 0; s < 3; ++s)
+    for (int h = 0; h < heads; ++h)
+      for (int e = 0; e < dh; ++e)
+        std::memcpy(&dst[(static_cast<size_t>(s) * d + h * dh + e) * d],
+                    src + (static_cast<size_t>(s) * d + e * heads + h) * d, sizeof(float) * d);
+  return dst;
+}
+
+// w12 [2F, d] stored gate half first (TimestralWeights.mlpUp swaps the halves so SiLU applies to
+// stored rows F..2F). Packed for the SwiGLU epilogue: rows 64u..64u+31 are SiLU rows F+32u.., rows
+// 64u+32.. are linear rows 32u..
+std::vector<float> swiglu_interleave(const float* src, int F, int d) {
+  std::vector<float> dst(static_cast<size_t>(2) * F * d);
+  for (int u = 0; u < F / 32; ++u)
+    for (int i = 0; i < 32; ++i) {
+      std::memcpy(&dst[(static_cast<size_t>(64) * u + i) * d], src + (static_cast<size_t>(F) + 32 * u + i) * d,
+                  sizeof(float) * d);
+      std::memcpy(&dst[(static_cast<size_t>(64) * u + 32 + i) * d], src + (static_cast<size_t>(32) * u + i) * d,
+                  sizeof(float) * d);
+    }
+  return dst;
+}
+
+struct HostTs {
+  const float *emb_hw, *emb_hb, *emb_ow, *emb_ob, *emb_rw, *emb_rb, *fq, *out_norm, *head_hw, *head_ow, *head_rw;
+  struct A {
+    bool time, gated;
+    const float *norm, *wqkv, *gate, *wo;
+  };
+  struct L {
+    std::vector<A> attns;
+    const float *mlp_norm, *w12, *w3;
+  };
+  std::vector<L> layers;
+};
+
+bool bind_weights(const TimestralEngine& e, const jc_timestral_desc& desc, Binder& b, HostTs* hw) {
+  const int d = e.d, p = e.P, F = e.F, Q = e.Q;
+  const std::string pe = "representation.patch_proj.";
+  hw->emb_hw = b.take(pe + "hidden_layer.weight", {4LL * d, 2LL * p});
+  hw->emb_hb = b.take(pe + "hidden_layer.bias", {4LL * d});
+  hw->emb_ow = b.take(pe + "output_layer.weight", {d, 4LL * d});
+  hw->emb_ob = b.take(pe + "output_layer.bias", {d});
+  hw->emb_rw = b.take(pe + "residual_layer.weight", {d, 2LL * p});
+  hw->emb_rb = b.take(pe + "residual_layer.bias", {d});
+  hw->fq = b.take("representation.forecast_query", {d});
+  for (int i = 0; i < desc.num_layers; ++i) {
+    const std::string s = "transformer.layers." + std::to_string(i);
+    HostTs::L L;
+    const int kind = desc.layer_kinds[i];
+    std::vector<bool> axes;
+    if (kind == JC_LAYER_TIME) axes = {true};
+    if (kind == JC_LAYER_VARIATE) axes = {false};
+    if (kind == JC_LAYER_TIME_VARIATE) axes = {true, false};
+    if (kind == JC_LAYER_VARIATE_TIME) axes = {false, true};
+    for (size_t a = 0; a < axes.size(); ++a) {
+      HostTs::A A;
+      A.time = axes[a];
+      A.gated = axes[a] ? desc.time_attn_gate : desc.variate_attn_gate;
+      const std::string pa = s + ".attns." + std::to_string(a);
+      A.norm = b.take(s + ".attn_norms." + std::to_string(a) + ".scale", {d});
+      A.wqkv = b.take(pa + ".wQKV.weight", {3LL * d, d});
+      A.gate = A.gated ? b.take(pa + "._gate.weight", {d, d}) : nullptr;
+      A.wo = b.take(pa + ".wO.weight", {d, d});
+      L.attns.push_back(A);
+    }
+    L.mlp_norm = b.take(s + ".mlp_norm.scale", {d});
+    L.w12 = b.take(s + ".mlp.w12.weight", {2LL * F, d});
+    L.w3 = b.take(s + ".mlp.w3.weight", {d, F});
+    hw->layers.push_back(L);
+  }
+  hw->out_norm = b.take("transformer.out_norm.scale", {d});
+  const std::string hp = "head.projection.";
+  hw->head_hw = b.take(hp + "hidden_layer.weight", {4LL * d, d});
+  hw->head_ow = b.take(hp + "output_layer.weight", {static_cast<long long>(p) * Q, 4LL * d});
+  hw->head_rw = b.take(hp + "residual_layer.weight", {static_cast<long long>(p) * Q, d});
+  return b.require_all_bound();
+}
+
+bool upload_weights(TimestralEngine& e, const HostTs& hw, TsDevice& dv, std::string* err) {
+  const int d = e.d, p = e.P, F = e.F, Q = e.Q, op = e.op;
+  DeviceMem& m = dv.weights;
+  TsWeights& w = dv.w;
+  if (!upload_linear(m, op, hw.emb_hw, hw.emb_hb, 2 * p, 4 * d, &w.emb_h, err) ||
+      !upload_linear(m, op, hw.emb_ow, hw.emb_ob, 4 * d, d, &w.emb_o, err) ||
+      !upload_linear(m, op, hw.emb_rw, hw.emb_rb, 2 * p, d, &w.emb_r, err))
+    return false;
+  if (!(w.forecast_query = upload_f32(m, hw.fq, d, err))) return false;
+  for (const auto& L : hw.layers) {
+    TsLayer tl;
+    for (const auto& A : L.attns) {
+      TsAttn ta;
+      ta.time = A.time;
+      ta.gated = A.gated;
+      if (!(ta.norm = upload_f32(m, A.norm, d, err))) return false;
+      std::vector<float> q = qkv_heads_major(A.wqkv, d, e.heads, e.dh);
+      if (A.gated) q.insert(q.end(), A.gate, A.gate + static_cast<size_t>(d) * d);
+      if (!upload_linear(m, op, q.data(), nullptr, d, A.gated ? 4 * d : 3 * d, &ta.qkvg, err) ||
+          !upload_linear(m, op, A.wo, nullptr, d, d, &ta.wo, err))
+        return false;
+      tl.attns.push_back(std::move(ta));
+    }
+    if (!(tl.mlp_norm = upload_f32(m, L.mlp_norm, d, err))) return false;
+    std::vector<float> up = swiglu_interleave(L.w12, F, d);
+    if (!upload_linear(m, op, up.data(), nullptr, d, 2 * F, &tl.w12, err) ||
+        !upload_linear(m, op, L.w3, nullptr, F, d, &tl.w3, err))
+      return false;
+    w.layers.push_back(std::move(tl));
+  }
+  if (!(w.out_norm = upload_f32(m, hw.out_norm, d, err))) return false;
+  return upload_linear(m, op, hw.head_hw, nullptr, d, 4 * d, &w.head_h, err) &&
+         upload_linear(m, op, hw.head_ow, nullptr, 4 * d, p * Q, &w.head_o, err) &&
+         upload_linear(m, op, hw.head_rw, nullptr, d, p * Q, &w.head_r, err);
+}
+
+// ---- plans --------------------------------------------------------------------------------------
+
+std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, int h, int ll, int cov) {
+  auto p = std::make_unique<TsPlan>();
+  p->rows = rows;
+  p->enc = enc;
+  p->h = h;
+  p->ll = ll;
+  p->cov = cov;
+  const int n = enc + h, d = e.d, op = e.op;
+  const long long T = static_cast<long long>(rows) * n, encT = static_cast<long long>(rows) * enc,
+                  decT = static_cast<long long>(rows) * h;
+  DeviceMem& m = p->mem;
+  bool ok = (p->tok_f32 = static_cast<float*>(m.alloc(sizeof(float) * encT * 2 * e.P))) &&
+            alloc_op(m, op, encT, 2 * e.P, &p->tok) && alloc_op(m, op, encT, 4 * d, &p->emb_h) &&
+            (p->x = static_cast<float*>(m.alloc(sizeof(float) * T * d))) && alloc_op(m, op, T, d, &p->hn) &&
+            (p->qkv = m.alloc(e.qkv_esize() * T * 3 * d)) && (p->gate = m.alloc(e.qkv_esize() * T * d)) &&
+            alloc_op(m, op, T, d, &p->att) && alloc_op(m, op, T, e.F, &p->act) && alloc_op(m, op, decT, d, &p->dec) &&
+            alloc_op(m, op, decT, 4 * d, &p->head_h) &&
+            (p->raw = static_cast<float*>(m.alloc(sizeof(float) * decT * e.P * e.Q))) &&
+            (p->pos = static_cast<int*>(m.alloc(sizeof(int) * T))) &&
+            (p->key_valid = static_cast<int*>(m.alloc(sizeof(int) * encT))) &&
+            (p->known = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
+            (p->role = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
+            (p->gs = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
+            (p->ge = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
+            (p->table = static_cast<float*>(m.alloc(sizeof(float) * (2 * enc + h) * e.dh)));
+  if (!ok) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  // RoPE table over every position a token can have, (−enc, enc + h), row p ↔ position p − enc,
+  // as TimestralForward.Plan.run builds it (TimestralForward.java:600-608)
+  const int half = e.dh / 2;
+  std::vector<float> table(static_cast<size_t>(2 * enc + h) * e.dh, 0.0f);
+  for (int q = 0; q < 2 * enc + h; ++q) {
+    const float position = static_cast<float>(q - enc);
+    for (int k = 0; k < half; ++k) {
+      const float a = position * e.inv_freq[k];
+      table[static_cast<size_t>(q) * e.dh + k] = static_cast<float>(std::cos(static_cast<double>(a)));
+      table[static_cast<size_t>(q) * e.dh + half + k] = static_cast<float>(std::sin(static_cast<double>(a)));
+    }
+  }
+  if (cudaMemcpy(p->table, table.data(), sizeof(float) * table.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+    return nullptr;
+  p->h_pos.resize(T);
+  p->h_gs.resize(rows);
+  p->h_ge.resize(rows);
+  return p;
+}
+
+TsPlan* get_plan(TimestralEngine& e, TsDevice& dv, int rows, int enc, int h, int ll, int cov, std::string* err) {
+  for (auto it = dv.plans.begin(); it != dv.plans.end(); ++it) {
+    TsPlan* p = it->get();
+    if (p->rows == rows && p->enc == enc && p->h == h && p->ll == ll && p->cov == cov) {
+      dv.plans.splice(dv.plans.begin(), dv.plans, it);
+      return p;
+    }
+  }
+  while (static_cast<int>(dv.plans.size()) >= std::max(1, e.max_plans)) dv.plans.pop_back();
+  auto p = make_plan(e, rows, enc, h, ll, cov);
+  if (!p && !dv.plans.empty()) {
+    // out of memory: drop the cached plans and retry once (PlanCache.run, PlanCache.java:70-100)
+    cudaStreamSynchronize(dv.stream);
+    dv.plans.clear();
+    p = make_plan(e, rows, enc, h, ll, cov);
+  }
+  if (!p) {
+    *err = "out of device memory for a plan of " + std::to_string(rows) + " rows";
+    return nullptr;
+  }
+  dv.plans.push_front(std::move(p));
+  return dv.plans.front().get();
+}
+
+// ---- the forward ----------------------------------------------------------------------------------
+
+cudaError_t gemm(TsDevice& dv, GemmArgs& g, cudaStream_t s) {
+  dv.prof.begin(s, "gemm", 2.0 * g.M * g.N * g.K);  // algorithmic FLOPs (the split mode runs 3 MMAs each)
+  cudaError_t r = launch_gemm(g, s, dv.err);
+  dv.prof.end(s);
+  return r;
+}
+
+void set_op_out(EpiParams& ep, int op, const OpBuf& o) {
+  ep.o_kind = out_of_op(op);
+  ep.o_hi = o.hi;
+  ep.o_lo = o.lo;
+  ep.ldo = o.ld;
+}
+
+cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, cudaStream_t s) {
+  const int R = p.rows, E = p.enc, H = p.h, n = E + H, d = e.d, op = e.op, P2 = 2 * e.P;
+  const long long T = static_cast<long long>(R) * n, encT = static_cast<long long>(R) * E,
+                  decT = static_cast<long long>(R) * H;
+  const TsWeights& w = dv.w;
+  Profiler& prof = dv.prof;
+  cudaError_t r;
+#define JC_TRY(x)                   \
+  do {                              \
+    if ((r = (x)) != cudaSuccess) { \
+      return r;                     \
+    }                               \
+  } while (0)
+
+  prof.begin(s, "convert", 0);
+  launch_convert(op, p.tok_f32, P2, p.tok.hi, p.tok.lo, p.tok.ld, encT, P2, s);
+  prof.end(s);
+  // patch embedding: output(SiLU(hidden(tok))) + residual(tok), into the encoder rows of x
+  GemmArgs g = gemm_args(op, p.tok, encT, w.emb_h);
+  g.ep.act = kActSilu;
+  set_op_out(g.ep, op, p.emb_h);
+  JC_TRY(gemm(dv, g, s));
+  g = gemm_args(op, p.emb_h, encT, w.emb_o);
+  g.ep.c = p.x;
+  g.ep.ldc = d;
+  g.ep.rg = E;
+  g.ep.rg_stride = n;
+  JC_TRY(gemm(dv, g, s));
+  g = gemm_args(op, p.tok, encT, w.emb_r);
+  g.ep.c = p.x;
+  g.ep.ldc = d;
+  g.ep.cin = p.x;
+  g.ep.ldcin = d;
+  g.ep.accumulate = 1;
+  g.ep.rg = E;
+  g.ep.rg_stride = n;
+  JC_TRY(gemm(dv, g, s));
+  prof.begin(s, "fill", 0);
+  launch_fill_rows(p.x, d, w.forecast_query, d, R, E, n, s);
+  prof.end(s);
+
+  const int out_kind = out_of_op(op);
+  for (const TsLayer& L : w.layers) {
+    for (const TsAttn& A : L.attns) {
+      prof.begin(s, "rmsnorm", 0);
+      launch_rmsnorm(p.x, d, A.norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
+      prof.end(s);
+      g = gemm_args(op, p.hn, T, A.qkvg);
+      g.ep.mode = kEpiQKV;
+      g.ep.o_kind = e.qkv_out_kind();
+      g.ep.o_hi = p.qkv;
+      g.ep.ldo = 3LL * d;
+      g.ep.rope_cols = A.time ? 2 * d : 0;
+      g.ep.head_dim = e.dh;
+      g.ep.pos = p.pos;
+      g.ep.rope_table = p.table;
+      g.ep.n_split = 3 * d;
+      g.ep.g_out = p.gate;
+      g.ep.ldg = d;
+      g.ep.g_bf16 = op == kOpBF16;
+      JC_TRY(gemm(dv, g, s));
+      AttnArgs a{};
+      a.qkv = p.qkv;
+      a.qkv_bf16 = op == kOpBF16;
+      a.ld_qkv = 3LL * d;
+      a.gate = A.gated ? p.gate : nullptr;
+      a.gate_bf16 = op == kOpBF16;
+      a.ld_gate = d;
+      a.out_hi = p.att.hi;
+      a.out_lo = p.att.lo;
+      a.ld_out = p.att.ld;
+      a.out_kind = out_kind;
+      a.rows = R;
+      a.n = n;
+      a.enc = E;
+      a.ll = p.ll;
+      a.heads = e.heads;
+      a.head_dim = e.dh;
+      a.d = d;
+      a.scale = 1.0f / std::sqrt(static_cast<float>(e.dh));
+      a.key_valid = p.key_valid;
+      a.known = p.known;
+      a.role = p.role;
+      a.group_start = p.gs;
+      a.group_end = p.ge;
+      a.covariates = p.cov;
+      prof.begin(s, "attention", 4.0 * T * n * d);
+      JC_TRY(A.time ? launch_time_attention(a, s) : launch_variate_attention(a, s));
+      prof.end(s);
+      g = gemm_args(op, p.att, T, A.wo);
+      g.ep.c = p.x;
+      g.ep.ldc = d;
+      g.ep.cin = p.x;
+      g.ep.ldcin = d;
+      g.ep.accumulate = 1;
+      JC_TRY(gemm(dv, g, s));
+    }
+    prof.begin(s, "rmsnorm", 0);
+    launch_rmsnorm(p.x, d, L.mlp_norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
+    prof.end(s);
+    g = gemm_args(op, p.hn, T, L.w12);
+    g.ep.mode = kEpiSwiGLU;
+    set_op_out(g.ep, op, p.act);
+    JC_TRY(gemm(dv, g, s));
+    g = gemm_args(op, p.act, T, L.w3);
+    g.ep.c = p.x;
+    g.ep.ldc = d;
+    g.ep.cin = p.x;
+    g.ep.ldcin = d;
+    g.ep.accumulate = 1;
+    JC_TRY(gemm(dv, g, s));
+  }
+  // out_norm on the decoder tokens only (the head reads nothing else), gathered per row
+  prof.begin(s, "rmsnorm", 0);
+  launch_rmsnorm(p.x, d, w.out_norm, d, e.eps, out_kind, p.dec.hi, p.dec.lo, p.dec.ld, decT, H, n, E, s);
+  prof.end(s);
+  g = gemm_args(op, p.dec, decT, w.head_h);
+  g.ep.act = kActSilu;
+  set_op_out(g.ep, op, p.head_h);
+  JC_TRY(gemm(dv, g, s));
+  const int pq = e.P * e.Q;
+  g = gemm_args(op, p.head_h, decT, w.head_o);
+  g.ep.c = p.raw;
+  g.ep.ldc = pq;
+  JC_TRY(gemm(dv, g, s));
+  g = gemm_args(op, p.dec, decT, w.head_r);
+  g.ep.c = p.raw;
+  g.ep.ldc = pq;
+  g.ep.cin = p.raw;
+  g.ep.ldcin = pq;
+  g.ep.accumulate = 1;
+  JC_TRY(gemm(dv, g, s));
+#undef JC_TRY
+  return cudaGetLastError();
+}
+
+// Validates one block's host or device-independent fields.
+jc_status check_block(const TimestralEngine& e, const jc_timestral_block* b, bool host) {
+  if (!b) return fail(JC_ERR_INVALID_ARG, "null block");
+  if (b->rows < 1) return fail(JC_ERR_INVALID_ARG, "rows must be >= 1");
+  if (b->encoder < 1) return fail(JC_ERR_INVALID_ARG, "encoder tokens must be >= 1");
+  if (b->horizon < 1) return fail(JC_ERR_INVALID_ARG, "horizon patches must be >= 1, got " + std::to_string(b->horizon));
+  if (b->context_patches < 1 || b->context_patches > b->encoder)
+    return fail(JC_ERR_INVALID_ARG, "context patches must be in [1, encoder]");
+  if (!b->tokens || !b->positions || !b->key_valid || !b->known || !b->role || !b->group_start || !b->group_end)
+    return fail(JC_ERR_INVALID_ARG, "null block field");
+  if (host) {
+    for (int i = 0; i < b->rows; ++i) {
+      const int s = b->group_start[i], t = b->group_end[i];
+      if (s < 0 || s > i || t <= i || t > b->rows || b->group_start[s] != s || b->group_end[s] != t)
+        return fail(JC_ERR_INVALID_ARG, "rows of a series are not contiguous (row " + std::to_string(i) + ")");
+    }
+  }
+  (void)e;
+  return JC_OK;
+}
+
+// Copies rows [r0, r1) of a block into the plan's device inputs. Positions become RoPE table
+// rows (position + encoder) and series ranges become shard-relative. `kind` is HostToDevice for
+// host blocks and DeviceToDevice for device blocks (then the integer transforms run on the GPU).
+cudaError_t upload_shard(const jc_timestral_block* b, int r0, int r1, TsPlan& p, int two_p, cudaStream_t s,
+                         bool host) {
+  const int rows = r1 - r0, E = b->encoder, n = E + b->horizon;
+  const long long T = static_cast<long long>(rows) * n;
+  const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+  cudaError_t e = cudaMemcpyAsync(p.tok_f32, b->tokens + static_cast<long long>(r0) * E * two_p,
+                                  sizeof(float) * rows * E * two_p, kind, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(p.key_valid, b->key_valid + static_cast<long long>(r0) * E, sizeof(int) * rows * E, kind, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(p.known, b->known + r0, sizeof(int) * rows, kind, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(p.role, b->role + r0, sizeof(int) * rows, kind, s);
+  if (e != cudaSuccess) return e;
+  if (host) {
+    for (long long i = 0; i < T; ++i) p.h_pos[i] = b->positions[static_cast<long long>(r0) * n + i] + E;
+    for (int i = 0; i < rows; ++i) {
+      p.h_gs[i] = b->group_start[r0 + i] - r0;
+      p.h_ge[i] = b->group_end[r0 + i] - r0;
+    }
+    e = cudaMemcpyAsync(p.pos, p.h_pos.data(), sizeof(int) * T, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(p.gs, p.h_gs.data(), sizeof(int) * rows, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(p.ge, p.h_ge.data(), sizeof(int) * rows, cudaMemcpyHostToDevice, s);
+    return e;
+  }
+  launch_add_i32(b->positions + static_cast<long long>(r0) * n, p.pos, T, E, s);
+  launch_add_i32(b->group_start + r0, p.gs, rows, -r0, s);
+  launch_add_i32(b->group_end + r0, p.ge, rows, -r0, s);
+  return cudaGetLastError();
+}
+
+// Runs rows [r0, r1) of `b` on one GPU; raw_out points at the block's first row's outputs.
+jc_status run_shard(TimestralEngine& e, TsDevice& dv, const jc_timestral_block* b, int r0, int r1, float* raw_out,
+                    bool host, cudaStream_t stream, std::string* err) {
+  if (cudaSetDevice(dv.device) != cudaSuccess) {
+    *err = "cannot select device " + std::to_string(dv.device);
+    return JC_ERR_CUDA;
+  }
+  // always run on the engine's own stream (graph capture needs a non-legacy stream); a device
+  // caller's stream is chained in and out with events
+  cudaStream_t s = dv.stream;
+  if (!host) {
+    if (cudaEventRecord(dv.ev_in, stream) != cudaSuccess || cudaStreamWaitEvent(s, dv.ev_in, 0) != cudaSuccess) {
+      *err = "cannot order the caller's stream before the forward";
+      return JC_ERR_CUDA;
+    }
+  }
+  TsPlan* p = get_plan(e, dv, r1 - r0, b->encoder, b->horizon, b->context_patches, b->covariates, err);
+  if (!p) return JC_ERR_OOM;
+  cudaError_t ce = upload_shard(b, r0, r1, *p, 2 * e.P, s, host);
+  if (ce != cudaSuccess) {
+    *err = std::string("upload: ") + cudaGetErrorString(ce);
+    return JC_ERR_CUDA;
+  }
+  dv.prof.on = e.profile;
+  TimestralEngine& ec = e;
+  TsDevice& dvc = dv;
+  ce = p->graph.run(s, [&](cudaStream_t st) { return enqueue_forward(ec, dvc, *p, st); }, e.use_graph && !e.profile);
+  if (ce != cudaSuccess) {
+    *err = std::string("forward: ") + cudaGetErrorString(ce);
+    return JC_ERR_CUDA;
+  }
+  const size_t nraw = static_cast<size_t>(r1 - r0) * b->horizon * e.P * e.Q;
+  ce = cudaMemcpyAsync(raw_out + static_cast<size_t>(r0) * b->horizon * e.P * e.Q, p->raw, sizeof(float) * nraw,
+                       host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s);
+  if (ce != cudaSuccess) {
+    *err = std::string("download: ") + cudaGetErrorString(ce);
+    return JC_ERR_CUDA;
+  }
+  if (!host) {
+    if (cudaEventRecord(dv.ev_out, s) != cudaSuccess || cudaStreamWaitEvent(stream, dv.ev_out, 0) != cudaSuccess) {
+      *err = "cannot order the caller's stream after the forward";
+      return JC_ERR_CUDA;
+    }
+    return JC_OK;
+  }
+  ce = cudaStreamSynchronize(s);
+  if (ce != cudaSuccess) {
+    *err = std::string("forward: ") + cudaGetErrorString(ce);
+    return JC_ERR_CUDA;
+  }
+  if (e.profile) dv.prof.collect();
+  uint32_t word = 0;
+  cudaMemcpy(&word, dv.err, sizeof word, cudaMemcpyDeviceToHost);
+  if (word) {
+    cudaMemset(dv.err, 0, sizeof word);
+    *err = "a device wait gave up (error bits " + std::to_string(word) + ")";
+    return JC_ERR_TIMEOUT;
+  }
+  return JC_OK;
+}
+
+}  // namespace
+}  // namespace jc
+
+using namespace jc;
+
+extern "C" {
+
+jc_status jc_engine_create_timestral(const jc_timestral_desc* desc, const jc_tensor_view* weights, int n_weights,
+                                     const int* devices, int n_devices, jc_precision precision, jc_engine** out) {
+  clear_error();
+  if (!out) return fail(JC_ERR_INVALID_ARG, "null engine out-pointer");
+  *out = nullptr;
+  if (!desc || !weights || n_weights < 1) return fail(JC_ERR_INVALID_ARG, "null description or weights");
+  if (precision != JC_FP32 && precision != JC_TF32 && precision != JC_BF16)
+    return fail(JC_ERR_INVALID_ARG, "unknown precision");
+  const jc_timestral_desc& c = *desc;
+  if (c.patch_size < 1 || c.d_model < 1 || c.num_heads < 1 || c.d_model % c.num_heads != 0)
+    return fail(JC_ERR_INVALID_ARG, "d_model " + std::to_string(c.d_model) + " is not divisible by num_heads " +
+                                        std::to_string(c.num_heads));
+  if (c.num_layers < 0 || (c.num_layers > 0 && !c.layer_kinds)) return fail(JC_ERR_INVALID_ARG, "layer kinds");
+  for (int i = 0; i < c.num_layers; ++i)
+    if (c.layer_kinds[i] < JC_LAYER_TIME || c.layer_kinds[i] > JC_LAYER_VARIATE_TIME)
+      return fail(JC_ERR_INVALID_ARG, "unknown layer kind " + std::to_string(c.layer_kinds[i]));
+  if (c.num_quantiles < 1 || c.mlp_hidden_dim < 1) return fail(JC_ERR_INVALID_ARG, "quantiles / mlp width");
+  auto e = std::make_unique<TimestralEngine>();
+  e->family = 1;
+  e->P = c.patch_size;
+  e->d = c.d_model;
+  e->heads = c.num_heads;
+  e->dh = c.d_model / c.num_heads;
+  e->F = c.mlp_hidden_dim;
+  e->Q = c.num_quantiles;
+  e->theta = c.rope_theta;
+  e->partial = c.rope_partial_factor;
+  e->eps = c.norm_eps;
+  e->rope_dim = static_cast<int>(e->dh * c.rope_partial_factor);
+  e->op = op_of_precision(precision);
+  if (e->rope_dim <= 0 || e->rope_dim % 2 != 0)
+    return fail(JC_ERR_INVALID_ARG, "rope_partial_factor gives rope_dim " + std::to_string(e->rope_dim));
+  if (e->dh != 64)
+    return fail(JC_ERR_UNSUPPORTED_SHAPE, "unsupported attention head width " + std::to_string(e->dh) +
+                                              " (this engine supports 64)");
+  if (e->F % 32 != 0) return fail(JC_ERR_UNSUPPORTED_SHAPE, "mlp_hidden_dim must be a multiple of 32");
+  // CpuTimestral.inverseFrequencies (timestral/cpu/CpuTimestral.java:108-116), in float
+  e->inv_freq.assign(e->dh / 2, 0.0f);
+  for (int i = 0; i < e->rope_dim / 2; ++i) {
+    const float ex = static_cast<float>(2 * i) / static_cast<float>(e->rope_dim);
+    e->inv_freq[i] = 1.0f / static_cast<float>(std::pow(static_cast<double>(c.rope_theta), static_cast<double>(ex)));
+  }
+  Binder binder(weights, n_weights);
+  HostTs hw;
+  if (!bind_weights(*e, c, binder, &hw)) return fail(JC_ERR_INVALID_ARG, binder.error());
+  std::vector<int> devs;
+  if (n_devices <= 0 || !devices) {
+    devs.push_back(0);
+  } else {
+    devs.assign(devices, devices + n_devices);
+  }
+  for (int dev : devs) {
+    std::string why;
+    if (!device_rt(dev, &why)) return fail(JC_ERR_NO_DEVICE, why);
+    auto dv = std::make_unique<TsDevice>();
+    dv->device = dev;
+    cudaSetDevice(dev);
+    if (cudaStreamCreateWithFlags(&dv->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&dv->err, sizeof(uint32_t)) != cudaSuccess || cudaMemset(dv->err, 0, sizeof(uint32_t)) != cudaSuccess ||
+        cudaEventCreateWithFlags(&dv->ev_in, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&dv->ev_out, cudaEventDisableTiming) != cudaSuccess)
+      return fail_cuda(cudaGetLastError(), "engine device setup");
+    std::string err;
+    if (!upload_weights(*e, hw, *dv, &err)) return fail(JC_ERR_OOM, err);
+    e->devs.push_back(std::move(dv));
+  }
+  *out = e.release();
+  return JC_OK;
+}
+
+jc_status jc_forward_timestral(jc_engine* engine, const jc_timestral_block* block, float* raw_out) {
+  clear_error();
+  if (!engine || engine->family != 1) return fail(JC_ERR_INVALID_ARG, "not a Timestral engine");
+  auto* e = static_cast<TimestralEngine*>(engine);
+  if (!raw_out) return fail(JC_ERR_INVALID_ARG, "null output");
+  jc_status st = check_block(*e, block, true);
+  if (st != JC_OK) return st;
+  std::lock_guard<std::mutex> lk(e->mu);
+  const int parts = std::min<int>(static_cast<int>(e->devs.size()), block->rows);
+  std::vector<int> cuts = shard_rows(block->rows, block->group_start, block->group_end, parts);
+  std::vector<jc_status> status(parts, JC_OK);
+  std::vector<std::string> errs(parts);
+  auto work = [&](int i) {
+    if (cuts[i + 1] > cuts[i])
+      status[i] = run_shard(*e, *e->devs[i], block, cuts[i], cuts[i + 1], raw_out, true, nullptr, &errs[i]);
+  };
+  if (parts == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < parts; ++i) th.emplace_back(work, i);
+    for (auto& t : th) t.join();
+  }
+  for (int i = 0; i < parts; ++i)
+    if (status[i] != JC_OK)
+      return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+  return JC_OK;
+}
+
+jc_status jc_forward_timestral_device(jc_engine* engine, int slot, const jc_timestral_block* block, float* raw_out,
+                                      void* stream) {
+  clear_error();
+  if (!engine || engine->family != 1) return fail(JC_ERR_INVALID_ARG, "not a Timestral engine");
+  auto* e = static_cast<TimestralEngine*>(engine);
+  if (slot < 0 || slot >= static_cast<int>(e->devs.size())) return fail(JC_ERR_INVALID_ARG, "slot out of range");
+  if (!raw_out) return fail(JC_ERR_INVALID_ARG, "null output");
+  jc_status st = check_block(*e, block, false);
+  if (st != JC_OK) return st;
+  std::lock_guard<std::mutex> lk(e->mu);
+  std::string err;
+  st = run_shard(*e, *e->devs[slot], block, 0, block->rows, raw_out, false, static_cast<cudaStream_t>(stream), &err);
+  return st == JC_OK ? JC_OK : fail(st, err);
+}
+
+}  // extern "C"
