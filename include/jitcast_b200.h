@@ -90,6 +90,28 @@ jc_status jc_linear_device(int device, jc_precision precision, const float* a, l
                            void* stream);
 
 /*
+ * jc_linear_device for callers that cannot allocate GPU memory once they are running: code that has
+ * handed the GPU to a fixed arena or memory budget (where a cudaMalloc could fail or stall between
+ * steps), or that must not call cudaMalloc / cudaFree because those can synchronise the device.
+ * This entry point has no counterpart in the reference.
+ *
+ * Same arguments and result as jc_linear_device, but the converted operands go into a fixed scratch
+ * array compiled into the library (16 MiB on every GPU that loads the library, held until the
+ * process exits) instead of memory allocated on demand, and nothing in the call allocates.
+ *   - (m + n) x round_up(k, 64) operands must fit: 2 bytes per element for JC_BF16, 4 for JC_TF32,
+ *     8 for JC_FP32 (hi and lo). Larger shapes fail with JC_ERR_UNSUPPORTED_SHAPE.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
+ *     that device current; make that first call before any stream capture.
+ *   - Every call shares the one array and it keeps the last call's contents; the operands are fully
+ *     rewritten by each call. Calls that overlapped on the GPU would race on it, so calls are
+ *     serialised and each one waits for its own kernels on `stream` before it returns.
+ *   - Returns JC_ERR_TIMEOUT if a bounded wait inside the GEMM gave up.
+ */
+jc_status jc_linear_device_noalloc(int device, jc_precision precision, const float* a, long long lda, const float* w,
+                                   long long ldw, const float* bias, float* c, long long ldc, int m, int n, int k,
+                                   int flags, void* stream);
+
+/*
  * The GEMM on DEVICE operands already in the precision's storage format, with no conversion and
  * no scratch memory (the form the engine's own layers use):
  *   JC_BF16  a_hi [m, k] and w_hi [n, k] bfloat16; a_lo and w_lo unused (NULL)

@@ -56,6 +56,8 @@ PROTOTYPES: dict[str, tuple] = {
     "jc_linear": (c_int, [c_int, c_int, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int]),
     "jc_linear_device": (c_int, [c_int, c_int, c_vp, c_ll, c_vp, c_ll, c_vp, c_vp, c_ll, c_int, c_int, c_int, c_int,
                                  c_vp]),
+    "jc_linear_device_noalloc": (c_int, [c_int, c_int, c_vp, c_ll, c_vp, c_ll, c_vp, c_vp, c_ll, c_int, c_int, c_int,
+                                         c_int, c_vp]),
     "jc_gemm_device": (c_int, [c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_int, c_int,
                                c_int, c_int, c_vp]),
     "jc_device_sync": (c_int, [c_int]),
