@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--series", type=int, default=65536, help="series per step, whole job")
     ap.add_argument("--chunk", type=int, default=8192, help="series per forward call")
-    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--precision", default="fp16", choices=["fp16", "bf16", "tf32", "fp32"])
     ap.add_argument("--cpu-series", type=int, default=2, help="series in the CPU baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
     return ap.parse_args()

@@ -42,8 +42,10 @@ typedef enum jc_status {
 /* Arithmetic of the tensor-core GEMMs (replaces tornado/GemmMode.java:40-41).
  *   JC_FP32  FP32 operands as TF32 hi/lo pairs, three TF32 MMAs per product (≈ FP32 accuracy)
  *   JC_TF32  TF32 operands, FP32 accumulation (the reference's CUBLAS_TF32)
- *   JC_BF16  BF16 operands, FP32 accumulation and FP32 residual stream (replaces CUBLAS_FP16) */
-typedef enum jc_precision { JC_FP32 = 0, JC_TF32 = 1, JC_BF16 = 2 } jc_precision;
+ *   JC_BF16  BF16 operands, FP32 accumulation and FP32 residual stream
+ *   JC_FP16  FP16 operands (stores saturate at ±65504, as Kernels.HALF_MAX), FP32 accumulation and
+ *            FP32 residual stream (the reference's CUBLAS_FP16 / gemmHalf, fused) */
+typedef enum jc_precision { JC_FP32 = 0, JC_TF32 = 1, JC_BF16 = 2, JC_FP16 = 3 } jc_precision;
 
 /* GEMM epilogue flags: the values of tornado/Kernels.java:50-56, plus GELU.
  * Order as Kernels.gemm (Kernels.java:86-100): bias, then SiLU and/or ReLU (or GELU), then += C. */
@@ -98,8 +100,8 @@ jc_status jc_linear_device(int device, jc_precision precision, const float* a, l
  * Same arguments and result as jc_linear_device, but the converted operands go into a fixed scratch
  * array compiled into the library (16 MiB on every GPU that loads the library, held until the
  * process exits) instead of memory allocated on demand, and nothing in the call allocates.
- *   - (m + n) x round_up(k, 64) operands must fit: 2 bytes per element for JC_BF16, 4 for JC_TF32,
- *     8 for JC_FP32 (hi and lo). Larger shapes fail with JC_ERR_UNSUPPORTED_SHAPE.
+ *   - (m + n) x round_up(k, 64) operands must fit: 2 bytes per element for JC_BF16 and JC_FP16, 4
+ *     for JC_TF32, 8 for JC_FP32 (hi and lo). Larger shapes fail with JC_ERR_UNSUPPORTED_SHAPE.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
  *     that device current; make that first call before any stream capture.
  *   - Every call shares the one array and it keeps the last call's contents; the operands are fully

@@ -17,8 +17,8 @@ OK, ERR_INVALID_ARG, ERR_UNSUPPORTED_SHAPE, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_
 STATUS_NAMES = ["OK", "INVALID_ARG", "UNSUPPORTED_SHAPE", "OOM", "CUDA", "TIMEOUT", "INTERNAL", "NO_DEVICE"]
 
 # jc_precision
-FP32, TF32, BF16 = 0, 1, 2
-PRECISIONS = {"fp32": FP32, "tf32": TF32, "bf16": BF16}
+FP32, TF32, BF16, FP16 = 0, 1, 2, 3
+PRECISIONS = {"fp32": FP32, "tf32": TF32, "bf16": BF16, "fp16": FP16}
 
 # GEMM flags (tornado/Kernels.java:50-56, plus GELU)
 BIAS, ACCUMULATE, SILU, TWIN_ONLY, RELU, GELU = 1, 2, 4, 8, 16, 32

@@ -14,7 +14,7 @@ namespace {
 
 enum Slot { kSlotA = 0, kSlotALo, kSlotW, kSlotWLo, kSlotAF32, kSlotWF32, kSlotBias, kSlotC };
 
-int op_of(jc_precision p) { return p == JC_BF16 ? kOpBF16 : p == JC_TF32 ? kOpTF32 : kOpSplit; }
+int op_of(jc_precision p) { return p == JC_BF16 ? kOpBF16 : p == JC_FP16 ? kOpF16 : p == JC_TF32 ? kOpTF32 : kOpSplit; }
 
 // Maps Kernels.gemm flags to an activation; false for flags this engine rejects.
 bool act_of(int flags, int* act, std::string* why) {
@@ -36,14 +36,14 @@ bool act_of(int flags, int* act, std::string* why) {
   return true;
 }
 
-bool valid_precision(int p) { return p == JC_FP32 || p == JC_TF32 || p == JC_BF16; }
+bool valid_precision(int p) { return p == JC_FP32 || p == JC_TF32 || p == JC_BF16 || p == JC_FP16; }
 
 // Converts fp32 A [rows, cols] (pitch ld) into the operand buffers of slot pair (hi, lo),
 // K padded to a multiple of 64 elements.
 bool stage_operand(DeviceRt* rt, int op, const float* src, long long ld, long long rows, int cols, int slot_hi,
                    int slot_lo, void** hi, void** lo, long long* ldp, cudaStream_t s) {
   const long long kp = round_up(cols, 64);
-  const size_t esz = op == kOpBF16 ? 2 : 4;
+  const size_t esz = (op == kOpBF16 || op == kOpF16) ? 2 : 4;
   *hi = scratch(rt, slot_hi, rows * kp * esz);
   *lo = op == kOpSplit ? scratch(rt, slot_lo, rows * kp * esz) : nullptr;
   if (!*hi || (op == kOpSplit && !*lo)) return false;

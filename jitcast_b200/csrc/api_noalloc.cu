@@ -43,7 +43,7 @@ extern "C" jc_status jc_linear_device_noalloc(int device, jc_precision precision
                                               const float* w, long long ldw, const float* bias, float* c,
                                               long long ldc, int m, int n, int k, int flags, void* stream) {
   clear_error();
-  if (precision != JC_FP32 && precision != JC_TF32 && precision != JC_BF16)
+  if (precision != JC_FP32 && precision != JC_TF32 && precision != JC_BF16 && precision != JC_FP16)
     return fail(JC_ERR_INVALID_ARG, "unknown precision");
   if (m < 1 || n < 1 || k < 1) return fail(JC_ERR_INVALID_ARG, "m, n and k must be positive");
   if (!a || !w || !c) return fail(JC_ERR_INVALID_ARG, "null buffer");
@@ -55,9 +55,12 @@ extern "C" jc_status jc_linear_device_noalloc(int device, jc_precision precision
   if (gelu && (silu || relu)) return fail(JC_ERR_INVALID_ARG, "JC_GELU cannot be combined with JC_SILU or JC_RELU");
   const int act = silu && relu ? kActSiluRelu : silu ? kActSilu : relu ? kActRelu : gelu ? kActGelu : kActNone;
 
-  const int op = precision == JC_BF16 ? kOpBF16 : precision == JC_TF32 ? kOpTF32 : kOpSplit;
+  const int op = precision == JC_BF16   ? kOpBF16
+                 : precision == JC_FP16 ? kOpF16
+                 : precision == JC_TF32 ? kOpTF32
+                                        : kOpSplit;
   const long long kp = round_up(k, 64);
-  const size_t esz = op == kOpBF16 ? 2 : 4;
+  const size_t esz = (op == kOpBF16 || op == kOpF16) ? 2 : 4;
   const size_t a_part = align256(static_cast<size_t>(m) * kp * esz);
   const size_t w_part = align256(static_cast<size_t>(n) * kp * esz);
   const size_t parts = op == kOpSplit ? 2 : 1;

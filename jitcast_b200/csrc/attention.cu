@@ -19,10 +19,19 @@ template <>
 __device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
 template <>
 __device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <>
+__device__ __forceinline__ float ld_f<__half>(const __half* p) { return __half2float(*p); }
+
+__device__ __forceinline__ float ld_gate(const AttnArgs& a, long long i) {
+  if (a.gate_kind == kOutBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(a.gate)[i]);
+  if (a.gate_kind == kOutF16) return __half2float(static_cast<const __half*>(a.gate)[i]);
+  return static_cast<const float*>(a.gate)[i];
+}
 
 __device__ __forceinline__ void put_op(int kind, void* hi, void* lo, long long i, float v) {
   switch (kind) {
     case kOutBF16: static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v); break;
+    case kOutF16: static_cast<__half*>(hi)[i] = __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f)); break;
     case kOutTF32: static_cast<float*>(hi)[i] = round_tf32(v); break;
     case kOutSplit: {
       const float h = round_tf32(v);
@@ -108,8 +117,7 @@ __global__ void __launch_bounds__(kQ) time_attention_kernel(AttnArgs a) {
 #pragma unroll
   for (int e = 0; e < DH; ++e) {
     float v = acc[e] * inv;
-    if (a.gate) v *= a.gate_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.gate)[go + e])
-                                 : static_cast<const float*>(a.gate)[go + e];
+    if (a.gate) v *= ld_gate(a, go + e);
     put_op(a.out_kind, a.out_hi, a.out_lo, o + e, v);
   }
 }
@@ -167,9 +175,225 @@ __global__ void variate_attention_kernel(AttnArgs a) {
 #pragma unroll
     for (int e = 0; e < DH; ++e) {
       float v = acc[e] * inv;
-      if (a.gate) v *= a.gate_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(a.gate)[go + e])
-                                   : static_cast<const float*>(a.gate)[go + e];
+      if (a.gate) v *= ld_gate(a, go + e);
       put_op(a.out_kind, a.out_hi, a.out_lo, o + e, v);
+    }
+  }
+}
+
+// ---- tensor-core time attention (16-bit q/k/v) ---------------------------------------------
+// One CTA (4 warps) per (row, head). K and V of the row's n tokens are staged in shared memory
+// (rows padded to a multiple of 64, 72-element pitch so ldmatrix rows avoid bank conflicts). Each
+// warp walks 16-query tiles; per 64-key block it forms S = Q·Kᵀ with mma.sync m16n8k16 (FP32
+// accumulate), applies the BlockLayout mask and an online softmax in registers, converts P to the
+// A-operand layout in place and accumulates O += P·V. Key blocks no query of the tile may read
+// (beyond the last query of an all-encoder tile on a row that is not a known covariate) are skipped.
+constexpr int kMmaWarps = 4;
+constexpr int kPitch = 72;       // 64 + 8 halves
+constexpr int kMaxTokens = 256;  // longer rows use the FP32 kernel
+
+template <typename T>
+struct MmaT;
+template <>
+struct MmaT<__nv_bfloat16> {
+  __device__ static void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ static uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&t);
+  }
+};
+template <>
+struct MmaT<__half> {
+  __device__ static void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+  __device__ static uint32_t pack(float lo, float hi) {
+    __half2 t = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&t);
+  }
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int n = a.n, npad = (n + 63) & ~63;
+  T* ks = reinterpret_cast<T*>(smem_raw);
+  T* vs = ks + npad * kPitch;
+  int* kvalid = reinterpret_cast<int*>(vs + npad * kPitch);  // per key: may encoder queries read it
+  const int hh = blockIdx.x % a.heads;
+  const int row = blockIdx.x / a.heads;
+  const T* qkv = static_cast<const T*>(a.qkv);
+  const long long ld = a.ld_qkv;
+  // stage K and V (16-byte vectors), zero rows past n
+  for (int i = threadIdx.x; i < npad * 8; i += blockDim.x) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (r < n) {
+      const T* base = qkv + ((long long)row * n + r) * ld + hh * 64 + c;
+      kv = *reinterpret_cast<const uint4*>(base + a.d);
+      vv = *reinterpret_cast<const uint4*>(base + 2 * a.d);
+    }
+    *reinterpret_cast<uint4*>(ks + r * kPitch + c) = kv;
+    *reinterpret_cast<uint4*>(vs + r * kPitch + c) = vv;
+  }
+  for (int k = threadIdx.x; k < npad; k += blockDim.x)
+    kvalid[k] = k < a.enc ? a.key_valid[(long long)row * a.enc + k] : 0;
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;  // fragment row group and column pair
+  const bool known = a.known[row] != 0;
+  const float sl2 = a.scale * 1.4426950408889634f;  // softmax in base 2
+  const uint32_t ks_base = smem_u32(ks), vs_base = smem_u32(vs);
+  const int qtiles = (n + 15) >> 4;
+  for (int qt = warp; qt < qtiles; qt += kMmaWarps) {
+    const int q0 = qt * 16;
+    // Q fragments for the 4 k-steps of dh = 64, straight from global (rows past n read as 0)
+    uint32_t qf[4][4];
+    {
+      const int ra = q0 + g, rb = q0 + g + 8;
+      const T* pa = qkv + ((long long)row * n + ra) * ld + hh * 64;
+      const T* pb = qkv + ((long long)row * n + rb) * ld + hh * 64;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int c = kk * 16 + tq * 2;
+        qf[kk][0] = ra < n ? *reinterpret_cast<const uint32_t*>(pa + c) : 0u;
+        qf[kk][1] = rb < n ? *reinterpret_cast<const uint32_t*>(pb + c) : 0u;
+        qf[kk][2] = ra < n ? *reinterpret_cast<const uint32_t*>(pa + c + 8) : 0u;
+        qf[kk][3] = rb < n ? *reinterpret_cast<const uint32_t*>(pb + c + 8) : 0u;
+      }
+    }
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
+    // an all-encoder tile on a row that is not a known covariate reads no key past its last query
+    int kend = npad;
+    if (q0 + 15 < a.enc && !known) kend = min(npad, ((q0 + 15) / 64 + 1) * 64);
+    for (int k0 = 0; k0 < kend; k0 += 64) {
+      float sc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp) {  // two 8-key n-tiles per ldmatrix.x4
+          const int krow = k0 + jp * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int kcol = kk * 16 + ((lane >> 3) & 1) * 8;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(ks_base + (krow * kPitch + kcol) * 2, b0, b1, b2, b3);
+          MmaT<T>::mma(sc[2 * jp], qf[kk], b0, b1);
+          MmaT<T>::mma(sc[2 * jp + 1], qf[kk], b2, b3);
+        }
+      }
+      // mask, scale, online softmax (rows g and g + 8 of the tile)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int q = q0 + g + hr * 8;
+        float mx = mrow[hr];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int k = k0 + j * 8 + tq * 2 + c;
+            bool ok;
+            if (q < a.enc) {
+              ok = k < a.enc && (k == q || (kvalid[k] && (k <= q || known)));
+            } else {
+              ok = k < a.enc ? (k < a.ll && kvalid[k]) : (k <= q && k < n);
+            }
+            float v = ok ? sc[j][hr * 2 + c] * sl2 : -INFINITY;
+            sc[j][hr * 2 + c] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float corr = mx == -INFINITY ? 1.0f : ex2(mrow[hr] - mx);
+        mrow[hr] = mx;
+        float sum = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const float v = sc[j][hr * 2 + c];
+            const float p = v == -INFINITY ? 0.0f : ex2(v - mx);
+            sc[j][hr * 2 + c] = p;
+            sum += p;
+          }
+        lrow[hr] = lrow[hr] * corr + sum;  // per-thread partial; reduced at the end
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[j][hr * 2] *= corr;
+          o[j][hr * 2 + 1] *= corr;
+        }
+      }
+      // O += P·V: P's accumulator layout is the A-operand layout of the next MMA
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t pf[4];
+        pf[0] = MmaT<T>::pack(sc[2 * kk][0], sc[2 * kk][1]);
+        pf[1] = MmaT<T>::pack(sc[2 * kk][2], sc[2 * kk][3]);
+        pf[2] = MmaT<T>::pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+        pf[3] = MmaT<T>::pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+        for (int jp = 0; jp < 4; ++jp) {  // two 8-wide dh tiles per ldmatrix.x4.trans
+          const int vrow = k0 + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int vcol = jp * 16 + ((lane >> 4) << 3);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vs_base + (vrow * kPitch + vcol) * 2, b0, b1, b2, b3);
+          MmaT<T>::mma(o[2 * jp], pf, b0, b1);
+          MmaT<T>::mma(o[2 * jp + 1], pf, b2, b3);
+        }
+      }
+    }
+    // finish: full row sums across the quad, normalise, gate, store in the operand format
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float l = lrow[hr];
+      l += __shfl_xor_sync(0xffffffffu, l, 1);
+      l += __shfl_xor_sync(0xffffffffu, l, 2);
+      const int q = q0 + g + hr * 8;
+      if (q >= n) continue;
+      const float inv = 1.0f / l;
+      const long long ob = ((long long)row * n + q) * a.ld_out + hh * 64;
+      const long long gb = ((long long)row * n + q) * a.ld_gate + hh * 64;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int e = j * 8 + tq * 2 + c;
+          float v = o[j][hr * 2 + c] * inv;
+          if (a.gate) v *= ld_gate(a, gb + e);
+          put_op(a.out_kind, a.out_hi, a.out_lo, ob + e, v);
+        }
     }
   }
 }
@@ -207,12 +431,39 @@ cudaError_t launch_variate_t(const AttnArgs& a, cudaStream_t s) {
 
 cudaError_t launch_time_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.rows <= 0) return cudaSuccess;
-  return a.qkv_bf16 ? launch_time_t<__nv_bfloat16>(a, s) : launch_time_t<float>(a, s);
+  if ((a.qkv_kind == kOutBF16 || a.qkv_kind == kOutF16) && a.head_dim == 64 && a.n <= kMaxTokens &&
+      a.ld_qkv % 8 == 0 && a.d % 8 == 0) {
+    const int npad = (a.n + 63) & ~63;
+    const size_t smem = 2 * static_cast<size_t>(npad) * kPitch * 2 + sizeof(int) * npad;
+    const unsigned blocks = static_cast<unsigned>(static_cast<long long>(a.rows) * a.heads);
+    // the shared-memory limit is raised once per device for the largest row (outside any capture:
+    // the first forward of an engine runs eagerly)
+    static bool raised[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!raised[dev & 63]) {
+      const int most = static_cast<int>(2 * static_cast<size_t>(kMaxTokens) * kPitch * 2 + sizeof(int) * kMaxTokens);
+      cudaFuncSetAttribute(time_attention_mma_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+      cudaFuncSetAttribute(time_attention_mma_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+      raised[dev & 63] = true;
+    }
+    if (a.qkv_kind == kOutBF16) {
+      time_attention_mma_kernel<__nv_bfloat16><<<blocks, kMmaWarps * 32, smem, s>>>(a);
+    } else {
+      time_attention_mma_kernel<__half><<<blocks, kMmaWarps * 32, smem, s>>>(a);
+    }
+    return cudaGetLastError();
+  }
+  if (a.qkv_kind == kOutBF16) return launch_time_t<__nv_bfloat16>(a, s);
+  if (a.qkv_kind == kOutF16) return launch_time_t<__half>(a, s);
+  return launch_time_t<float>(a, s);
 }
 
 cudaError_t launch_variate_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.rows <= 0) return cudaSuccess;
-  return a.qkv_bf16 ? launch_variate_t<__nv_bfloat16>(a, s) : launch_variate_t<float>(a, s);
+  if (a.qkv_kind == kOutBF16) return launch_variate_t<__nv_bfloat16>(a, s);
+  if (a.qkv_kind == kOutF16) return launch_variate_t<__half>(a, s);
+  return launch_variate_t<float>(a, s);
 }
 
 }  // namespace jc

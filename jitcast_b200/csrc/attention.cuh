@@ -9,10 +9,10 @@ namespace jc {
 
 struct AttnArgs {
   const void* qkv;  // [rows·n, ld_qkv]: q | k | v, heads-major (head h at columns h·dh within each part)
-  int qkv_bf16;     // qkv element type: bf16 (1) or fp32 (0)
+  int qkv_kind;     // qkv element type: kOutF32, kOutBF16 or kOutF16
   long long ld_qkv;
   const void* gate;  // [rows·n, ld_gate] sigmoid gate multiplied into the output, or null
-  int gate_bf16;
+  int gate_kind;    // kOutF32, kOutBF16 or kOutF16
   long long ld_gate;
   void* out_hi;  // [rows·n, ld_out] in OutKind out_kind
   void* out_lo;

@@ -51,9 +51,15 @@ struct DevLinear {
   int in = 0, out = 0;
 };
 
-inline int op_of_precision(jc_precision p) { return p == JC_BF16 ? kOpBF16 : p == JC_TF32 ? kOpTF32 : kOpSplit; }
-inline int out_of_op(int op) { return op == kOpBF16 ? kOutBF16 : op == kOpTF32 ? kOutTF32 : kOutSplit; }
-inline size_t op_esize(int op) { return op == kOpBF16 ? 2 : 4; }
+inline int op_of_precision(jc_precision p) {
+  return p == JC_BF16 ? kOpBF16 : p == JC_FP16 ? kOpF16 : p == JC_TF32 ? kOpTF32 : kOpSplit;
+}
+inline int out_of_op(int op) {
+  return op == kOpBF16 ? kOutBF16 : op == kOpF16 ? kOutF16 : op == kOpTF32 ? kOutTF32 : kOutSplit;
+}
+inline size_t op_esize(int op) { return (op == kOpBF16 || op == kOpF16) ? 2 : 4; }
+inline bool op_is_16bit(int op) { return op == kOpBF16 || op == kOpF16; }
+inline bool valid_precision_code(int p) { return p == JC_FP32 || p == JC_TF32 || p == JC_BF16 || p == JC_FP16; }
 
 // Allocates an operand buffer of rows × round_up(cols, 64) elements.
 bool alloc_op(DeviceMem& mem, int op, long long rows, long long cols, OpBuf* out);

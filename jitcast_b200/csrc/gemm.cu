@@ -26,7 +26,7 @@ struct Cfg {
   static constexpr int BN = BN_;
   static constexpr int OPK = OPK_;
   static constexpr int BM = 128;
-  static constexpr int ESZ = OPK == kOpBF16 ? 2 : 4;
+  static constexpr int ESZ = (OPK == kOpBF16 || OPK == kOpF16) ? 2 : 4;
   static constexpr int BK = 128 / ESZ;   // K elements per 128-byte swizzled row
   static constexpr int UK = 32 / ESZ;    // K per tcgen05.mma (32 bytes)
   static constexpr int NSUB = BK / UK;   // MMAs per stage per product
@@ -39,7 +39,7 @@ struct Cfg {
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : 2u, BM, BN);
+  static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : OPK == kOpF16 ? 0u : 2u, BM, BN);
   static_assert(STAGES >= 2, "too few stages");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
 };
@@ -112,6 +112,29 @@ __device__ __forceinline__ void store_bf16(__nv_bfloat16* dst, int nv, bool vec,
   }
 }
 
+constexpr float kHalfMax = 65504.0f;
+
+__device__ __forceinline__ void store_f16(__half* dst, int nv, bool vec, const float (&v)[32]) {
+  if (nv == 32 && vec) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half2 t = __floats2half2_rn(fminf(fmaxf(v[8 * q + 2 * j], -kHalfMax), kHalfMax),
+                                      fminf(fmaxf(v[8 * q + 2 * j + 1], -kHalfMax), kHalfMax));
+        w[j] = *reinterpret_cast<uint32_t*>(&t);
+      }
+      d4[q] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < nv) dst[j] = __float2half_rn(fminf(fmaxf(v[j], -kHalfMax), kHalfMax));
+  }
+}
+
 // The operand-typed copy of a row chunk (for the next GEMM's A).
 __device__ __forceinline__ void store_operand(const EpiParams& p, long long off, int nv, const float (&v)[32]) {
   const bool vec = p.vec_ok != 0;
@@ -121,6 +144,9 @@ __device__ __forceinline__ void store_operand(const EpiParams& p, long long off,
       break;
     case kOutF32:
       store_f32(static_cast<float*>(p.o_hi) + off, nv, vec, v);
+      break;
+    case kOutF16:
+      store_f16(static_cast<__half*>(p.o_hi) + off, nv, vec, v);
       break;
     case kOutTF32: {
       float t[32];
@@ -245,8 +271,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
           for (int j = 0; j < 32; ++j) v[j] = sigmoid_f(v[j]);
           const long long off = (long long)orow * p.ldg + (col0 - p.n_split);
           const int nv = min(32, N - col0);
-          if (p.g_bf16)
+          if (p.g_kind == kOutBF16)
             store_bf16(static_cast<__nv_bfloat16*>(p.g_out) + off, nv, p.vec_ok != 0, v);
+          else if (p.g_kind == kOutF16)
+            store_f16(static_cast<__half*>(p.g_out) + off, nv, p.vec_ok != 0, v);
           else
             store_f32(static_cast<float*>(p.g_out) + off, nv, p.vec_ok != 0, v);
         }
@@ -417,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t ad = sdesc_k_sw128(sa + 32 * k);
             const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
             const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            if (OPK == kOpBF16) {
+            if (OPK == kOpBF16 || OPK == kOpF16) {
               umma_bf16(d, ad, bd, C::IDESC, acc);
             } else if (OPK == kOpTF32) {
               umma_tf32(d, ad, bd, C::IDESC, acc);
@@ -493,12 +521,15 @@ static bool make_map(CUtensorMap* map, const void* base, int op, long long rows,
                      int box_rows) {
   auto enc = get_encode();
   if (!enc) return false;
-  const int esz = op == kOpBF16 ? 2 : 4;
+  const int esz = (op == kOpBF16 || op == kOpF16) ? 2 : 4;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * esz)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, op == kOpBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+  const CUtensorMapDataType dt = op == kOpBF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : op == kOpF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = enc(map, dt, 2,
                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -529,8 +560,8 @@ static int qkv_tile_choices(const EpiParams& e) {
 
 const char* check_gemm(const GemmArgs& g) {
   if (g.M < 1 || g.N < 1 || g.K < 1) return "M, N and K must be positive";
-  if (g.op < kOpBF16 || g.op > kOpSplit) return "unknown operand kind";
-  const int esz = g.op == kOpBF16 ? 2 : 4;
+  if (g.op < kOpBF16 || g.op > kOpF16) return "unknown operand kind";
+  const int esz = (g.op == kOpBF16 || g.op == kOpF16) ? 2 : 4;
   if (!g.a_hi || !g.w_hi) return "null operand";
   if (g.op == kOpSplit && (!g.a_lo || !g.w_lo)) return "split operands need hi and lo buffers";
   if (!aligned16(g.a_hi) || !aligned16(g.w_hi) || (g.a_lo && !aligned16(g.a_lo)) || (g.w_lo && !aligned16(g.w_lo)))
@@ -616,9 +647,9 @@ static int vector_ok(const EpiParams& e) {
   auto ok = [](const void* p, long long ld, int esz) {
     return p == nullptr || (aligned16(p) && (ld * esz) % 16 == 0);
   };
-  const int oesz = e.o_kind == kOutBF16 ? 2 : 4;
+  const int oesz = (e.o_kind == kOutBF16 || e.o_kind == kOutF16) ? 2 : 4;
   return ok(e.c, e.ldc, 4) && ok(e.cin, e.ldcin, 4) && ok(e.bias, 0, 4) && ok(e.o_hi, e.ldo, oesz) &&
-         ok(e.o_lo, e.ldo, oesz) && ok(e.g_out, e.ldg, e.g_bf16 ? 2 : 4);
+         ok(e.o_lo, e.ldo, oesz) && ok(e.g_out, e.ldg, (e.g_kind == kOutBF16 || e.g_kind == kOutF16) ? 2 : 4);
 }
 
 cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err) {
@@ -631,6 +662,7 @@ cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err)
   switch (g.op) {                                                       \
     case kOpBF16: return launch_cfg<BN_, kOpBF16>(g, stream, err, sms); \
     case kOpTF32: return launch_cfg<BN_, kOpTF32>(g, stream, err, sms); \
+    case kOpF16: return launch_cfg<BN_, kOpF16>(g, stream, err, sms);   \
     default: return launch_cfg<BN_, kOpSplit>(g, stream, err, sms);     \
   }
   if (bn == 256) {

@@ -13,6 +13,7 @@ enum OperandKind : int {
   kOpBF16 = 0,   // bfloat16; tcgen05 kind::f16
   kOpTF32 = 1,   // fp32 container rounded to TF32; kind::tf32
   kOpSplit = 2,  // fp32 as a TF32 hi/lo pair; three kind::tf32 MMAs (hi·hi + hi·lo + lo·hi)
+  kOpF16 = 3,    // IEEE half; tcgen05 kind::f16
 };
 
 // How an epilogue writes its operand-typed copy of the result.
@@ -22,6 +23,7 @@ enum OutKind : int {
   kOutTF32 = 2,   // fp32, rounded to TF32
   kOutSplit = 3,  // fp32 hi (TF32) and lo (residual) buffers
   kOutF32 = 4,    // fp32, unrounded
+  kOutF16 = 5,    // IEEE half, saturated to ±65504
 };
 
 // kActSiluRelu is the reference's SILU|RELU flag pair: ReLU(SiLU(v)).
@@ -66,9 +68,9 @@ struct EpiParams {
   const int* pos;           // [M] index into rope_table rows
   const float* rope_table;  // [positions, head_dim]: cos at e, sin at head_dim/2 + e
   int n_split;
-  void* g_out;  // gate output (sigmoid), fp32 or bf16
+  void* g_out;  // gate output (sigmoid) in OutKind g_kind: kOutF32, kOutBF16 or kOutF16
   long long ldg;
-  int g_bf16;
+  int g_kind;
   // Optional: Σ over the row of the fp32 output squared, atomically added per row.
   float* rowsq;
   // Optional: each output row scaled by row_scale[r] before the bias (a folded RMSNorm).

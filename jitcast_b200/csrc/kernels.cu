@@ -12,6 +12,7 @@ namespace {
 __device__ __forceinline__ void put(int kind, void* hi, void* lo, long long i, float v) {
   switch (kind) {
     case kOutBF16: static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v); break;
+    case kOutF16: static_cast<__half*>(hi)[i] = __float2half_rn(fminf(fmaxf(v, -65504.0f), 65504.0f)); break;
     case kOutTF32: static_cast<float*>(hi)[i] = round_tf32(v); break;
     case kOutSplit: {
       const float h = round_tf32(v);
@@ -23,7 +24,9 @@ __device__ __forceinline__ void put(int kind, void* hi, void* lo, long long i, f
   }
 }
 
-int out_kind_of(int op) { return op == kOpBF16 ? kOutBF16 : op == kOpTF32 ? kOutTF32 : kOutSplit; }
+int out_kind_of(int op) {
+  return op == kOpBF16 ? kOutBF16 : op == kOpF16 ? kOutF16 : op == kOpTF32 ? kOutTF32 : kOutSplit;
+}
 
 __global__ void convert_kernel(int kind, const float* __restrict__ src, long long lds, void* hi, void* lo,
                                long long ldd, long long rows, int cols) {

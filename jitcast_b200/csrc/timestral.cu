@@ -92,8 +92,9 @@ struct TimestralEngine : jc_engine {
     }
   }
 
-  int qkv_out_kind() const { return op == kOpBF16 ? kOutBF16 : kOutF32; }
-  size_t qkv_esize() const { return op == kOpBF16 ? 2 : 4; }
+  // q|k|v and the gate: 16-bit in the 16-bit modes, FP32 otherwise (attention then runs on FP32 inputs)
+  int qkv_out_kind() const { return op == kOpBF16 ? kOutBF16 : op == kOpF16 ? kOutF16 : kOutF32; }
+  size_t qkv_esize() const { return op_is_16bit(op) ? 2 : 4; }
 };
 
 // ---- weight binding and packing ---------------------------------------------------------------
@@ -366,14 +367,14 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       g.ep.n_split = 3 * d;
       g.ep.g_out = p.gate;
       g.ep.ldg = d;
-      g.ep.g_bf16 = op == kOpBF16;
+      g.ep.g_kind = e.qkv_out_kind();
       JC_TRY(gemm(dv, g, s));
       AttnArgs a{};
       a.qkv = p.qkv;
-      a.qkv_bf16 = op == kOpBF16;
+      a.qkv_kind = e.qkv_out_kind();
       a.ld_qkv = 3LL * d;
       a.gate = A.gated ? p.gate : nullptr;
-      a.gate_bf16 = op == kOpBF16;
+      a.gate_kind = e.qkv_out_kind();
       a.ld_gate = d;
       a.out_hi = p.att.hi;
       a.out_lo = p.att.lo;
@@ -570,8 +571,7 @@ jc_status jc_engine_create_timestral(const jc_timestral_desc* desc, const jc_ten
   if (!out) return fail(JC_ERR_INVALID_ARG, "null engine out-pointer");
   *out = nullptr;
   if (!desc || !weights || n_weights < 1) return fail(JC_ERR_INVALID_ARG, "null description or weights");
-  if (precision != JC_FP32 && precision != JC_TF32 && precision != JC_BF16)
-    return fail(JC_ERR_INVALID_ARG, "unknown precision");
+  if (!valid_precision_code(precision)) return fail(JC_ERR_INVALID_ARG, "unknown precision");
   const jc_timestral_desc& c = *desc;
   if (c.patch_size < 1 || c.d_model < 1 || c.num_heads < 1 || c.d_model % c.num_heads != 0)
     return fail(JC_ERR_INVALID_ARG, "d_model " + std::to_string(c.d_model) + " is not divisible by num_heads " +

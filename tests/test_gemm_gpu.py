@@ -6,7 +6,7 @@ error measure (relative max error, KernelHarness.java:104-117), plus BASELINE co
 that exercise every tile width, multi-stage K loops and the persistent tile walk.
 
 Tolerances: FP32 (3×TF32) 1e-4 — the reference's FP32 bar; TF32 1e-3 and BF16 1e-2 — the bars
-BASELINE.json sets for the reduced-precision modes.
+BASELINE.json sets for the reduced-precision modes; FP16 2e-3 (11-bit mantissa).
 """
 
 from pathlib import Path
@@ -18,12 +18,12 @@ import oracle
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"fp32": 1e-4, "tf32": 1e-3, "bf16": 1e-2}
+TOL = {"fp32": 1e-4, "tf32": 1e-3, "bf16": 1e-2, "fp16": 2e-3}
 GOLDEN = np.load(Path(__file__).parent / "golden" / "kernels_gemm.npz")
 CASES = ["every_flag", "blocked", "blocked_wide"]
 
 
-@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
 @pytest.mark.parametrize("case", CASES)
 def test_kernels_accel_cases(jc, case, precision):
     a, w, b, c0 = (GOLDEN[f"{case}/{k}"] for k in ("a", "w", "bias", "c0"))
@@ -45,7 +45,7 @@ def config1(seed=0):
     return x, w, b
 
 
-@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
 def test_config1_host(jc, precision):
     x, w, b = config1()
     got = jc.ops.linear(x, w, b, precision=precision)
@@ -65,7 +65,7 @@ def test_other_activations(jc, flags):
     assert err < 1e-4
 
 
-@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16"])
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
 @pytest.mark.parametrize("m,n,k", [(1024, 768, 256),      # config 1
                                    (10240, 256, 128),     # 128-wide tiles
                                    (2053, 2304, 768),     # 256-wide tiles, M tail, persistent walk

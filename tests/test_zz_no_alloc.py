@@ -16,7 +16,7 @@ from jitcast_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
-TOL = {_lib.FP32: 1e-4, _lib.TF32: 1e-3, _lib.BF16: 1e-2}
+TOL = {_lib.FP32: 1e-4, _lib.TF32: 1e-3, _lib.BF16: 1e-2, _lib.FP16: 2e-3}
 
 
 def _run(fn, prec, a, w, b, c, flags, stream):
@@ -27,7 +27,7 @@ def _run(fn, prec, a, w, b, c, flags, stream):
     assert st == _lib.OK, _lib.last_error()
 
 
-@pytest.mark.parametrize("prec", [_lib.BF16, _lib.TF32, _lib.FP32])
+@pytest.mark.parametrize("prec", [_lib.BF16, _lib.TF32, _lib.FP32, _lib.FP16])
 def test_noalloc_matches_allocating_entry_point(prec):
     import torch
 
