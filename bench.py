@@ -270,7 +270,8 @@ def main():
     prof = engine.profile()
     engine.set_option("profile", 0)
     launches_per_forward = sum(v["launches"] for v in prof.values()) + 3  # + the 3 index-rebasing kernels
-    g = prof["gemm"]
+    gemms = {k: v for k, v in prof.items() if k.startswith("gemm")}
+    g = {f: sum(v[f] for v in gemms.values()) for f in ("ms", "launches", "flops")}
     gemm_ms = g["ms"] / g["launches"]
     gemm_flops = g["flops"] / g["launches"]
     pk, pk_kind = peaks()
@@ -306,7 +307,9 @@ def main():
                          "gemm_time_share": total_gemm_share},
             "cpu_baseline": cpu, "clocks": clocks.summary(),
             "gpu_launches": launches_per_forward * len(chunks) * args.steps,
-            "kernel_profile": {k: {"ms": v["ms"], "launches": v["launches"]} for k, v in prof.items()}}
+            "kernel_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
+                                   **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {})}
+                               for k, v in prof.items()}}
     print(json.dumps(line), flush=True)
     engine.close()
     if world > 1:

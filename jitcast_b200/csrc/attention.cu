@@ -6,6 +6,8 @@
 // Semantics: CpuTimestral.timeAttention / variateAttention (timestral/cpu/CpuTimestral.java:191-314)
 // and the masks of BlockLayout.timeAllowed / variateAllowed (timestral/BlockLayout.java:209-243);
 // the gate att · sigmoid(g) of CpuTimestral.java:156-161.
+#include <type_traits>
+
 #include "attention.cuh"
 #include "ptx.cuh"
 
@@ -182,7 +184,8 @@ __global__ void variate_attention_kernel(AttnArgs a) {
 }
 
 // ---- tensor-core time attention (16-bit q/k/v) ---------------------------------------------
-// One CTA (4 warps) per (row, head). K and V of the row's n tokens are staged in shared memory
+// One CTA (4 warps) per (row, head). K and V of the row's n tokens are staged in shared memory as
+// FP16 (a BF16 input converts exactly within FP16's range, so P·V keeps an 11-bit P in both modes)
 // (rows padded to a multiple of 64, 72-element pitch so ldmatrix rows avoid bank conflicts). Each
 // warp walks 16-query tiles; per 64-key block it forms S = Q·Kᵀ with mma.sync m16n8k16 (FP32
 // accumulate), applies the BlockLayout mask and an online softmax in registers, converts P to the
@@ -241,12 +244,43 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+__device__ __forceinline__ uint32_t to_h2(__nv_bfloat162 v) {
+  const float2 f = __bfloat1622float2(v);
+  __half2 h = __floats2half2_rn(fminf(fmaxf(f.x, -65504.0f), 65504.0f), fminf(fmaxf(f.y, -65504.0f), 65504.0f));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t to_h2(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// Eight 16-bit values (one 16-byte vector) as FP16.
+template <typename T>
+__device__ __forceinline__ uint4 to_h8(uint4 u) {
+  if constexpr (std::is_same<T, __half>::value) {
+    return u;
+  } else {
+    uint4 r;
+    r.x = to_h2(*reinterpret_cast<__nv_bfloat162*>(&u.x));
+    r.y = to_h2(*reinterpret_cast<__nv_bfloat162*>(&u.y));
+    r.z = to_h2(*reinterpret_cast<__nv_bfloat162*>(&u.z));
+    r.w = to_h2(*reinterpret_cast<__nv_bfloat162*>(&u.w));
+    return r;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t ld_h2(const T* p) {
+  if constexpr (std::is_same<T, __half>::value) {
+    return *reinterpret_cast<const uint32_t*>(p);
+  } else {
+    return to_h2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int n = a.n, npad = (n + 63) & ~63;
-  T* ks = reinterpret_cast<T*>(smem_raw);
-  T* vs = ks + npad * kPitch;
+  __half* ks = reinterpret_cast<__half*>(smem_raw);
+  __half* vs = ks + npad * kPitch;
   int* kvalid = reinterpret_cast<int*>(vs + npad * kPitch);  // per key: may encoder queries read it
   const int hh = blockIdx.x % a.heads;
   const int row = blockIdx.x / a.heads;
@@ -258,8 +292,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
     uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
     if (r < n) {
       const T* base = qkv + ((long long)row * n + r) * ld + hh * 64 + c;
-      kv = *reinterpret_cast<const uint4*>(base + a.d);
-      vv = *reinterpret_cast<const uint4*>(base + 2 * a.d);
+      kv = to_h8<T>(*reinterpret_cast<const uint4*>(base + a.d));
+      vv = to_h8<T>(*reinterpret_cast<const uint4*>(base + 2 * a.d));
     }
     *reinterpret_cast<uint4*>(ks + r * kPitch + c) = kv;
     *reinterpret_cast<uint4*>(vs + r * kPitch + c) = vv;
@@ -285,10 +319,10 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const int c = kk * 16 + tq * 2;
-        qf[kk][0] = ra < n ? *reinterpret_cast<const uint32_t*>(pa + c) : 0u;
-        qf[kk][1] = rb < n ? *reinterpret_cast<const uint32_t*>(pb + c) : 0u;
-        qf[kk][2] = ra < n ? *reinterpret_cast<const uint32_t*>(pa + c + 8) : 0u;
-        qf[kk][3] = rb < n ? *reinterpret_cast<const uint32_t*>(pb + c + 8) : 0u;
+        qf[kk][0] = ra < n ? ld_h2(pa + c) : 0u;
+        qf[kk][1] = rb < n ? ld_h2(pb + c) : 0u;
+        qf[kk][2] = ra < n ? ld_h2(pa + c + 8) : 0u;
+        qf[kk][3] = rb < n ? ld_h2(pb + c + 8) : 0u;
       }
     }
     float o[8][4];
@@ -310,8 +344,8 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
           const int kcol = kk * 16 + ((lane >> 3) & 1) * 8;
           uint32_t b0, b1, b2, b3;
           ldsm_x4(ks_base + (krow * kPitch + kcol) * 2, b0, b1, b2, b3);
-          MmaT<T>::mma(sc[2 * jp], qf[kk], b0, b1);
-          MmaT<T>::mma(sc[2 * jp + 1], qf[kk], b2, b3);
+          MmaT<__half>::mma(sc[2 * jp], qf[kk], b0, b1);
+          MmaT<__half>::mma(sc[2 * jp + 1], qf[kk], b2, b3);
         }
       }
       // mask, scale, online softmax (rows g and g + 8 of the tile)
@@ -359,18 +393,18 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         uint32_t pf[4];
-        pf[0] = MmaT<T>::pack(sc[2 * kk][0], sc[2 * kk][1]);
-        pf[1] = MmaT<T>::pack(sc[2 * kk][2], sc[2 * kk][3]);
-        pf[2] = MmaT<T>::pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
-        pf[3] = MmaT<T>::pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+        pf[0] = MmaT<__half>::pack(sc[2 * kk][0], sc[2 * kk][1]);
+        pf[1] = MmaT<__half>::pack(sc[2 * kk][2], sc[2 * kk][3]);
+        pf[2] = MmaT<__half>::pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+        pf[3] = MmaT<__half>::pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
 #pragma unroll
         for (int jp = 0; jp < 4; ++jp) {  // two 8-wide dh tiles per ldmatrix.x4.trans
           const int vrow = k0 + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
           const int vcol = jp * 16 + ((lane >> 4) << 3);
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(vs_base + (vrow * kPitch + vcol) * 2, b0, b1, b2, b3);
-          MmaT<T>::mma(o[2 * jp], pf, b0, b1);
-          MmaT<T>::mma(o[2 * jp + 1], pf, b2, b3);
+          MmaT<__half>::mma(o[2 * jp], pf, b0, b1);
+          MmaT<__half>::mma(o[2 * jp + 1], pf, b2, b3);
         }
       }
     }

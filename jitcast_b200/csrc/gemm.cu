@@ -44,9 +44,12 @@ struct Cfg {
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
 };
 
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int kEpiWarps = 8;                    // two warps per TMEM lane quarter, splitting the columns
+constexpr int kThreads = 32 * (2 + kEpiWarps);  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 
 // ---- epilogue helpers ---------------------------------------------------------------------
+// vec_ok levels: 2 = every pointer and pitch 32-byte aligned (256-bit accesses, whole 32-byte
+// sectors), 1 = 16-byte aligned, 0 = scalar.
 __device__ __forceinline__ float apply_act(int act, float v) {
   switch (act) {
     case kActSilu: return silu_f(v);
@@ -58,27 +61,63 @@ __device__ __forceinline__ float apply_act(int act, float v) {
   }
 }
 
-__device__ __forceinline__ void add_bias(const EpiParams& p, int col0, int nv, float (&v)[32]) {
-  if (nv == 32 && p.vec_ok) {
-    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+__device__ __forceinline__ void st8_f32(float* p, const float* v) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
+               "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void st8_b32(void* p, const uint32_t* u) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(u[0]), "r"(u[1]), "r"(u[2]),
+               "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void ld8_f32(const float* p, float* v) {
+  asm volatile("ld.global.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+               : "l"(p));
+}
+
+__device__ __forceinline__ void ld8_f32_nc(const float* p, float* v) {
+  asm volatile("ld.global.nc.v8.f32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+               : "l"(p));
+}
+
+// 32 (or nv) fp32 values starting at src: read-only data (bias, tables).
+__device__ __forceinline__ void load_ro(const float* src, int nv, int vec, float (&v)[32]) {
+  if (nv == 32 && vec == 2) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) ld8_f32_nc(src + 8 * q, v + 8 * q);
+  } else if (nv == 32 && vec == 1) {
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      float4 b = __ldg(b4 + q);
-      v[4 * q] += b.x;
-      v[4 * q + 1] += b.y;
-      v[4 * q + 2] += b.z;
-      v[4 * q + 3] += b.w;
+      const float4 b = __ldg(reinterpret_cast<const float4*>(src) + q);
+      v[4 * q] = b.x;
+      v[4 * q + 1] = b.y;
+      v[4 * q + 2] = b.z;
+      v[4 * q + 3] = b.w;
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nv) v[j] += __ldg(p.bias + col0 + j);
+    for (int j = 0; j < 32; ++j) v[j] = j < nv ? __ldg(src + j) : 0.0f;
   }
 }
 
+__device__ __forceinline__ void add_bias(const EpiParams& p, int col0, int nv, float (&v)[32]) {
+  float b[32];
+  load_ro(p.bias + col0, nv, p.vec_ok, b);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] += b[j];
+}
+
 // Writes 32 (or nv) fp32 values of one row to an fp32 buffer.
-__device__ __forceinline__ void store_f32(float* dst, int nv, bool vec, const float (&v)[32]) {
-  if (nv == 32 && vec) {
+__device__ __forceinline__ void store_f32(float* dst, int nv, int vec, const float (&v)[32]) {
+  if (nv == 32 && vec == 2) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) st8_f32(dst + 8 * q, v + 8 * q);
+  } else if (nv == 32 && vec == 1) {
     float4* d4 = reinterpret_cast<float4*>(dst);
 #pragma unroll
     for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
@@ -89,64 +128,57 @@ __device__ __forceinline__ void store_f32(float* dst, int nv, bool vec, const fl
   }
 }
 
-__device__ __forceinline__ void store_bf16(__nv_bfloat16* dst, int nv, bool vec, const float (&v)[32]) {
-  if (nv == 32 && vec) {
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 u;
-      __nv_bfloat162 t0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
-      __nv_bfloat162 t1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
-      __nv_bfloat162 t2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
-      __nv_bfloat162 t3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
-      u.x = *reinterpret_cast<uint32_t*>(&t0);
-      u.y = *reinterpret_cast<uint32_t*>(&t1);
-      u.z = *reinterpret_cast<uint32_t*>(&t2);
-      u.w = *reinterpret_cast<uint32_t*>(&t3);
-      d4[q] = u;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < nv) dst[j] = __float2bfloat16_rn(v[j]);
-  }
-}
-
 constexpr float kHalfMax = 65504.0f;
 
-__device__ __forceinline__ void store_f16(__half* dst, int nv, bool vec, const float (&v)[32]) {
-  if (nv == 32 && vec) {
-    uint4* d4 = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  __half2 t = __floats2half2_rn(fminf(fmaxf(a, -kHalfMax), kHalfMax), fminf(fmaxf(b, -kHalfMax), kHalfMax));
+  return *reinterpret_cast<uint32_t*>(&t);
+}
+
+// 32 values as 16-bit (bf16 or saturated f16) to dst.
+template <bool F16>
+__device__ __forceinline__ void store_16(void* dst, int nv, int vec, const float (&v)[32]) {
+  if (nv == 32 && vec >= 1) {
+    uint32_t u[16];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t w[4];
+    for (int j = 0; j < 16; ++j) u[j] = F16 ? pack_f16(v[2 * j], v[2 * j + 1]) : pack_bf16(v[2 * j], v[2 * j + 1]);
+    if (vec == 2) {
+      st8_b32(dst, u);
+      st8_b32(static_cast<uint32_t*>(dst) + 8, u + 8);
+    } else {
+      uint4* d4 = static_cast<uint4*>(dst);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        __half2 t = __floats2half2_rn(fminf(fmaxf(v[8 * q + 2 * j], -kHalfMax), kHalfMax),
-                                      fminf(fmaxf(v[8 * q + 2 * j + 1], -kHalfMax), kHalfMax));
-        w[j] = *reinterpret_cast<uint32_t*>(&t);
-      }
-      d4[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int q = 0; q < 4; ++q) d4[q] = make_uint4(u[4 * q], u[4 * q + 1], u[4 * q + 2], u[4 * q + 3]);
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (j < nv) dst[j] = __float2half_rn(fminf(fmaxf(v[j], -kHalfMax), kHalfMax));
+      if (j < nv) {
+        if (F16)
+          static_cast<__half*>(dst)[j] = __float2half_rn(fminf(fmaxf(v[j], -kHalfMax), kHalfMax));
+        else
+          static_cast<__nv_bfloat16*>(dst)[j] = __float2bfloat16_rn(v[j]);
+      }
   }
 }
 
 // The operand-typed copy of a row chunk (for the next GEMM's A).
 __device__ __forceinline__ void store_operand(const EpiParams& p, long long off, int nv, const float (&v)[32]) {
-  const bool vec = p.vec_ok != 0;
+  const int vec = p.vec_ok;
   switch (p.o_kind) {
     case kOutBF16:
-      store_bf16(static_cast<__nv_bfloat16*>(p.o_hi) + off, nv, vec, v);
+      store_16<false>(static_cast<__nv_bfloat16*>(p.o_hi) + off, nv, vec, v);
+      break;
+    case kOutF16:
+      store_16<true>(static_cast<__half*>(p.o_hi) + off, nv, vec, v);
       break;
     case kOutF32:
       store_f32(static_cast<float*>(p.o_hi) + off, nv, vec, v);
-      break;
-    case kOutF16:
-      store_f16(static_cast<__half*>(p.o_hi) + off, nv, vec, v);
       break;
     case kOutTF32: {
       float t[32];
@@ -186,7 +218,13 @@ __device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int
   }
   if (p.accumulate) {
     const float* src = p.cin + (long long)orow * p.ldcin + col0;
-    if (nv == 32 && p.vec_ok) {
+    if (nv == 32 && p.vec_ok == 2) {
+      float c[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ld8_f32(src + 8 * q, c + 8 * q);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] += c[j];
+    } else if (nv == 32 && p.vec_ok == 1) {
       const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
@@ -202,7 +240,7 @@ __device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int
         if (j < nv) v[j] += src[j];
     }
   }
-  if (p.c) store_f32(p.c + (long long)orow * p.ldc + col0, nv, p.vec_ok != 0, v);
+  if (p.c) store_f32(p.c + (long long)orow * p.ldc + col0, nv, p.vec_ok, v);
   if (p.o_kind != kOutNone) store_operand(p, (long long)orow * p.ldo + col0, nv, v);
   if (p.rowsq) {
 #pragma unroll
@@ -219,96 +257,93 @@ __device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
-// One accumulator tile (rows m0.., columns n0..) → HBM, for the thread's row.
+// One accumulator tile (rows m0.., columns n0..) → HBM, for the thread's row. The tile's columns are
+// split into 64-column units (a head of q|k|v in the RoPE mode); `half` (0 or 1) takes every other unit.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, int m0, int n0, uint32_t tbase,
-                                              int row_in_tile) {
+                                              int row_in_tile, int half) {
   const int row = m0 + row_in_tile;
   const bool live = row < M;
   const int orow = live ? (row / p.rg) * p.rg_stride + row % p.rg + p.rg_off : 0;
   float sq = 0.0f;
-  if (p.mode == kEpiPlain) {
+  if (p.mode == kEpiPlain || (p.mode == kEpiQKV && n0 >= p.n_split)) {
+    const bool gate = p.mode == kEpiQKV;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      const int col0 = n0 + 32 * c;
-      if (col0 >= N) break;  // warp-uniform
-      float v[32];
-      load_chunk(tbase + 32 * c, v);
-      if (live) epi_plain_chunk(p, row, orow, col0, min(32, N - col0), v, sq);
+    for (int u = half; u < BN / 64; u += 2) {
+#pragma unroll 1
+      for (int c = 2 * u; c < 2 * u + 2; ++c) {
+        const int col0 = n0 + 32 * c;
+        if (col0 >= N) break;  // warp-uniform
+        float v[32];
+        load_chunk(tbase + 32 * c, v);
+        if (!live) continue;
+        const int nv = min(32, N - col0);
+        if (!gate) {
+          epi_plain_chunk(p, row, orow, col0, nv, v, sq);
+          continue;
+        }
+        if (p.bias_on) add_bias(p, col0, nv, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = sigmoid_f(v[j]);
+        const long long off = (long long)orow * p.ldg + (col0 - p.n_split);
+        if (p.g_kind == kOutBF16)
+          store_16<false>(static_cast<__nv_bfloat16*>(p.g_out) + off, nv, p.vec_ok, v);
+        else if (p.g_kind == kOutF16)
+          store_16<true>(static_cast<__half*>(p.g_out) + off, nv, p.vec_ok, v);
+        else
+          store_f32(static_cast<float*>(p.g_out) + off, nv, p.vec_ok, v);
+      }
     }
   } else if (p.mode == kEpiSwiGLU) {
     // tile columns (64u .. 64u+31) are the SiLU half of output columns (n0/2 + 32u ..), (64u+32 ..) the linear half
 #pragma unroll 1
-    for (int u = 0; u < BN / 64; ++u) {
+    for (int u = half; u < BN / 64; u += 2) {
       const int col0 = n0 + 64 * u;
       if (col0 >= N) break;
       float a[32], b[32];
       load_chunk(tbase + 64 * u, a);
       load_chunk(tbase + 64 * u + 32, b);
-      if (live) {
-        if (p.bias_on) {
-          add_bias(p, col0, 32, a);
-          add_bias(p, col0 + 32, 32, b);
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) a[j] = silu_f(a[j]) * b[j];
-        const int ocol = col0 / 2;
-        store_operand(p, (long long)orow * p.ldo + ocol, min(32, N / 2 - ocol), a);
+      if (!live) continue;
+      if (p.bias_on) {
+        add_bias(p, col0, 32, a);
+        add_bias(p, col0 + 32, 32, b);
       }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) a[j] = silu_f(a[j]) * b[j];
+      const int ocol = col0 / 2;
+      store_operand(p, (long long)orow * p.ldo + ocol, min(32, N / 2 - ocol), a);
     }
-  } else {  // kEpiQKV
-    const int hd = p.head_dim, half = hd / 2;
-    if (n0 >= p.n_split) {
+  } else {  // kEpiQKV, q|k|v columns: one head (head_dim columns) at a time, RoPE on q and k
+    const int hd = p.head_dim, hh = hd / 2;
+    const int pos = live ? p.pos[row] : 0;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col0 = n0 + 32 * c;
-        if (col0 >= N) break;
-        float v[32];
-        load_chunk(tbase + 32 * c, v);
-        if (live) {
-          if (p.bias_on) add_bias(p, col0, min(32, N - col0), v);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = sigmoid_f(v[j]);
-          const long long off = (long long)orow * p.ldg + (col0 - p.n_split);
-          const int nv = min(32, N - col0);
-          if (p.g_kind == kOutBF16)
-            store_bf16(static_cast<__nv_bfloat16*>(p.g_out) + off, nv, p.vec_ok != 0, v);
-          else if (p.g_kind == kOutF16)
-            store_f16(static_cast<__half*>(p.g_out) + off, nv, p.vec_ok != 0, v);
-          else
-            store_f32(static_cast<float*>(p.g_out) + off, nv, p.vec_ok != 0, v);
+    for (int h0 = half * hd; h0 < BN; h0 += 2 * hd) {
+#pragma unroll 1
+      for (int s = 0; s < hh; s += 32) {
+        const int ca = h0 + s, cb = h0 + hh + s;
+        if (n0 + ca >= N) break;
+        float a[32], b[32];
+        load_chunk(tbase + ca, a);
+        load_chunk(tbase + cb, b);
+        if (!live) continue;
+        if (p.bias_on) {
+          add_bias(p, n0 + ca, 32, a);
+          add_bias(p, n0 + cb, 32, b);
         }
-      }
-    } else {
-      const int pos = live ? p.pos[row] : 0;
-#pragma unroll 1
-      for (int h0 = 0; h0 < BN; h0 += hd) {
-#pragma unroll 1
-        for (int s = 0; s < half; s += 32) {
-          const int ca = h0 + s, cb = h0 + half + s;
-          if (n0 + ca >= N) break;
-          float a[32], b[32];
-          load_chunk(tbase + ca, a);
-          load_chunk(tbase + cb, b);
-          if (!live) continue;
-          if (p.bias_on) {
-            add_bias(p, n0 + ca, 32, a);
-            add_bias(p, n0 + cb, 32, b);
-          }
-          if (n0 + ca < p.rope_cols) {
-            const float* tc = p.rope_table + (long long)pos * hd + s;
-            const float* ts = tc + half;
+        if (n0 + ca < p.rope_cols) {
+          float cs[32], sn[32];
+          const float* tc = p.rope_table + (long long)pos * hd + s;
+          load_ro(tc, 32, p.vec_ok, cs);
+          load_ro(tc + hh, 32, p.vec_ok, sn);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float cs = __ldg(tc + j), sn = __ldg(ts + j);
-              const float x = a[j], y = b[j];
-              a[j] = x * cs + -y * sn;
-              b[j] = y * cs + x * sn;
-            }
+          for (int j = 0; j < 32; ++j) {
+            const float x = a[j], y = b[j];
+            a[j] = x * cs[j] + -y * sn[j];
+            b[j] = y * cs[j] + x * sn[j];
           }
-          store_operand(p, (long long)orow * p.ldo + n0 + ca, 32, a);
-          store_operand(p, (long long)orow * p.ldo + n0 + cb, 32, b);
         }
+        store_operand(p, (long long)orow * p.ldo + n0 + ca, 32, a);
+        store_operand(p, (long long)orow * p.ldo + n0 + cb, 32, b);
       }
     }
   }
@@ -344,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(acc_full + b, 1);
-      mbar_init(acc_empty + b, 128);
+      mbar_init(acc_empty + b, 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -471,8 +506,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0);
     }
   } else {
-    // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 ----
+    // ---- epilogue: warps 2..9; TMEM lane quarter = warp % 4, column half = (warp - 2) / 4 ----
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     int it = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
@@ -488,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile);
+      epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile, half);
       tc_fence_before();
       mbar_arrive(acc_empty + buf);
     }
@@ -642,14 +678,20 @@ static int choose_bn(const GemmArgs& g, int num_sms) {
   return 256;
 }
 
-// Whether every epilogue pointer and pitch allows 16-byte vector access.
+// The widest access every epilogue pointer and pitch allows: 2 = 32 bytes, 1 = 16 bytes, 0 = scalar.
 static int vector_ok(const EpiParams& e) {
-  auto ok = [](const void* p, long long ld, int esz) {
-    return p == nullptr || (aligned16(p) && (ld * esz) % 16 == 0);
+  auto ok = [](const void* p, long long ld, int esz, unsigned align) {
+    return p == nullptr || ((reinterpret_cast<uintptr_t>(p) % align) == 0 && (ld * esz) % align == 0);
   };
   const int oesz = (e.o_kind == kOutBF16 || e.o_kind == kOutF16) ? 2 : 4;
-  return ok(e.c, e.ldc, 4) && ok(e.cin, e.ldcin, 4) && ok(e.bias, 0, 4) && ok(e.o_hi, e.ldo, oesz) &&
-         ok(e.o_lo, e.ldo, oesz) && ok(e.g_out, e.ldg, (e.g_kind == kOutBF16 || e.g_kind == kOutF16) ? 2 : 4);
+  const int gesz = (e.g_kind == kOutBF16 || e.g_kind == kOutF16) ? 2 : 4;
+  for (unsigned align : {32u, 16u}) {
+    const bool all = ok(e.c, e.ldc, 4, align) && ok(e.cin, e.ldcin, 4, align) && ok(e.bias, 0, 4, align) &&
+                     ok(e.o_hi, e.ldo, oesz, align) && ok(e.o_lo, e.ldo, oesz, align) &&
+                     ok(e.g_out, e.ldg, gesz, align) && ok(e.rope_table, e.head_dim, 4, align);
+    if (all) return align == 32u ? 2 : 1;
+  }
+  return 0;
 }
 
 cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err) {

@@ -294,8 +294,9 @@ TsPlan* get_plan(TimestralEngine& e, TsDevice& dv, int rows, int enc, int h, int
 
 // ---- the forward ----------------------------------------------------------------------------------
 
-cudaError_t gemm(TsDevice& dv, GemmArgs& g, cudaStream_t s) {
-  dv.prof.begin(s, "gemm", 2.0 * g.M * g.N * g.K);  // algorithmic FLOPs (the split mode runs 3 MMAs each)
+// One GEMM launch, timed under `name` ("gemm.<layer>") when profiling.
+cudaError_t gemm(TsDevice& dv, GemmArgs& g, cudaStream_t s, const char* name) {
+  dv.prof.begin(s, name, 2.0 * g.M * g.N * g.K);  // algorithmic FLOPs (the split mode runs 3 MMAs each)
   cudaError_t r = launch_gemm(g, s, dv.err);
   dv.prof.end(s);
   return r;
@@ -329,13 +330,13 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   GemmArgs g = gemm_args(op, p.tok, encT, w.emb_h);
   g.ep.act = kActSilu;
   set_op_out(g.ep, op, p.emb_h);
-  JC_TRY(gemm(dv, g, s));
+  JC_TRY(gemm(dv, g, s, "gemm.embed"));
   g = gemm_args(op, p.emb_h, encT, w.emb_o);
   g.ep.c = p.x;
   g.ep.ldc = d;
   g.ep.rg = E;
   g.ep.rg_stride = n;
-  JC_TRY(gemm(dv, g, s));
+  JC_TRY(gemm(dv, g, s, "gemm.embed"));
   g = gemm_args(op, p.tok, encT, w.emb_r);
   g.ep.c = p.x;
   g.ep.ldc = d;
@@ -344,7 +345,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   g.ep.accumulate = 1;
   g.ep.rg = E;
   g.ep.rg_stride = n;
-  JC_TRY(gemm(dv, g, s));
+  JC_TRY(gemm(dv, g, s, "gemm.embed"));
   prof.begin(s, "fill", 0);
   launch_fill_rows(p.x, d, w.forecast_query, d, R, E, n, s);
   prof.end(s);
@@ -368,7 +369,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       g.ep.g_out = p.gate;
       g.ep.ldg = d;
       g.ep.g_kind = e.qkv_out_kind();
-      JC_TRY(gemm(dv, g, s));
+      JC_TRY(gemm(dv, g, s, "gemm.qkvg"));
       AttnArgs a{};
       a.qkv = p.qkv;
       a.qkv_kind = e.qkv_out_kind();
@@ -403,7 +404,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       g.ep.cin = p.x;
       g.ep.ldcin = d;
       g.ep.accumulate = 1;
-      JC_TRY(gemm(dv, g, s));
+      JC_TRY(gemm(dv, g, s, "gemm.wo"));
     }
     prof.begin(s, "rmsnorm", 0);
     launch_rmsnorm(p.x, d, L.mlp_norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
@@ -411,14 +412,14 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
     g = gemm_args(op, p.hn, T, L.w12);
     g.ep.mode = kEpiSwiGLU;
     set_op_out(g.ep, op, p.act);
-    JC_TRY(gemm(dv, g, s));
+    JC_TRY(gemm(dv, g, s, "gemm.w12"));
     g = gemm_args(op, p.act, T, L.w3);
     g.ep.c = p.x;
     g.ep.ldc = d;
     g.ep.cin = p.x;
     g.ep.ldcin = d;
     g.ep.accumulate = 1;
-    JC_TRY(gemm(dv, g, s));
+    JC_TRY(gemm(dv, g, s, "gemm.w3"));
   }
   // out_norm on the decoder tokens only (the head reads nothing else), gathered per row
   prof.begin(s, "rmsnorm", 0);
@@ -427,19 +428,19 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   g = gemm_args(op, p.dec, decT, w.head_h);
   g.ep.act = kActSilu;
   set_op_out(g.ep, op, p.head_h);
-  JC_TRY(gemm(dv, g, s));
+  JC_TRY(gemm(dv, g, s, "gemm.head"));
   const int pq = e.P * e.Q;
   g = gemm_args(op, p.head_h, decT, w.head_o);
   g.ep.c = p.raw;
   g.ep.ldc = pq;
-  JC_TRY(gemm(dv, g, s));
+  JC_TRY(gemm(dv, g, s, "gemm.head"));
   g = gemm_args(op, p.dec, decT, w.head_r);
   g.ep.c = p.raw;
   g.ep.ldc = pq;
   g.ep.cin = p.raw;
   g.ep.ldcin = pq;
   g.ep.accumulate = 1;
-  JC_TRY(gemm(dv, g, s));
+  JC_TRY(gemm(dv, g, s, "gemm.head"));
 #undef JC_TRY
   return cudaGetLastError();
 }

@@ -103,8 +103,10 @@ def test_eager_equals_graph_and_profile(jc, tiny):
         prof = eng.profile()
     np.testing.assert_array_equal(g1, g2)
     np.testing.assert_array_equal(g1, e1)
-    assert prof["gemm"]["launches"] == 3 + 2 * 5 + 2 * 3 + 3  # embed 3, per attention 2, per MLP 2, head 3
-    assert prof["gemm"]["ms"] > 0 and prof["attention"]["launches"] == 5
+    gemm_launches = sum(v["launches"] for k, v in prof.items() if k.startswith("gemm"))
+    assert gemm_launches == 3 + 2 * 5 + 2 * 3 + 3  # embed 3, per attention 2, per MLP 2, head 3
+    assert prof["gemm.w12"]["launches"] == 3 and prof["gemm.w12"]["ms"] > 0
+    assert prof["attention"]["launches"] == 5
 
 
 def test_bad_checkpoint_is_rejected(jc, tiny):
