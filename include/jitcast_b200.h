@@ -13,6 +13,9 @@
  *   - timestral/BlockForward.java:20-24 and timestral/tornado/TimestralForward.java:187-642
  *       BlockForward.predictBlock's device forward (TimestralForward)   → jc_engine_create_timestral,
  *                                                                          jc_forward_timestral
+ *   - chronos2/ModelForward.java and chronos2/tornado/Chronos2Forward.java:148-494
+ *       ModelForward.forward's device forward (Chronos2Forward)         → jc_engine_create_chronos2,
+ *                                                                          jc_forward_chronos2
  *   - tornado/PlanCache.java:40-162  per-shape plans, CUDA-graph replay → engine plans, jc_engine_set_option
  */
 #ifndef JITCAST_B200_H
@@ -214,6 +217,53 @@ jc_status jc_forward_timestral(jc_engine* engine, const jc_timestral_block* bloc
  */
 jc_status jc_forward_timestral_device(jc_engine* engine, int slot, const jc_timestral_block* block, float* raw_out,
                                       void* stream);
+
+/* The Chronos2Config fields the forward pass uses (chronos2/Chronos2Config.java:45-60). */
+typedef struct jc_chronos2_desc {
+  int d_model;
+  int d_kv;
+  int d_ff;
+  int num_layers;
+  int num_heads;
+  int patch_size;
+  int num_quantiles;
+  int use_reg_token;
+  float layer_norm_eps;
+  float rope_theta;
+} jc_chronos2_desc;
+
+/*
+ * Creates a Chronos-2 engine: binds `weights` by the checkpoint's names and shapes (every tensor once,
+ * as chronos2/Chronos2Weights.java:80-100; unknown, missing or misshapen tensors fail with
+ * JC_ERR_INVALID_ARG) and converts them to `precision` on every GPU in `devices`. Head widths other
+ * than 64 fail with JC_ERR_UNSUPPORTED_SHAPE (as Chronos2Forward.java:126-128 rejects widths).
+ */
+jc_status jc_engine_create_chronos2(const jc_chronos2_desc* desc, const jc_tensor_view* weights, int n_weights,
+                                    const int* devices, int n_devices, jc_precision precision, jc_engine** out);
+
+/* One forward pass's device inputs: what Chronos2Forward.Plan.run uploads
+ * (chronos2/tornado/Chronos2Forward.java:463-489), as ModelLayout and ModelPrep compute them. */
+typedef struct jc_chronos2_block {
+  int rows;
+  int context_patches; /* ModelLayout.contextPatches (nc) */
+  int output_patches;  /* ModelLayout.outputPatches (h) */
+  const float* tokens;        /* [rows · (nc + h) · 3P] ModelPrep.tokens */
+  const int32_t* live;        /* [rows · (nc + reg + h)] ModelLayout.live, 0/1 */
+  const int32_t* group_start; /* [rows] first row of the row's group */
+  const int32_t* group_end;   /* [rows] one past its last row */
+} jc_chronos2_block;
+
+/*
+ * The Chronos-2 encoder on HOST buffers: raw_out [rows · h · Q · P] receives the output patch
+ * embedding's raw values, each token's quantiles level-major (the caller then runs
+ * ModelPrep.finish). Rows are sharded across the engine's GPUs in contiguous ranges that keep each
+ * group on one GPU; rows of one group must be contiguous (JC_ERR_INVALID_ARG otherwise).
+ */
+jc_status jc_forward_chronos2(jc_engine* engine, const jc_chronos2_block* block, float* raw_out);
+
+/* The same on inputs already in HBM of the engine's GPU number `slot`, enqueued on `stream`. */
+jc_status jc_forward_chronos2_device(jc_engine* engine, int slot, const jc_chronos2_block* block, float* raw_out,
+                                     void* stream);
 
 /* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
 jc_status jc_engine_sync(jc_engine* engine);

@@ -45,8 +45,10 @@ __device__ __forceinline__ void put_op(int kind, void* hi, void* lo, long long i
   }
 }
 
-// BlockLayout.timeAllowed for row `row`, query q, key k.
+// BlockLayout.timeAllowed for row `row`, query q, key k (mask mode 0), or key liveness (mode 1,
+// Chronos-2's time attention: every live key in both directions).
 __device__ __forceinline__ bool time_allowed(const AttnArgs& a, int row, int q, int k) {
+  if (a.mask_mode == 1) return a.live[(long long)row * a.n + k] != 0;
   if (q < a.enc) {
     if (k >= a.enc) return false;
     return k == q || (a.key_valid[(long long)row * a.enc + k] && (k <= q || a.known[row]));
@@ -146,7 +148,9 @@ __global__ void variate_attention_kernel(AttnArgs a) {
     float m = -INFINITY, l = 0.0f;
     for (int j = gs; j < ge; ++j) {
       bool ok = true;
-      if (j != i) {
+      if (a.mask_mode == 1) {
+        ok = a.live[(long long)j * a.n + t] != 0;
+      } else if (j != i) {
         if (t < a.enc && !a.key_valid[(long long)j * a.enc + t]) ok = false;
         if (ok && a.covariates) {
           if (a.role[i] != 0 && a.role[j] == 0) ok = false;
@@ -171,7 +175,7 @@ __global__ void variate_attention_kernel(AttnArgs a) {
 #pragma unroll
       for (int e = 0; e < DH; ++e) acc[e] += p * ld_f(vp + e);
     }
-    const float inv = 1.0f / l;
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;  // no live row in the group: zeros
     const long long o = ((long long)i * a.n + t) * a.ld_out + hh * DH;
     const long long go = ((long long)i * a.n + t) * a.ld_gate + hh * DH;
 #pragma unroll
@@ -298,13 +302,18 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
     *reinterpret_cast<uint4*>(ks + r * kPitch + c) = kv;
     *reinterpret_cast<uint4*>(vs + r * kPitch + c) = vv;
   }
-  for (int k = threadIdx.x; k < npad; k += blockDim.x)
-    kvalid[k] = k < a.enc ? a.key_valid[(long long)row * a.enc + k] : 0;
+  for (int k = threadIdx.x; k < npad; k += blockDim.x) {
+    if (a.mask_mode == 1)
+      kvalid[k] = k < n ? a.live[(long long)row * n + k] : 0;
+    else
+      kvalid[k] = k < a.enc ? a.key_valid[(long long)row * a.enc + k] : 0;
+  }
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;  // fragment row group and column pair
-  const bool known = a.known[row] != 0;
+  const bool live_mode = a.mask_mode == 1;
+  const bool known = !live_mode && a.known[row] != 0;
   const float sl2 = a.scale * 1.4426950408889634f;  // softmax in base 2
   const uint32_t ks_base = smem_u32(ks), vs_base = smem_u32(vs);
   const int qtiles = (n + 15) >> 4;
@@ -331,7 +340,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
     float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
     // an all-encoder tile on a row that is not a known covariate reads no key past its last query
     int kend = npad;
-    if (q0 + 15 < a.enc && !known) kend = min(npad, ((q0 + 15) / 64 + 1) * 64);
+    if (!live_mode && q0 + 15 < a.enc && !known) kend = min(npad, ((q0 + 15) / 64 + 1) * 64);
     for (int k0 = 0; k0 < kend; k0 += 64) {
       float sc[8][4];
 #pragma unroll
@@ -359,7 +368,9 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
           for (int c = 0; c < 2; ++c) {
             const int k = k0 + j * 8 + tq * 2 + c;
             bool ok;
-            if (q < a.enc) {
+            if (live_mode) {
+              ok = kvalid[k] != 0;
+            } else if (q < a.enc) {
               ok = k < a.enc && (k == q || (kvalid[k] && (k <= q || known)));
             } else {
               ok = k < a.enc ? (k < a.ll && kvalid[k]) : (k <= q && k < n);

@@ -26,6 +26,11 @@ struct AttnArgs {
   const int* group_start;
   const int* group_end;
   int covariates;
+  // 0: the Timestral block layout (key_valid, known, enc, ll; variate rows always read themselves);
+  // 1: per-token liveness (live [rows·n]): every live key of the row in time attention, the live
+  //    rows of the group in group attention, zeros when a group has none (Chronos-2's ModelLayout).
+  int mask_mode;
+  const int* live;
 };
 
 cudaError_t launch_time_attention(const AttnArgs& a, cudaStream_t s);

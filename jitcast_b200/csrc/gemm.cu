@@ -264,7 +264,8 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
                                               int row_in_tile, int half) {
   const int row = m0 + row_in_tile;
   const bool live = row < M;
-  const int orow = live ? (row / p.rg) * p.rg_stride + row % p.rg + p.rg_off : 0;
+  const int rr = row % p.rg;
+  const int orow = live ? (row / p.rg) * p.rg_stride + rr + p.rg_off + (rr >= p.rg_split ? p.rg_shift : 0) : 0;
   float sq = 0.0f;
   if (p.mode == kEpiPlain || (p.mode == kEpiQKV && n0 >= p.n_split)) {
     const bool gate = p.mode == kEpiQKV;
@@ -577,6 +578,8 @@ EpiParams epi_default() {
   p.rg = 1 << 30;
   p.rg_stride = 1 << 30;
   p.rg_off = 0;
+  p.rg_split = 1 << 30;
+  p.rg_shift = 0;
   p.vec_ok = 0;
   return p;
 }

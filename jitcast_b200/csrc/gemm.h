@@ -61,8 +61,9 @@ struct EpiParams {
   void* o_lo;
   long long ldo;
   int o_kind;
-  // Row remap of the outputs: out_row = (r / rg) * rg_stride + r % rg + rg_off.
-  int rg, rg_stride, rg_off;
+  // Row remap of the outputs: out_row = (r / rg) * rg_stride + r % rg + rg_off, plus rg_shift when
+  // r % rg >= rg_split (places embedded tokens around inserted ones, e.g. a [REG] token).
+  int rg, rg_stride, rg_off, rg_split, rg_shift;
   // kEpiQKV
   int rope_cols, head_dim;
   const int* pos;           // [M] index into rope_table rows

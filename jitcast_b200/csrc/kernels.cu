@@ -57,16 +57,16 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const
   }
 }
 
-__global__ void fill_rows_kernel(float* x, long long ldx, const float* __restrict__ q, int cols, int rows, int enc,
-                                 int n) {
-  const int h = n - enc;
+__global__ void fill_rows_kernel(float* x, long long ldx, const float* __restrict__ q, int cols, int rows, int t0,
+                                 int t1, int n) {
+  const int h = t1 - t0;
   const long long total = (long long)rows * h * cols;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const int c = static_cast<int>(i % cols);
     const long long t = i / cols;
     const long long r = t / h;
-    const int tok = enc + static_cast<int>(t % h);
+    const int tok = t0 + static_cast<int>(t % h);
     x[(r * n + tok) * ldx + c] = q[c];
   }
 }
@@ -100,10 +100,11 @@ void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, flo
                                                           gather_rows, gather_stride, gather_off);
 }
 
-void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int enc, int n, cudaStream_t s) {
-  const long long total = (long long)rows * (n - enc) * cols;
+void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int t0, int t1, int n,
+                      cudaStream_t s) {
+  const long long total = (long long)rows * (t1 - t0) * cols;
   if (total <= 0) return;
-  fill_rows_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, ldx, q, cols, rows, enc, n);
+  fill_rows_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, ldx, q, cols, rows, t0, t1, n);
 }
 
 void launch_add_i32(const int* in, int* out, long long n, int add, cudaStream_t s) {

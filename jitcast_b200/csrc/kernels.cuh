@@ -21,8 +21,9 @@ void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, flo
                     void* y_lo, long long ldy, long long rows, int gather_rows, int gather_stride, int gather_off,
                     cudaStream_t s);
 
-// x[(r·n + t), :] = q for every row r and decoder token t in [enc, n).
-void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int enc, int n, cudaStream_t s);
+// x[(r·n + t), :] = q for every row r and token t in [t0, t1) (the decoder tokens, a [REG] token).
+void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int t0, int t1, int n,
+                      cudaStream_t s);
 
 // out[i] = in[i] + add for i < n (integer index rebasing on the device).
 void launch_add_i32(const int* in, int* out, long long n, int add, cudaStream_t s);

@@ -347,7 +347,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   g.ep.rg_stride = n;
   JC_TRY(gemm(dv, g, s, "gemm.embed"));
   prof.begin(s, "fill", 0);
-  launch_fill_rows(p.x, d, w.forecast_query, d, R, E, n, s);
+  launch_fill_rows(p.x, d, w.forecast_query, d, R, E, n, n, s);
   prof.end(s);
 
   const int out_kind = out_of_op(op);

@@ -1,0 +1,118 @@
+"""The Chronos-2 forward on a B200 through the C ABI, against the C restatement of the reference's
+FP32 CPU forward (CpuChronos2.forward) on the same seeded inputs and random-init weights.
+
+Inputs follow the reference's batch-parity test (Chronos2BatchParityAccelTest.java:45-114: random walks
+plus a daily sinusoid, NaN gaps, late starts, multi-row groups with known future covariates); the
+error is max|a − e| / max|e| on every quantile level. Bars: FP32 1e-4 (the reference's FP32 device
+bar), TF32 2e-3, BF16 and FP16 1e-2; on config 2 (12 random-init layers) FP32 is held to BASELINE's
+1e-3, FP16 to 1e-2, TF32 to 4e-3 and BF16 to 4e-2 (its 8-bit mantissa, as for Timestral).
+"""
+
+import numpy as np
+import pytest
+
+from jitcast_b200 import chronos2 as c2
+from jitcast_b200 import workloads
+from oracle import chronos2 as oc2
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-4, "tf32": 2e-3, "bf16": 1e-2, "fp16": 1e-2}
+TOL_CONFIG2 = {"fp32": 1e-3, "tf32": 4e-3, "bf16": 4e-2, "fp16": 1e-2}
+
+
+def per_quantile_err(actual, expected):
+    """Out is [rows, Q, h·P]: the error of each quantile level relative to that level's largest value."""
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    assert not np.isnan(a).any()
+    return max(np.abs(a[:, k] - e[:, k]).max() / max(np.abs(e[:, k]).max(), 1e-6) for k in range(e.shape[1]))
+
+
+def tiny_config(**kw):
+    base = dict(d_model=128, d_kv=64, d_ff=256, num_layers=2, num_heads=2, quantiles=[0.1, 0.5, 0.9],
+                context_length=256, patch_size=16, max_output_patches=2)
+    base.update(kw)
+    return c2.Chronos2Config(**base).validate()
+
+
+def mixed_input(c, series=7, length=300, h=2, covariate_groups=2, seed=11, shuffle=False):
+    x, obs, group, _ = workloads.mixed_batch(series, length, c.patch_size, seed=seed, covariate_groups=covariate_groups)
+    ctx = np.where(obs, x, np.nan).astype(np.float32)
+    fut = None
+    if covariate_groups:
+        rng = np.random.default_rng(seed + 1)
+        fut = np.full((x.shape[0], h * c.patch_size - 3), np.nan, np.float32)
+        sel = group < covariate_groups
+        fut[sel] = rng.standard_normal((int(sel.sum()), fut.shape[1]))
+    if shuffle:  # rows of a group need not be adjacent in the caller's order
+        perm = np.random.default_rng(seed + 2).permutation(len(group))
+        ctx, group = ctx[perm], group[perm]
+        fut = None if fut is None else fut[perm]
+    return c2.ModelInput(ctx, group, h, fut)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    c = tiny_config()
+    w = c2.random_checkpoint(c, seed=4)
+    return c, w, oc2.Model(c, w)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
+@pytest.mark.parametrize("covariate_groups,shuffle", [(0, False), (2, True)])
+def test_tiny_model_matches_oracle(jc, tiny, precision, covariate_groups, shuffle):
+    c, w, model = tiny
+    inp = mixed_input(c, covariate_groups=covariate_groups, shuffle=shuffle)
+    exp, _ = model.forward(inp)
+    with c2.Chronos2Engine(c, w, precision=precision) as eng:
+        fwd = c2.B200Chronos2Forward(eng)
+        got = fwd.forward(inp)
+        got2 = fwd.forward(inp)  # graph replay
+    assert got.shape == exp.shape
+    err = per_quantile_err(got, exp)
+    assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+    np.testing.assert_array_equal(got, got2)
+
+
+def test_without_reg_token(jc):
+    c = tiny_config(use_reg_token=False)
+    w = c2.random_checkpoint(c, seed=6)
+    inp = mixed_input(c, covariate_groups=1, length=200)
+    exp, _ = oc2.Model(c, w).forward(inp)
+    with c2.Chronos2Engine(c, w, precision="fp32") as eng:
+        got = c2.B200Chronos2Forward(eng).forward(inp)
+    assert per_quantile_err(got, exp) < TOL["fp32"]
+
+
+def test_sharded_two_slots(jc, tiny):
+    c, w, _ = tiny
+    inp = mixed_input(c, series=9, covariate_groups=3)
+    with c2.Chronos2Engine(c, w, devices=(0,), precision="fp32") as one, \
+            c2.Chronos2Engine(c, w, devices=(0, 0), precision="fp32") as two:
+        a = c2.B200Chronos2Forward(one).forward(inp)
+        b = c2.B200Chronos2Forward(two).forward(inp)
+    np.testing.assert_allclose(a, b, rtol=1e-6, atol=1e-6)
+
+
+@pytest.fixture(scope="module")
+def config2_case():
+    """BASELINE config 2 (d 768, 12 layers, 128 context patches + [REG] + 4 future, 21 quantiles) on a few
+    random-walk series, with the oracle's outputs."""
+    c = c2.config2()
+    w = c2.random_checkpoint(c, seed=0)
+    series = 2
+    x = workloads.random_walk(series, 2048, seed=0)
+    inp = c2.ModelInput(x, np.arange(series, dtype=np.int32), 4)
+    exp, _ = oc2.Model(c, w).forward(inp)
+    return c, w, inp, exp
+
+
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
+def test_config2_full_size_matches_oracle(jc, config2_case, precision):
+    c, w, inp, exp = config2_case
+    with c2.Chronos2Engine(c, w, precision=precision) as eng:
+        got = c2.B200Chronos2Forward(eng).forward(inp)
+    err = per_quantile_err(got, exp)
+    print(f"config2 {precision}: per-quantile rel max err {err:.3e}")
+    assert err < TOL_CONFIG2[precision], f"{precision}: per-quantile rel max err {err:.3e}"
