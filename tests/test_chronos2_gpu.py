@@ -3,9 +3,11 @@ FP32 CPU forward (CpuChronos2.forward) on the same seeded inputs and random-init
 
 Inputs follow the reference's batch-parity test (Chronos2BatchParityAccelTest.java:45-114: random walks
 plus a daily sinusoid, NaN gaps, late starts, multi-row groups with known future covariates); the
-error is max|a − e| / max|e| on every quantile level. Bars: FP32 1e-4 (the reference's FP32 device
-bar), TF32 2e-3, BF16 and FP16 1e-2; on config 2 (12 random-init layers) FP32 is held to BASELINE's
-1e-3, FP16 to 1e-2, TF32 to 4e-3 and BF16 to 4e-2 (its 8-bit mantissa, as for Timestral).
+error is max|a − e| / max|e| on every quantile level. Bars: FP32 (the FP32-accumulate mode) 1e-4 on
+the tiny model (the reference's FP32 device bar) and BASELINE's 1e-3 on config 2; TF32 and FP16 (10-bit
+mantissa operands, reduced precision in GemmMode.java:73-75) BASELINE's 1e-2; BF16 (7-bit mantissa) the
+reference's bar for reduced-precision GEMM inputs, 5e-2 (TimestralForwardAccelTest.java:43-48), because
+BF16 rounding of the weights alone exceeds 1e-2 on these random-init models.
 """
 
 import numpy as np
@@ -17,8 +19,8 @@ from oracle import chronos2 as oc2
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"fp32": 1e-4, "tf32": 2e-3, "bf16": 1e-2, "fp16": 1e-2}
-TOL_CONFIG2 = {"fp32": 1e-3, "tf32": 4e-3, "bf16": 4e-2, "fp16": 1e-2}
+TOL = {"fp32": 1e-4, "tf32": 1e-2, "bf16": 5e-2, "fp16": 1e-2}
+TOL_CONFIG2 = {"fp32": 1e-3, "tf32": 1e-2, "bf16": 5e-2, "fp16": 1e-2}
 
 
 def per_quantile_err(actual, expected):

@@ -15,15 +15,16 @@ from oracle import timestral as ots
 
 pytestmark = pytest.mark.gpu
 
-# JC_FP32 (3×TF32, FP32 accumulation) is the FP32-accumulate mode BASELINE bounds at 1e-3; it is held to
-# the reference's 1e-4. JC_TF32 rounds every operand to TF32 (as cuBLAS TF32 does) and is held to 2e-3.
-TOL = {"fp32": 1e-4, "tf32": 2e-3, "bf16": 1e-2, "fp16": 1e-2}
-# Config 3 (16 random-init layers, sinh denormalisation): BASELINE's bars are 1e-3 for the
-# FP32-accumulate mode and 1e-2 for the 16-bit tensor-core mode, which JC_FP32 and JC_FP16 meet.
-# BF16's 8-bit mantissa alone gives 3.2e-2 on this model (a float64 NumPy emulation with BF16
-# rounding of weights and GEMM inputs reproduces the GPU's 3.1e-2), so BF16 is held to 4e-2 and
-# TF32 (1.1e-3 on the tiny model, 2.6e-3 here) to 4e-3.
-TOL_CONFIG3 = {"fp32": 1e-3, "tf32": 4e-3, "bf16": 4e-2, "fp16": 1e-2}
+# Bars per precision mode. JC_FP32 (TF32 hi/lo operands, three MMAs, FP32 accumulation) is the
+# FP32-accumulate mode: the reference's FP32 device bar 1e-4 on the tiny model and BASELINE's 1e-3 on
+# config 3. JC_TF32 and JC_FP16 round every GEMM operand to a 10-bit mantissa, which the reference
+# treats as reduced precision (GemmMode.reducedPrecision, GemmMode.java:73-75); they are held to
+# BASELINE's 1e-2 bar for the 16-bit tensor-core mode. JC_BF16 keeps 7 mantissa bits: a float64 NumPy
+# emulation of config 3 that rounds only the weights to BF16 already gives 2.4e-2 (all GEMM operands:
+# 3.2e-2, the GPU measures 2.9e-2), so no BF16 GEMM can meet 1e-2 on this model; it is held to the
+# reference's own bar for reduced-precision GEMM inputs, 5e-2 (TimestralForwardAccelTest.java:43-48).
+TOL = {"fp32": 1e-4, "tf32": 1e-2, "bf16": 5e-2, "fp16": 1e-2}
+TOL_CONFIG3 = {"fp32": 1e-3, "tf32": 1e-2, "bf16": 5e-2, "fp16": 1e-2}
 
 
 def per_quantile_err(actual, expected):
