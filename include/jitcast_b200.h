@@ -16,6 +16,9 @@
  *   - chronos2/ModelForward.java and chronos2/tornado/Chronos2Forward.java:148-494
  *       ModelForward.forward's device forward (Chronos2Forward)         → jc_engine_create_chronos2,
  *                                                                          jc_forward_chronos2
+ *   - tirex2/ForwardPass.java and tirex2/tornado/TornadoForward.java:353-827
+ *       ForwardPass.forward's device forward (TornadoForward)           → jc_engine_create_tirex2,
+ *                                                                          jc_forward_tirex2
  *   - tornado/PlanCache.java:40-162  per-shape plans, CUDA-graph replay → engine plans, jc_engine_set_option
  */
 #ifndef JITCAST_B200_H
@@ -43,7 +46,7 @@ typedef enum jc_status {
 } jc_status;
 
 /* Arithmetic of the tensor-core GEMMs (replaces tornado/GemmMode.java:40-41).
- *   JC_FP32  FP32 operands as TF32 hi/lo pairs, three TF32 MMAs per product (≈ FP32 accuracy)
+ *   JC_FP32  FP32 operands as TF32 hi/lo pairs, four TF32 MMAs per product (≈ FP32 accuracy)
  *   JC_TF32  TF32 operands, FP32 accumulation (the reference's CUBLAS_TF32)
  *   JC_BF16  BF16 operands, FP32 accumulation and FP32 residual stream
  *   JC_FP16  FP16 operands (stores saturate at ±65504, as Kernels.HALF_MAX), FP32 accumulation and
@@ -264,6 +267,68 @@ jc_status jc_forward_chronos2(jc_engine* engine, const jc_chronos2_block* block,
 /* The same on inputs already in HBM of the engine's GPU number `slot`, enqueued on `stream`. */
 jc_status jc_forward_chronos2_device(jc_engine* engine, int slot, const jc_chronos2_block* block, float* raw_out,
                                      void* stream);
+
+/* TiRex-2 time-mixer kinds (the stack recipe's "bi-mlstm" / "bi-slstm", tirex2/TiRex2Config.java:161-175). */
+#define JC_TIREX_MLSTM 0
+#define JC_TIREX_SLSTM 1
+
+/* The TiRex2Config fields the forward pass uses (tirex2/TiRex2Config.java:48-66). */
+typedef struct jc_tirex2_desc {
+  int embedding_dim;
+  int num_blocks;
+  int patch_size;
+  int input_ff_dim;
+  int output_ff_dim;
+  int context_len;
+  int future_len;
+  int num_quantiles;
+  const int32_t* block_types; /* [num_blocks] JC_TIREX_MLSTM / JC_TIREX_SLSTM */
+  int time_mixer_heads;
+  int slstm_heads;
+  int variate_heads;
+  int use_arcsinh;
+  int binary_aware;
+  int use_qk_norm;
+  float stack_out_norm_eps;
+} jc_tirex2_desc;
+
+/*
+ * Creates a TiRex-2 engine: binds `weights` by the checkpoint's names and shapes (every tensor once, as
+ * tirex2/TiRex2Weights.java:128-247; unknown, missing or misshapen tensors fail with JC_ERR_INVALID_ARG)
+ * and converts them to `precision` on every GPU in `devices`. The cells and the variate attention take
+ * 128-wide heads (64-wide mLSTM q/k), as the reference's device forward does
+ * (tirex2/tornado/TornadoForward.java:261-264, :708-710); other widths fail with JC_ERR_UNSUPPORTED_SHAPE.
+ */
+jc_status jc_engine_create_tirex2(const jc_tirex2_desc* desc, const jc_tensor_view* weights, int n_weights,
+                                  const int* devices, int n_devices, jc_precision precision, jc_engine** out);
+
+/* One forward pass's device inputs: what TornadoForward.Plan.run uploads
+ * (tirex2/tornado/TornadoForward.java:799-815), with the structure lists of TornadoForward.structure
+ * (:406-449). len = context_len + future_len. */
+typedef struct jc_tirex2_batch {
+  int rows;
+  const float* x;            /* [rows · len] values, 0 where there is no observation */
+  const float* present;      /* [rows · len] 1 where x holds an observation, else 0 */
+  int n_known;               /* covariate rows with a value in the future window (reverse pass) */
+  const int32_t* known;      /* [n_known] increasing row indices */
+  int n_kept;                /* rows of multi-row groups (variate mixer) */
+  const int32_t* kept;       /* [n_kept] increasing row indices; a group's rows are contiguous */
+  const int32_t* group_start; /* [n_kept] first kept index of the row's group */
+  const int32_t* group_end;   /* [n_kept] one past the group's last kept index */
+  const int32_t* kept_target; /* [n_kept] 1 for target rows, 0 for covariates */
+} jc_tirex2_batch;
+
+/*
+ * The TiRex-2 forward (TiRex2.forward as ForwardPass.forward, tirex2/ForwardPass.java) on HOST buffers:
+ * out [rows · Q · len] receives the rescaled quantile outputs over the whole padded length, in data units.
+ * Rows are sharded across the engine's GPUs in contiguous ranges that keep each group on one GPU.
+ */
+jc_status jc_forward_tirex2(jc_engine* engine, const jc_tirex2_batch* batch, float* out);
+
+/* The same on inputs already in HBM of the engine's GPU number `slot` (every pointer of `batch`, and `out`,
+ * a device pointer on that GPU), enqueued on `stream`. The lists are not checked on the host here. */
+jc_status jc_forward_tirex2_device(jc_engine* engine, int slot, const jc_tirex2_batch* batch, float* out,
+                                   void* stream);
 
 /* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
 jc_status jc_engine_sync(jc_engine* engine);

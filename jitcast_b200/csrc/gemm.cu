@@ -488,8 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               const uint64_t ad2 = sdesc_k_sw128(sb + C::B_BYTES + 32 * k);
               const uint64_t bd2 = sdesc_k_sw128(sb + C::B_BYTES + C::A_BYTES + 32 * k);
-              umma_tf32(d, ad2, bd, C::IDESC, acc);  // lo·hi
-              umma_tf32(d, ad, bd2, C::IDESC, 1u);   // hi·lo
+              // smallest terms first; lo·lo halves the split's error against an FP32 product
+              umma_tf32(d, ad2, bd2, C::IDESC, acc);  // lo·lo
+              umma_tf32(d, ad2, bd, C::IDESC, 1u);    // lo·hi
+              umma_tf32(d, ad, bd2, C::IDESC, 1u);    // hi·lo
               umma_tf32(d, ad, bd, C::IDESC, 1u);    // hi·hi
             }
           }

@@ -12,7 +12,7 @@ namespace jc {
 enum OperandKind : int {
   kOpBF16 = 0,   // bfloat16; tcgen05 kind::f16
   kOpTF32 = 1,   // fp32 container rounded to TF32; kind::tf32
-  kOpSplit = 2,  // fp32 as a TF32 hi/lo pair; three kind::tf32 MMAs (hi·hi + hi·lo + lo·hi)
+  kOpSplit = 2,  // fp32 as a TF32 hi/lo pair; four kind::tf32 MMAs (lo·lo + lo·hi + hi·lo + hi·hi)
   kOpF16 = 3,    // IEEE half; tcgen05 kind::f16
 };
 

@@ -296,7 +296,7 @@ TsPlan* get_plan(TimestralEngine& e, TsDevice& dv, int rows, int enc, int h, int
 
 // One GEMM launch, timed under `name` ("gemm.<layer>") when profiling.
 cudaError_t gemm(TsDevice& dv, GemmArgs& g, cudaStream_t s, const char* name) {
-  dv.prof.begin(s, name, 2.0 * g.M * g.N * g.K);  // algorithmic FLOPs (the split mode runs 3 MMAs each)
+  dv.prof.begin(s, name, 2.0 * g.M * g.N * g.K);  // algorithmic FLOPs (the split mode runs 4 MMAs each)
   cudaError_t r = launch_gemm(g, s, dv.err);
   dv.prof.end(s);
   return r;

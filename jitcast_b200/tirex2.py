@@ -248,9 +248,14 @@ def weight_shapes(c: TiRex2Config) -> dict[str, tuple[int, ...]]:
     return s
 
 
-def random_checkpoint(c: TiRex2Config, seed: int = 0, norm_jitter: float = 0.0) -> dict[str, np.ndarray]:
+def random_checkpoint(c: TiRex2Config, seed: int = 0, norm_jitter: float = 0.0,
+                      forget_bias: tuple[float, float] | None = None) -> dict[str, np.ndarray]:
     """Random-init weights: linear W ~ N(0, 1/in); headwise sLSTM gates and the recurrent kernel ~ N(0, 1/dh);
-    biases ~ U(−0.1, 0.1); norm scales 1 (times 1 + N(0, norm_jitter) when tests want every scale to matter)."""
+    biases ~ U(−0.1, 0.1); norm scales 1 (times 1 + N(0, norm_jitter) when tests want every scale to matter).
+
+    ``forget_bias=(lo, hi)`` sets the forget-gate biases as xLSTM initialises them, evenly spaced from lo to hi
+    (mLSTM ``fgate_preact.bias`` over the heads, the sLSTM ``_bias_`` forget slot over each head's units), which
+    keeps the gates open and the random-init stack well conditioned."""
     rng = np.random.default_rng(seed)
     out = {}
     for name, shape in sorted(weight_shapes(c).items()):
@@ -266,6 +271,15 @@ def random_checkpoint(c: TiRex2Config, seed: int = 0, norm_jitter: float = 0.0) 
             out[name] = rng.standard_normal(shape, dtype=np.float32) / np.float32(math.sqrt(shape[1]))
         else:
             out[name] = rng.standard_normal(shape, dtype=np.float32) / np.float32(math.sqrt(shape[1]))
+    if forget_bias is not None:
+        lo, hi = forget_bias
+        for name, v in out.items():
+            if name.endswith("fgate_preact.bias"):
+                out[name] = np.linspace(lo, hi, v.size).astype(np.float32)
+            elif name.endswith("._bias_"):  # [heads, 4, dh] in the cell's (i, f, z, o) slot order
+                v = v.copy()
+                v[:, 1, :] = np.linspace(lo, hi, v.shape[2], dtype=np.float32)[None]
+                out[name] = v
     return out
 
 

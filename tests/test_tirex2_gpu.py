@@ -1,0 +1,206 @@
+"""The TiRex-2 forward on a B200 through the C ABI, against the C restatement of the reference's FP32
+CPU forward (CpuReference.forward) on the same seeded inputs and random-init weights.
+
+The tiny model has every path the reference's forward has (TornadoForwardAccelTest.java and
+KernelParityAccelTest.java cover the same): mLSTM and sLSTM blocks, a known covariate with the reverse pass
+and the combination, a multi-row group through the variate mixer (qk-norm, covariates not seeing targets),
+a binary series, NaN gaps and a late start. The error is max|a − e| / max|e| on every quantile level.
+Bars: FP32 (FP32-accumulate mode) BASELINE's 1e-3; TF32 and FP16 (10-bit mantissa operands) 1e-2; BF16 the
+reference's reduced-precision bar 5e-2 (TimestralForwardAccelTest.java:43-48).
+
+Random-init xLSTM stacks can be chaotic: on BASELINE config 4 (seed 0) the oracle ITSELF moves by 0.2 when its
+weights are rounded to TF32 and by 0.57 when rounded to BF16, and exact FP32 arithmetic that only accumulates
+differently moves it too (the oracle's GEMMs accumulated in FP32 with round-to-nearest: 3.5e-5; with the
+truncating accumulation of tensor cores: 2.5e-3). So on that instance:
+  * the reduced-precision bar follows the reference's own rule for its reduced-precision device path
+    (TornadoForwardAccelTest.java:39-44, GoldenData.nxaiGpuError: no further from the FP32 reference than a
+    reduced-precision run of the reference arithmetic is): 1.5 × the oracle's own deviation with its weights
+    rounded to the mode's operand format, or the absolute bar if that is larger;
+  * the FP32 bar is 3e-3, above the largest FP32-arithmetic deviation measured.
+The same config-4 shapes with xLSTM's forget-gate bias initialisation (well conditioned) keep BASELINE's 1e-3 FP32
+bar, and the tiny model (seed 11, well conditioned) keeps every absolute bar.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from jitcast_b200 import _lib
+from jitcast_b200 import tirex2 as tx
+from jitcast_b200 import workloads
+from oracle import tirex2 as otx
+from test_tirex2_oracle import mixed_batch, tiny_config
+
+pytestmark = pytest.mark.gpu
+
+TOL = {"fp32": 1e-3, "tf32": 1e-2, "bf16": 5e-2, "fp16": 1e-2}
+
+
+def round_operands(w, precision):
+    """The checkpoint with every tensor rounded (to nearest even) to the mode's GEMM operand format."""
+    if precision == "fp16":
+        return {k: v.astype(np.float16).astype(np.float32) for k, v in w.items()}
+    bits = {"tf32": 10, "bf16": 7}[precision]
+    sh = 23 - bits
+    out = {}
+    for k, v in w.items():
+        u = np.ascontiguousarray(v, np.float32).view(np.uint32).astype(np.uint64)
+        u = (u + (1 << (sh - 1)) - 1 + ((u >> sh) & 1)) >> sh << sh
+        out[k] = u.astype(np.uint32).view(np.float32)
+    return out
+
+
+def per_quantile_err(actual, expected):
+    """Out is [rows, Q, len]: the error of each quantile level relative to that level's largest value."""
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    assert not np.isnan(a).any()
+    return max(np.abs(a[:, k] - e[:, k]).max() / max(np.abs(e[:, k]).max(), 1e-6) for k in range(e.shape[1]))
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    c = tiny_config()
+    w = tx.random_checkpoint(c, seed=11, norm_jitter=0.1)
+    return c, w, otx.Model(c, w)
+
+
+def univariate_batch(c, rows=4, seed=5):
+    x = workloads.ar2(rows, c.padded_length, seed=seed)
+    x[:, c.context_len:] = np.nan
+    return tx.ModelBatch(x, np.arange(rows, dtype=np.float32), np.ones(rows, bool))
+
+
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
+@pytest.mark.parametrize("mixed", [False, True])
+def test_tiny_model_matches_oracle(jc, tiny, precision, mixed):
+    c, w, model = tiny
+    b = mixed_batch(c) if mixed else univariate_batch(c)
+    exp = model.forward(b)
+    with tx.TiRex2Engine(c, w, precision=precision) as eng:
+        fwd = tx.B200TiRex2Forward(eng)
+        got = fwd.forward(b)
+        got2 = fwd.forward(b)  # second call replays the captured CUDA graph
+    assert got.shape == exp.shape
+    err = per_quantile_err(got, exp)
+    print(f"tirex2 tiny mixed={mixed} {precision}: per-quantile rel max err {err:.3e}")
+    assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+    np.testing.assert_array_equal(got, got2)
+
+
+def test_qk_norm_off(jc):
+    c = tiny_config(use_qk_norm=False, recipe=[tx.SLSTM, tx.MLSTM, tx.SLSTM])
+    w = tx.random_checkpoint(c, seed=9, norm_jitter=0.1)
+    b = mixed_batch(c, seed=4)
+    exp = otx.Model(c, w).forward(b)
+    with tx.TiRex2Engine(c, w, precision="fp32") as eng:
+        got = tx.B200TiRex2Forward(eng).forward(b)
+    assert per_quantile_err(got, exp) < TOL["fp32"]
+
+
+def test_sharded_two_slots_matches_one(jc, tiny):
+    # two engine slots on one GPU exercise the shard/gather path of multi-GPU runs, groups kept whole
+    c, w, _ = tiny
+    b1, b2 = mixed_batch(c, seed=3), mixed_batch(c, seed=8)
+    b = tx.ModelBatch(np.concatenate([b1.x, b2.x]), np.concatenate([b1.group, b2.group + 10]),
+                      np.concatenate([b1.target, b2.target]))
+    with tx.TiRex2Engine(c, w, devices=(0,), precision="fp32") as one, \
+            tx.TiRex2Engine(c, w, devices=(0, 0), precision="fp32") as two:
+        a = tx.B200TiRex2Forward(one).forward(b)
+        bb = tx.B200TiRex2Forward(two).forward(b)
+    np.testing.assert_allclose(a, bb, rtol=1e-6, atol=1e-6)
+
+
+def test_eager_equals_graph_and_profile(jc, tiny):
+    c, w, _ = tiny
+    b = mixed_batch(c)
+    with tx.TiRex2Engine(c, w, precision="bf16") as eng:
+        fwd = tx.B200TiRex2Forward(eng)
+        g1 = fwd.forward(b)
+        eng.set_option("cuda_graph", 0)
+        e1 = fwd.forward(b)
+        eng.set_option("profile", 1)
+        fwd.forward(b)
+        prof = eng.profile()
+    np.testing.assert_array_equal(g1, e1)
+    assert prof["mlstm"]["launches"] == 2 * 2  # 2 mLSTM blocks, forward and reverse pass
+    assert prof["slstm"]["launches"] == 2
+    assert prof["variate"]["launches"] == 3
+    assert prof["gemm.w12"]["launches"] == 3
+
+
+def test_device_entry_point_matches_host(jc, tiny):
+    torch = pytest.importorskip("torch")
+    c, w, _ = tiny
+    b = mixed_batch(c)
+    with tx.TiRex2Engine(c, w, precision="fp16") as eng:
+        host = tx.B200TiRex2Forward(eng).forward(b)
+        di = tx.DeviceInputs.of(c, b)
+        dev = torch.device("cuda", 0)
+        t = {k: torch.from_numpy(np.ascontiguousarray(v)).to(dev) for k, v in
+             dict(x=di.x, present=di.present, known=di.st.known, kept=di.st.kept, gs=di.st.group_start,
+                  ge=di.st.group_end, kt=di.st.kept_target).items()}
+        out = torch.empty(b.rows, c.num_quantiles, c.padded_length, device=dev)
+        blk = tx.Batch(b.rows, t["x"].data_ptr(), t["present"].data_ptr(), len(di.st.known), t["known"].data_ptr(),
+                       len(di.st.kept), t["kept"].data_ptr(), t["gs"].data_ptr(), t["ge"].data_ptr(),
+                       t["kt"].data_ptr())
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(_lib.lib().jc_forward_tirex2_device(eng.handle, 0, ctypes.byref(blk), out.data_ptr(),
+                                                       ctypes.c_void_p(stream.cuda_stream)))
+        eng.sync()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), host)
+
+
+def test_bad_checkpoint_and_shapes_are_rejected(jc, tiny):
+    c, w, _ = tiny
+    w2 = dict(w)
+    del w2["stack_out_norm.weight"]
+    with pytest.raises(jc.JcArgumentError, match="no tensor"):
+        tx.TiRex2Engine(c, w2)
+    w3 = dict(w)
+    w3["stack.0.time_mixer.norm_lstm.weight"] = np.ones(7, np.float32)
+    with pytest.raises(jc.JcArgumentError, match="shape"):
+        tx.TiRex2Engine(c, w3)
+    c64 = tiny_config(embedding_dim=256, time_mixer_heads=4, slstm_heads=4, variate_heads=4)
+    with pytest.raises(jc.JcArgumentError, match="head widths"):
+        tx.TiRex2Engine(c64, tx.random_checkpoint(c64, seed=1))
+
+
+@pytest.fixture(scope="module")
+def config4_case():
+    """BASELINE config 4 (d 512, 12 blocks with sLSTM at 3, 7, 11, 64 patches, 9 quantiles) on a few AR(2)
+    series, future window unobserved, with the oracle's outputs."""
+    c = tx.config4()
+    w = tx.random_checkpoint(c, seed=0)
+    b = univariate_batch(c, rows=3, seed=0)
+    return c, w, b, otx.Model(c, w).forward(b)
+
+
+@pytest.mark.parametrize("precision", ["fp32", "tf32", "bf16", "fp16"])
+def test_config4_full_size_matches_oracle(jc, config4_case, precision):
+    c, w, b, exp = config4_case
+    bar = 3e-3  # FP32 on this chaotic instance (module docstring)
+    if precision != "fp32":
+        floor = per_quantile_err(otx.Model(c, round_operands(w, precision)).forward(b), exp)
+        bar = max(TOL[precision], 1.5 * floor)
+        print(f"config4 {precision}: oracle with rounded weights moves {floor:.3e}")
+    with tx.TiRex2Engine(c, w, precision=precision) as eng:
+        got = tx.B200TiRex2Forward(eng).forward(b)
+    err = per_quantile_err(got, exp)
+    print(f"config4 {precision}: per-quantile rel max err {err:.3e} (bar {bar:.3e})")
+    assert err < bar, f"{precision}: per-quantile rel max err {err:.3e} (bar {bar:.3e})"
+
+
+def test_config4_conditioned_fp32_within_baseline_bar(jc):
+    """Config-4 shapes and inputs, forget-gate biases initialised as xLSTM does (3 … 6): FP32 within 1e-3."""
+    c = tx.config4()
+    w = tx.random_checkpoint(c, seed=0, forget_bias=(3.0, 6.0))
+    b = univariate_batch(c, rows=3, seed=0)
+    exp = otx.Model(c, w).forward(b)
+    with tx.TiRex2Engine(c, w, precision="fp32") as eng:
+        got = tx.B200TiRex2Forward(eng).forward(b)
+    err = per_quantile_err(got, exp)
+    print(f"config4 conditioned fp32: per-quantile rel max err {err:.3e}")
+    assert err < TOL["fp32"], f"per-quantile rel max err {err:.3e}"
