@@ -133,6 +133,30 @@ jc_status jc_gemm_device(int device, jc_precision precision, const void* a_hi, c
                          const void* w_hi, const void* w_lo, long long ldw, const float* bias, float* c,
                          long long ldc, int m, int n, int k, int flags, void* stream);
 
+/*
+ * Time attention of one layer on DEVICE buffers, the companion kernel of the Timestral and Chronos-2
+ * forwards (timestral/tornado/TimestralKernels.java:114 timeAttention, chronos2/tornado/Chronos2Kernels.java:130
+ * timeAttention), enqueued on `stream`:
+ *   qkv  [rows·n, ld_qkv]: q | k | v at columns 0, d, 2d, heads-major (head h at h·head_dim in each part)
+ *   gate [rows·n, ld_gate] multiplied into the output (NULL: none), out [rows·n, ld_out]
+ * in the precision's storage type (bfloat16 for JC_BF16, IEEE half for JC_FP16, FP32 otherwise).
+ * out = softmax(scale · q·kᵀ over the allowed keys) · v (· gate), per row, head and query (zeros for a query
+ * with no allowed key), with
+ *   mask_mode 0: BlockLayout.timeAllowed (timestral/BlockLayout.java:209-221): encoder queries (< enc) see
+ *                themselves and valid encoder keys up to themselves, or all valid encoder keys when the row
+ *                is a known covariate; decoder queries see valid encoder keys < ll and decoder keys up to
+ *                themselves. key_valid [rows·enc], known [rows] (0/1).
+ *   mask_mode 1: every live key in both directions (Chronos-2's ModelLayout.live), live [rows·n] (0/1).
+ * 16-bit operands of 64-wide heads and n ≤ 256 run on the tcgen05 tensor cores; flags JC_ATTN_CUDA_CORES
+ * forces the FP32-math CUDA-core kernel (a reference for comparisons).
+ */
+#define JC_ATTN_CUDA_CORES 1
+jc_status jc_time_attention_device(int device, jc_precision precision, const void* qkv, long long ld_qkv,
+                                   const void* gate, long long ld_gate, void* out, long long ld_out, int rows, int n,
+                                   int heads, int head_dim, int d, float scale, int mask_mode, int enc, int ll,
+                                   const int32_t* key_valid, const int32_t* known, const int32_t* live, int flags,
+                                   void* stream);
+
 /* Waits for all work on `device`, then returns and clears the device's kernel error word:
  * JC_ERR_TIMEOUT if a kernel's bounded wait gave up since the last call. */
 jc_status jc_device_sync(int device);

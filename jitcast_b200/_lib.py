@@ -23,6 +23,9 @@ PRECISIONS = {"fp32": FP32, "tf32": TF32, "bf16": BF16, "fp16": FP16}
 # GEMM flags (tornado/Kernels.java:50-56, plus GELU)
 BIAS, ACCUMULATE, SILU, TWIN_ONLY, RELU, GELU = 1, 2, 4, 8, 16, 32
 
+# jc_time_attention_device flags
+ATTN_CUDA_CORES = 1
+
 
 class JcUnavailable(RuntimeError):
     """The native library is not built or cannot be loaded."""
@@ -61,6 +64,8 @@ PROTOTYPES: dict[str, tuple] = {
     "jc_gemm_device": (c_int, [c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_int, c_int,
                                c_int, c_int, c_vp]),
     "jc_device_sync": (c_int, [c_int]),
+    "jc_time_attention_device": (c_int, [c_int, c_int, c_vp, c_ll, c_vp, c_ll, c_vp, c_ll, c_int, c_int, c_int, c_int,
+                                         c_int, ctypes.c_float, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp]),
 }
 
 

@@ -115,7 +115,9 @@ __global__ void __launch_bounds__(kQ) time_attention_kernel(AttnArgs a) {
     }
   }
   if (!live) return;
-  const float inv = 1.0f / l;  // every query attends at least itself
+  // a query with no allowed key gets zeros (the layouts never make one: every Timestral query sees itself,
+  // every Chronos-2 row has its live [REG] token)
+  const float inv = l > 0.0f ? 1.0f / l : 0.0f;
   const long long o = ((long long)row * a.n + t) * a.ld_out + hh * DH;
   const long long go = ((long long)row * a.n + t) * a.ld_gate + hh * DH;
 #pragma unroll
@@ -427,7 +429,7 @@ __global__ void __launch_bounds__(kMmaWarps * 32) time_attention_mma_kernel(Attn
       l += __shfl_xor_sync(0xffffffffu, l, 2);
       const int q = q0 + g + hr * 8;
       if (q >= n) continue;
-      const float inv = 1.0f / l;
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
       const long long ob = ((long long)row * n + q) * a.ld_out + hh * 64;
       const long long gb = ((long long)row * n + q) * a.ld_gate + hh * 64;
 #pragma unroll
@@ -476,7 +478,8 @@ cudaError_t launch_variate_t(const AttnArgs& a, cudaStream_t s) {
 
 cudaError_t launch_time_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.rows <= 0) return cudaSuccess;
-  if ((a.qkv_kind == kOutBF16 || a.qkv_kind == kOutF16) && a.head_dim == 64 && a.n <= kMaxTokens &&
+  if (!a.cuda_cores && time_attention_tc_ok(a)) return launch_time_attention_tc(a, s);
+  if (!a.cuda_cores && (a.qkv_kind == kOutBF16 || a.qkv_kind == kOutF16) && a.head_dim == 64 && a.n <= kMaxTokens &&
       a.ld_qkv % 8 == 0 && a.d % 8 == 0) {
     const int npad = (a.n + 63) & ~63;
     const size_t smem = 2 * static_cast<size_t>(npad) * kPitch * 2 + sizeof(int) * npad;

@@ -31,9 +31,15 @@ struct AttnArgs {
   //    rows of the group in group attention, zeros when a group has none (Chronos-2's ModelLayout).
   int mask_mode;
   const int* live;
+  uint32_t* err;  // device error word: bounded waits of the tensor-core kernel that gave up, or null
+  int cuda_cores;  // 1: the FP32-math CUDA-core kernel even where the tensor-core kernels apply
 };
 
 cudaError_t launch_time_attention(const AttnArgs& a, cudaStream_t s);
+
+// The tcgen05 time attention (attention_tc.cu): 16-bit q/k/v of 64-wide heads, ≤ 256 tokens per row.
+bool time_attention_tc_ok(const AttnArgs& a);
+cudaError_t launch_time_attention_tc(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_variate_attention(const AttnArgs& a, cudaStream_t s);
 
 }  // namespace jc

@@ -1,0 +1,462 @@
+// Time attention on the 5th-generation tensor cores (16-bit q/k/v, 64-wide heads, n ≤ 256 tokens).
+//
+// One CTA of 4 warps per (row, head). TMA brings the head's Q (the first 128 tokens) and K and V (the
+// row's tokens, rounded up to 16) into 128-byte-swizzled shared memory; one thread issues
+//
+//   S[128 × nk] = Q · Kᵀ            tcgen05.mma kind::f16, A and B K-major, accumulator in TMEM
+//   O[128 × 64] = P · V              A = P (K-major, written by the softmax), B = V read MN-major,
+//                                    both FP16 (a BF16 V is converted in shared memory)
+//
+// and each thread owns one query row in between: it reads its row of S from TMEM twice (row max, then
+// exp2 and the row sum), applies the row's mask, and writes P as 16-bit values straight into the
+// swizzled A-operand layout. The epilogue reads its row of O from TMEM, divides by the row sum,
+// multiplies the gate (Timestral) and stores 16-byte vectors. Queries past the first 128 (the decoder
+// tokens of a Timestral row, the [REG] and future tokens of a Chronos-2 row) run on the CUDA cores
+// from the same shared-memory K and V, one warp per query.
+//
+// Masks: BlockLayout.timeAllowed (timestral/BlockLayout.java:209-221; mask mode 0) or per-key
+// liveness in both directions (Chronos-2 ModelLayout; mask mode 1). Semantics: CpuTimestral.java:191-262
+// and CpuChronos2.timeAttention; softmax(scale · q·k) over the allowed keys, times the gate if any.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "attention.cuh"
+#include "ptx.cuh"
+
+namespace jc {
+
+namespace {
+
+constexpr int kTcThreads = 128;
+constexpr int kTcQ = 128;        // queries per MMA tile (TMEM lanes)
+constexpr int kTcMaxTokens = 256;
+constexpr uint32_t kErrAttnWait = 1u << 5;
+
+struct TcShape {
+  int nkl;        // K/V rows staged (round_up(n, 16))
+  int nkm;        // keys in the S = Q·Kᵀ MMA (multiple of 16, ≤ nkl)
+  int o_col;      // first TMEM column of O
+  int tmem_cols;  // TMEM columns allocated (power of two)
+  int k_off, v_off, p_off, bar_off;  // byte offsets into the 1024-aligned dynamic shared memory
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (std::is_same<T, __half>::value) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t u) {
+  if constexpr (std::is_same<T, __half>::value) {
+    return __half22float2(*reinterpret_cast<__half2*>(&u));
+  } else {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+  }
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Byte offset of element (r, c), c < 64, of a 16-bit tile of 128-byte rows stored with the 128-byte
+// swizzle (the layout TMA writes and the UMMA descriptors read; the tile is 1024-byte aligned).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((((c >> 3) ^ r) & 7) << 4) + ((c & 7) << 1));
+}
+
+// BlockLayout.timeAllowed (mode 0) or key liveness (mode 1) for query q and key k; `bits` holds the
+// row's key_valid (mode 0) or live (mode 1) flags, one bit per key.
+__device__ __forceinline__ bool allowed(const AttnArgs& a, const uint32_t* bits, bool known, int q, int k) {
+  const bool flag = (bits[k >> 5] >> (k & 31)) & 1u;
+  if (a.mask_mode == 1) return k < a.n && flag;
+  if (q < a.enc) return k < a.enc && (k == q || (flag && (k <= q || known)));
+  if (k < a.enc) return k < a.ll && flag;
+  return k <= q && k < a.n;
+}
+
+// Bits of the keys in [lo, hi) that fall in 32-key word w.
+__device__ __forceinline__ uint32_t range_bits(int w, int lo, int hi) {
+  const int a = max(lo - 32 * w, 0), b = min(hi - 32 * w, 32);
+  if (a >= b) return 0u;
+  return static_cast<uint32_t>((1ull << b) - 1ull) & ~static_cast<uint32_t>((1ull << a) - 1ull);
+}
+
+// Word w of the keys query q may read: BlockLayout.timeAllowed (mode 0) or the live keys (mode 1);
+// `bits` holds the row's key_valid (mode 0, keys < enc) or live (mode 1, keys < n) flags.
+__device__ __forceinline__ uint32_t allowed_word(const AttnArgs& a, const uint32_t* bits, bool known, int q, int w) {
+  const uint32_t f = bits[w];
+  if (a.mask_mode == 1) return f;
+  if (q < a.enc) return (known ? f : (f & range_bits(w, 0, q + 1))) | range_bits(w, q, q + 1);
+  return (f & range_bits(w, 0, a.ll)) | range_bits(w, a.enc, min(q, a.n - 1) + 1);
+}
+
+constexpr int kTailQ = 8;  // queries past the MMA tile handled per round
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                                                                  const __grid_constant__ CUtensorMap tmKV,
+                                                                  AttnArgs a, TcShape sh) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = smem;
+  uint8_t* ks = smem + sh.k_off;
+  uint8_t* vs = smem + sh.v_off;
+  uint8_t* ps = smem + sh.p_off;  // over Q and K when they are large enough (both dead by then)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sh.bar_off);  // [0] TMA, [1] S, [2] O
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
+  uint32_t* abort_flag = tmem_slot + 1;
+  uint32_t* bits = tmem_slot + 2;  // [8]: one bit per key
+  // tail-query scratch in Q's tile once the S MMA has read it: q (fp32), scores then probabilities, row sums
+  float* tq = reinterpret_cast<float*>(qs);                 // [kTailQ][64]
+  float* tsc = tq + kTailQ * 64;                            // [kTailQ][kTcMaxTokens]
+  float* tl = tsc + kTailQ * kTcMaxTokens;                  // [kTailQ]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hh = blockIdx.x % a.heads;
+  const int row = blockIdx.x / a.heads;
+  const int n = a.n;
+  const bool known = a.mask_mode == 0 && a.known[row] != 0;
+  const T* qkv = static_cast<const T*>(a.qkv);
+
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, static_cast<uint32_t>(sh.tmem_cols));
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  // the row's key flags as bit words (keys ≥ the flag array's length read as 0)
+  for (int k0 = 0; k0 < kTcMaxTokens; k0 += kTcThreads) {
+    const int k = k0 + tid;
+    int f = 0;
+    if (a.mask_mode == 1) {
+      f = k < n ? a.live[static_cast<long long>(row) * n + k] : 0;
+    } else {
+      f = k < a.enc ? a.key_valid[static_cast<long long>(row) * a.enc + k] : 0;
+    }
+    const uint32_t word = __ballot_sync(0xffffffffu, f != 0);
+    if (lane == 0) bits[k >> 5] = word;
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const long long row0 = static_cast<long long>(row) * n;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(kTcQ * 128 + 2 * sh.nkl * 128));
+    tma_load_2d(qs, &tmQ, &bars[0], hh * 64, static_cast<int>(row0));
+    tma_load_2d(ks, &tmKV, &bars[0], a.d + hh * 64, static_cast<int>(row0));
+    tma_load_2d(vs, &tmKV, &bars[0], 2 * a.d + hh * 64, static_cast<int>(row0));
+  }
+  // this thread's query and its allowed keys as bit words
+  const int q = tid;
+  const bool my_row = q < n;
+  if (!mbar_wait(&bars[0], 0)) atomicOr(abort_flag, 1u);
+  __syncthreads();
+  const bool ok = *abort_flag == 0;
+  const uint32_t fmt = std::is_same<T, __half>::value ? 0u : 1u;
+  if (ok && tid == 0) {
+    tc_fence_after();
+    const uint32_t idesc = idesc_f32acc(fmt, kTcQ, static_cast<uint32_t>(sh.nkm));
+    const uint32_t qa = smem_u32(qs), ka = smem_u32(ks);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_bf16(tmem, sdesc_k_sw128(qa + 32 * k), sdesc_k_sw128(ka + 32 * k), idesc, k > 0);
+    umma_commit(&bars[1]);
+  }
+
+  // P·V runs in FP16 in both modes (an 11-bit P): a BF16 V tile is converted in place, saturating at
+  // ±65504, while the S MMA reads Q and K
+  if (ok && !std::is_same<T, __half>::value) {
+    uint4* v4 = reinterpret_cast<uint4*>(vs);
+    for (int i = tid; i < sh.nkl * 8; i += kTcThreads) {
+      uint4 u = v4[i];
+      u.x = pack2<__half>(fminf(fmaxf(unpack2<__nv_bfloat16>(u.x).x, -65504.0f), 65504.0f),
+                          fminf(fmaxf(unpack2<__nv_bfloat16>(u.x).y, -65504.0f), 65504.0f));
+      u.y = pack2<__half>(fminf(fmaxf(unpack2<__nv_bfloat16>(u.y).x, -65504.0f), 65504.0f),
+                          fminf(fmaxf(unpack2<__nv_bfloat16>(u.y).y, -65504.0f), 65504.0f));
+      u.z = pack2<__half>(fminf(fmaxf(unpack2<__nv_bfloat16>(u.z).x, -65504.0f), 65504.0f),
+                          fminf(fmaxf(unpack2<__nv_bfloat16>(u.z).y, -65504.0f), 65504.0f));
+      u.w = pack2<__half>(fminf(fmaxf(unpack2<__nv_bfloat16>(u.w).x, -65504.0f), 65504.0f),
+                          fminf(fmaxf(unpack2<__nv_bfloat16>(u.w).y, -65504.0f), 65504.0f));
+      v4[i] = u;
+    }
+    fence_proxy_async_smem();
+  }
+  // the S MMA must have read Q before its tile holds the tail scratch
+  if (ok && !mbar_wait(&bars[1], 0)) atomicOr(abort_flag, 2u);
+  __syncthreads();
+  tc_fence_after();
+  const bool ok1 = *abort_flag == 0;
+  const float sl2 = a.scale * 1.4426950408889634f;
+
+  // queries past the MMA tile, kTailQ at a time by all threads on the CUDA cores: scores with a thread
+  // per key, softmax with a warp per query, P·V with a thread per (query, dim)
+  if (ok1) {
+    for (int t0 = kTcQ; t0 < n; t0 += kTailQ) {
+      const int nt = min(kTailQ, n - t0);
+      for (int i = tid; i < nt * 64; i += kTcThreads) {
+        const int j = i >> 6, e = i & 63;
+        tq[i] = unpack2<T>(*reinterpret_cast<const uint32_t*>(qkv + (row0 + t0 + j) * a.ld_qkv + hh * 64 + (e & ~1)))
+                    .x * (e & 1 ? 0.0f : 1.0f) +
+                unpack2<T>(*reinterpret_cast<const uint32_t*>(qkv + (row0 + t0 + j) * a.ld_qkv + hh * 64 + (e & ~1)))
+                    .y * (e & 1 ? 1.0f : 0.0f);
+      }
+      __syncthreads();
+      for (int k = tid; k < sh.nkl; k += kTcThreads) {
+        float acc[kTailQ];
+#pragma unroll
+        for (int j = 0; j < kTailQ; ++j) acc[j] = 0.0f;
+#pragma unroll 2
+        for (int c = 0; c < 8; ++c) {
+          const uint4 u = *reinterpret_cast<const uint4*>(ks + sw128(k, 8 * c));
+          const float2 f0 = unpack2<T>(u.x), f1 = unpack2<T>(u.y), f2 = unpack2<T>(u.z), f3 = unpack2<T>(u.w);
+#pragma unroll
+          for (int j = 0; j < kTailQ; ++j) {
+            if (j < nt) {
+              const float4 qa = *reinterpret_cast<const float4*>(tq + j * 64 + 8 * c);
+              const float4 qb = *reinterpret_cast<const float4*>(tq + j * 64 + 8 * c + 4);
+              acc[j] = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, acc[j]))));
+              acc[j] = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, acc[j]))));
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kTailQ; ++j) {
+          if (j < nt) {
+            const bool al = k < n && ((allowed_word(a, bits, known, t0 + j, k >> 5) >> (k & 31)) & 1u);
+            tsc[j * kTcMaxTokens + k] = al ? acc[j] * sl2 : -INFINITY;
+          }
+        }
+      }
+      __syncthreads();
+      for (int j = warp; j < nt; j += kTcThreads / 32) {
+        float* sj = tsc + j * kTcMaxTokens;
+        float mx = -INFINITY;
+        for (int k = lane; k < sh.nkl; k += 32) mx = fmaxf(mx, sj[k]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float l = 0.0f;
+        for (int k = lane; k < sh.nkl; k += 32) {
+          const float p = sj[k] == -INFINITY ? 0.0f : ex2f(sj[k] - mx);
+          sj[k] = p;
+          l += p;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) tl[j] = l;
+      }
+      __syncthreads();
+      for (int i = tid; i < nt * 64; i += kTcThreads) {
+        const int j = i >> 6, e = i & 63;
+        const float* pj = tsc + j * kTcMaxTokens;
+        float o = 0.0f;
+        for (int k = 0; k < sh.nkl; ++k) {
+          const float p = pj[k];
+          if (p != 0.0f) o = fmaf(p, __half2float(*reinterpret_cast<const __half*>(vs + sw128(k, e))), o);
+        }
+        const float l = tl[j];
+        o *= l > 0.0f ? 1.0f / l : 0.0f;
+        const long long tok = row0 + t0 + j;
+        if (a.gate) o *= unpack2<T>(*reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.gate) +
+                                                                      tok * a.ld_gate + hh * 64 + (e & ~1)))
+                             .x * (e & 1 ? 0.0f : 1.0f) +
+                         unpack2<T>(*reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.gate) +
+                                                                      tok * a.ld_gate + hh * 64 + (e & ~1)))
+                             .y * (e & 1 ? 1.0f : 0.0f);
+        T* op = static_cast<T*>(a.out_hi) + tok * a.ld_out + hh * 64 + e;
+        if constexpr (std::is_same<T, __half>::value)
+          *op = __float2half_rn(fminf(fmaxf(o, -65504.0f), 65504.0f));
+        else
+          *op = __float2bfloat16_rn(o);
+      }
+      __syncthreads();
+    }
+  }
+
+  // softmax of this thread's row of S into the swizzled FP16 A-operand tile of P. A 32-key chunk no
+  // query of the warp may read (past the diagonal of a causal row) is skipped by the whole warp.
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  float l = 0.0f;
+  if (ok1) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kTcMaxTokens / 32; ++c) {
+      const uint32_t mw = allowed_word(a, bits, known, q, c);
+      if (32 * c >= sh.nkm || !__any_sync(0xffffffffu, mw != 0u)) continue;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(lane_base + 32 * c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if ((mw >> j) & 1u) mx = fmaxf(mx, __uint_as_float(r[j]));
+    }
+    const float mo = mx == -INFINITY ? 0.0f : mx * sl2;
+#pragma unroll
+    for (int c = 0; c < kTcMaxTokens / 32; ++c) {
+      if (32 * c >= sh.nkm) continue;
+      uint32_t pk[16];
+      const uint32_t mw = allowed_word(a, bits, known, q, c);
+      if (__any_sync(0xffffffffu, mw != 0u)) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(lane_base + 32 * c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float p0 = (mw >> j) & 1u ? ex2f(fmaf(__uint_as_float(r[j]), sl2, -mo)) : 0.0f;
+          const float p1 = (mw >> (j + 1)) & 1u ? ex2f(fmaf(__uint_as_float(r[j + 1]), sl2, -mo)) : 0.0f;
+          l += p0 + p1;
+          pk[j >> 1] = pack2<__half>(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) pk[j] = 0u;
+      }
+      // 32 keys = 4 chunks of 16 bytes within the 64-key swizzle atom c / 2
+      uint8_t* atom = ps + (c >> 1) * (kTcQ * 128);
+      const int cc = (c & 1) * 4;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(atom + sw128(q, 8 * (cc + u))) =
+            make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  const bool ok2 = *abort_flag == 0;
+  if (ok2 && tid == 0) {
+    tc_fence_after();
+    // O into TMEM columns [0, 64) (S is consumed); V read MN-major: instruction descriptor bit 16
+    const uint32_t idesc = idesc_f32acc(0u, kTcQ, 64) | (1u << 16);  // FP16 P and V
+    const uint32_t pa = smem_u32(ps), va = smem_u32(vs);
+    for (int j = 0; j < sh.nkm / 16; ++j)
+      umma_bf16(tmem, sdesc_k_sw128(pa + (j >> 2) * (kTcQ * 128) + 32 * (j & 3)), sdesc_k_sw128(va + 2048 * j), idesc,
+                j > 0);
+    umma_commit(&bars[2]);
+  }
+  // this thread's gate row, fetched while the O MMA runs
+  uint4 gate[8];
+  if (a.gate && my_row) {
+    const uint4* gp = reinterpret_cast<const uint4*>(static_cast<const T*>(a.gate) + (row0 + q) * a.ld_gate + hh * 64);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gate[i] = __ldg(gp + i);
+  }
+  if (ok2 && !mbar_wait(&bars[2], 0)) atomicOr(abort_flag, 4u);
+  __syncthreads();
+  tc_fence_after();
+  const bool ok3 = *abort_flag == 0;
+  // tcgen05.ld and its wait are warp-collective: every lane runs them, only rows < n store
+  if (ok3) {
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    T* op = static_cast<T*>(a.out_hi) + (row0 + q) * a.ld_out + hh * 64;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(lane_base + static_cast<uint32_t>(32 * half), r);
+      tmem_ld_wait();
+      if (!my_row) continue;
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        float v0 = __uint_as_float(r[j]) * inv, v1 = __uint_as_float(r[j + 1]) * inv;
+        if (a.gate) {
+          const float2 g = unpack2<T>(word_of(gate[(16 * half + (j >> 1)) >> 2], (j >> 1) & 3));
+          v0 *= g.x;
+          v1 *= g.y;
+        }
+        pk[j >> 1] = pack2<T>(v0, v1);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(op + 32 * half);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) dst[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, static_cast<uint32_t>(sh.tmem_cols));
+  if (tid == 0 && *abort_flag != 0 && a.err) atomicOr(a.err, kErrAttnWait);
+}
+
+}  // namespace
+
+// Whether the tensor-core kernel takes this attention (16-bit operands of 64-wide heads, ≤ 256 tokens,
+// 16-byte aligned rows, 16-bit output).
+bool time_attention_tc_ok(const AttnArgs& a) {
+  const bool k16 = a.qkv_kind == kOutBF16 || a.qkv_kind == kOutF16;
+  return k16 && a.out_kind == a.qkv_kind && (!a.gate || a.gate_kind == a.qkv_kind) && a.head_dim == 64 &&
+         a.n >= 1 && a.n <= kTcMaxTokens && a.ld_qkv % 8 == 0 && a.d % 64 == 0 && a.ld_out % 8 == 0 &&
+         (!a.gate || a.ld_gate % 8 == 0) && (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0 &&
+         (reinterpret_cast<uintptr_t>(a.out_hi) & 15) == 0 && (!a.gate || (reinterpret_cast<uintptr_t>(a.gate) & 15) == 0);
+}
+
+cudaError_t launch_time_attention_tc(const AttnArgs& a, cudaStream_t s) {
+  TcShape sh{};
+  sh.nkl = (a.n + 15) & ~15;
+  const int first = a.n < kTcQ ? a.n : kTcQ;
+  // encoder queries of mask mode 0 read encoder keys only
+  sh.nkm = (a.mask_mode == 0 && a.enc >= first) ? ((a.enc + 15) & ~15) : sh.nkl;
+  if (sh.nkm > sh.nkl) sh.nkm = sh.nkl;
+  sh.o_col = 0;  // O reuses S's columns once the softmax has read S
+  sh.tmem_cols = sh.nkm <= 128 ? 128 : 256;
+  sh.k_off = kTcQ * 128;
+  sh.v_off = sh.k_off + sh.nkl * 128;
+  const int p_bytes = ((sh.nkm + 63) / 64) * kTcQ * 128;
+  const int qkv_end = (sh.v_off + sh.nkl * 128 + 1023) & ~1023;
+  // P over the Q and K tiles when it fits there (both are dead once the S MMA and the tail queries are
+  // done), else after V
+  sh.p_off = p_bytes <= sh.v_off ? 0 : qkv_end;
+  sh.bar_off = sh.p_off == 0 ? qkv_end : qkv_end + p_bytes;
+  int smem = sh.bar_off + 3 * 8 + 4 * 10 + 1024;
+  // never more CTAs on an SM than its 512 TMEM columns hold, so no tcgen05.alloc has to wait: ask for
+  // enough shared memory that one more CTA would not fit in the SM's 228 KB (1 KB reserved per CTA)
+  const int fit = 512 / sh.tmem_cols;
+  const int floor_smem = 233472 / (fit + 1) - 1024 + 16;
+  if (smem < floor_smem) smem = floor_smem;
+  const int op = a.qkv_kind == kOutBF16 ? kOpBF16 : kOpF16;
+  const long long tokens = static_cast<long long>(a.rows) * a.n;
+  CUtensorMap mq, mkv;
+  if (!make_operand_map(&mq, a.qkv, op, tokens, a.ld_qkv, a.ld_qkv, kTcQ) ||
+      !make_operand_map(&mkv, a.qkv, op, tokens, a.ld_qkv, a.ld_qkv, sh.nkl))
+    return cudaErrorInvalidValue;
+  static bool raised[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!raised[dev & 63]) {
+    const int most = 200 * 1024;
+    cudaFuncSetAttribute(attention_tc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(attention_tc_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    raised[dev & 63] = true;
+  }
+  const unsigned blocks = static_cast<unsigned>(static_cast<long long>(a.rows) * a.heads);
+  if (a.qkv_kind == kOutBF16)
+    attention_tc_kernel<__nv_bfloat16><<<blocks, kTcThreads, smem, s>>>(mq, mkv, a, sh);
+  else
+    attention_tc_kernel<__half><<<blocks, kTcThreads, smem, s>>>(mq, mkv, a, sh);
+  return cudaGetLastError();
+}
+
+}  // namespace jc

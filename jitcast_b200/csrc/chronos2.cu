@@ -331,6 +331,7 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   a.group_end = p.ge;
   a.mask_mode = 1;
   a.live = p.live;
+  a.err = dv.err;
   for (const C2Layer& L : w.layers) {
     for (int which = 0; which < 2; ++which) {
       const C2Attn& A = which == 0 ? L.time : L.group;

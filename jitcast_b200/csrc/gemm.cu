@@ -575,6 +575,11 @@ static bool make_map(CUtensorMap* map, const void* base, int op, long long rows,
   return r == CUDA_SUCCESS;
 }
 
+bool make_operand_map(CUtensorMap* map, const void* base, int op, long long rows, long long k, long long ld,
+                      int box_rows) {
+  return make_map(map, base, op, rows, k, ld, box_rows);
+}
+
 EpiParams epi_default() {
   EpiParams p{};
   p.rg = 1 << 30;

@@ -3,6 +3,7 @@
 // and W [N, K] both K-major (PyTorch [out, in] weights), the accumulator in TMEM.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -101,5 +102,11 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream, uint32_t* err);
 
 // Checks the alignment and shape rules of launch_gemm; returns nullptr or a message.
 const char* check_gemm(const GemmArgs& g);
+
+// A 2-D TMA tensor map over a row-major [rows, k] matrix of operand kind `op` (row pitch `ld`
+// elements): 128-byte swizzle, box = 128 bytes of a row × box_rows rows, zero fill past the edges.
+// The layout the tcgen05 K-major (and, for 64 16-bit columns, MN-major) operand descriptors read.
+bool make_operand_map(CUtensorMap* map, const void* base, int op, long long rows, long long k, long long ld,
+                      int box_rows);
 
 }  // namespace jc

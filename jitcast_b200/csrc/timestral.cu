@@ -395,6 +395,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       a.group_start = p.gs;
       a.group_end = p.ge;
       a.covariates = p.cov;
+      a.err = dv.err;
       prof.begin(s, "attention", 4.0 * T * n * d);
       JC_TRY(A.time ? launch_time_attention(a, s) : launch_variate_attention(a, s));
       prof.end(s);
