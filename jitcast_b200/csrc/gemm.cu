@@ -249,6 +249,27 @@ __device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int
   }
 }
 
+// Pulls the thread's share of a tile's residual input (the 128-byte lines of its row in the tile's columns it
+// will add) into L2, issued before the epilogue waits for the tile's accumulator so that the HBM reads
+// overlap the tile's MMAs instead of the epilogue.
+template <int BN>
+__device__ __forceinline__ void prefetch_residual(const EpiParams& p, int M, int N, int m0, int n0, int row_in_tile,
+                                                  int half) {
+  if (!p.accumulate || p.mode != kEpiPlain) return;
+  const int row = m0 + row_in_tile;
+  if (row >= M) return;
+  const int rr = row % p.rg;
+  const int orow = (row / p.rg) * p.rg_stride + rr + p.rg_off + (rr >= p.rg_split ? p.rg_shift : 0);
+  const float* base = p.cin + (long long)orow * p.ldcin;
+#pragma unroll 1
+  for (int u = half; u < BN / 64; u += 2)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = n0 + 64 * u + 32 * c;
+      if (col0 < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + col0));
+    }
+}
+
 __device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   tmem_ld_32x32b_x32(taddr, r);
@@ -517,6 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t aph = (it >> 1) & 1;
+      prefetch_residual<BN>(ep, M, N, (t / n_blks) * C::BM, (t % n_blks) * BN, row_in_tile, half);
       const bool got = mbar_wait(acc_full + buf, aph);
       const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
       if (!all) {

@@ -57,6 +57,55 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const
   }
 }
 
+// One warp per row held in registers: NV float4 per lane (cols = 128·NV), one read of x, 16-byte loads.
+template <int NV>
+__global__ void rmsnorm_vec_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w, float eps,
+                                   int kind, void* hi, void* lo, long long ldy, long long rows, int grows, int gstride,
+                                   int goff) {
+  constexpr int cols = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const long long src = grows > 0 ? (r / grows) * gstride + goff + r % grows : r;
+    const float4* xr = reinterpret_cast<const float4*>(x + src * ldx);
+    float4 v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(ss) / cols + eps));
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = 4 * (lane + 32 * i);
+      float4 g = w ? __ldg(reinterpret_cast<const float4*>(w + c)) : make_float4(1.0f, 1.0f, 1.0f, 1.0f);
+      const float y0 = v[i].x * inv * g.x, y1 = v[i].y * inv * g.y, y2 = v[i].z * inv * g.z, y3 = v[i].w * inv * g.w;
+      const long long o = r * ldy + c;
+      if (kind == kOutBF16) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(y0, y1), b = __floats2bfloat162_rn(y2, y3);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(hi) + o) = u;
+      } else if (kind == kOutF16) {
+        __half2 a = __floats2half2_rn(fminf(fmaxf(y0, -65504.0f), 65504.0f), fminf(fmaxf(y1, -65504.0f), 65504.0f));
+        __half2 b = __floats2half2_rn(fminf(fmaxf(y2, -65504.0f), 65504.0f), fminf(fmaxf(y3, -65504.0f), 65504.0f));
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&a);
+        u.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(hi) + o) = u;
+      } else {
+        put(kind, hi, lo, o, y0);
+        put(kind, hi, lo, o + 1, y1);
+        put(kind, hi, lo, o + 2, y2);
+        put(kind, hi, lo, o + 3, y3);
+      }
+    }
+  }
+}
+
 __global__ void fill_rows_kernel(float* x, long long ldx, const float* __restrict__ q, int cols, int rows, int t0,
                                  int t1, int n) {
   const int h = t1 - t0;
@@ -96,8 +145,34 @@ void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, flo
                     void* y_lo, long long ldy, long long rows, int gather_rows, int gather_stride, int gather_off,
                     cudaStream_t s) {
   if (rows <= 0) return;
-  rmsnorm_kernel<<<grid_for(rows * 32, 256), 256, 0, s>>>(x, ldx, w, cols, eps, out_kind, y_hi, y_lo, ldy, rows,
-                                                          gather_rows, gather_stride, gather_off);
+  // the register-resident kernel when the row is a whole number of 128-column groups and every row and the
+  // weight start on a 16-byte boundary (8 bytes for the 16-bit output)
+  const bool vec = cols % 128 == 0 && cols <= 1024 && ldx % 4 == 0 && ldy % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (!w || (reinterpret_cast<uintptr_t>(w) & 15) == 0) &&
+                   (reinterpret_cast<uintptr_t>(y_hi) & 7) == 0;
+  const int blocks = grid_for(rows * 32, 256);
+  if (vec) {
+    switch (cols / 128) {
+#define JC_RMS_CASE(NV)                                                                                          \
+  case NV:                                                                                                       \
+    rmsnorm_vec_kernel<NV><<<blocks, 256, 0, s>>>(x, ldx, w, eps, out_kind, y_hi, y_lo, ldy, rows, gather_rows, \
+                                                  gather_stride, gather_off);                                    \
+    return;
+      JC_RMS_CASE(1)
+      JC_RMS_CASE(2)
+      JC_RMS_CASE(3)
+      JC_RMS_CASE(4)
+      JC_RMS_CASE(5)
+      JC_RMS_CASE(6)
+      JC_RMS_CASE(7)
+      JC_RMS_CASE(8)
+#undef JC_RMS_CASE
+      default:
+        break;
+    }
+  }
+  rmsnorm_kernel<<<blocks, 256, 0, s>>>(x, ldx, w, cols, eps, out_kind, y_hi, y_lo, ldy, rows, gather_rows,
+                                        gather_stride, gather_off);
 }
 
 void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int t0, int t1, int n,
