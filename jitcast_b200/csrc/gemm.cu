@@ -17,6 +17,7 @@
 
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 namespace jc {
@@ -563,6 +564,202 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---- the CTA-pair kernel --------------------------------------------------------------------
+// The same GEMM over 256 × 256 tiles shared by a cluster of two CTAs on neighbouring SMs: each CTA stages
+// its own 128 rows of A and its own 128 rows (half of the tile's N) of W, and one thread of CTA 0 issues
+// tcgen05.mma.cta_group::2 (M 256 × N 256) that reads both CTAs' tiles and leaves each CTA's 128 rows of
+// the accumulator in its own TMEM. Per SM that halves the W bytes per MMA, so six 32 KB stages stay in
+// flight instead of four 48 KB ones. Both CTAs' TMA loads complete on CTA 0's stage barrier (armed by CTA
+// 0 for both CTAs' bytes); CTA 0's commits arrive on both CTAs' stage-free and accumulator-ready barriers;
+// each CTA's epilogue warps release an accumulator with one arrive on CTA 0's barrier. No TMA multicast.
+template <int OPK_>
+struct CfgPair {
+  static constexpr int OPK = OPK_;
+  static constexpr int BN = 256;  // tile N; each CTA stages BN / 2 rows of W
+  static constexpr int BM = 128;  // rows per CTA; the tile is 2 · BM rows
+  static constexpr int ESZ = (OPK == kOpBF16 || OPK == kOpF16) ? 2 : 4;
+  static constexpr int BK = 128 / ESZ;
+  static constexpr int UK = 32 / ESZ;
+  static constexpr int NSUB = BK / UK;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = (BN / 2) * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : OPK == kOpF16 ? 0u : 2u, 2 * BM, BN);
+  static_assert(OPK != kOpSplit, "the split FP32 mode runs on the single-CTA kernel");
+  static_assert(SMEM <= 200 * 1024, "shared memory");
+};
+
+template <int OPK>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                     int K, EpiParams ep, uint32_t* err) {
+  using C = CfgPair<OPK>;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile uint32_t* abort_flag = tmem_holder + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int m_blks = (M + 2 * C::BM - 1) / (2 * C::BM), n_blks = (N + BN - 1) / BN;
+  const int tiles = m_blks * n_blks;
+  const int kblks = (K + C::BK - 1) / C::BK;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 2 * kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  // both CTAs' barriers exist and their TMEM is allocated before any cross-CTA arrival or load
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs): this CTA's A rows and W half, counted on CTA 0's stage barrier ----
+      const uint32_t full0 = mapa_shared(smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        const int m0 = (t / n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM;
+        const int n0 = (t % n_blks) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < kblks; ++kb) {
+          if (!mbar_wait(empty + stage, phase ^ 1) || *abort_flag) {
+            atomicOr(err, kErrTimeoutEmpty);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * C::STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(full + stage, 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, full0 + 8 * stage, kb * C::BK, m0);
+          tma_load_2d_pair(sa + C::A_BYTES, &tmB, full0 + 8 * stage, kb * C::BK, n0);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (CTA 0 only) ----
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs, ++it) {
+        const int buf = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag) {
+          atomicOr(err, kErrTimeoutAccFree);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < kblks; ++kb) {
+          if (!mbar_wait(full + stage, phase) || *abort_flag) {
+            atomicOr(err, kErrTimeoutFull);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < C::NSUB; ++k) {
+            const uint64_t ad = sdesc_k_sw128(sa + 32 * k);
+            const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if (OPK == kOpTF32)
+              umma_tf32_pair(d, ad, bd, C::IDESC, acc);
+            else
+              umma_f16_pair(d, ad, bd, C::IDESC, acc);
+          }
+          umma_commit_pair_multicast(empty + stage, 0x3);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_multicast(acc_full + buf, 0x3);
+      }
+      // every MMA this thread issued has completed once `drain` flips
+      umma_commit_pair(smem_u32(drain));
+      mbar_wait(drain, 0);
+    }
+  } else {
+    // ---- epilogue (both CTAs): warps 2..9; this CTA's 128 rows of each tile ----
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
+    int it = 0;
+    for (int t = pair; t < tiles; t += pairs, ++it) {
+      const int buf = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const int m0 = (t / n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (t % n_blks) * BN;
+      prefetch_residual<BN>(ep, M, N, m0, n0, row_in_tile, half);
+      const bool got = mbar_wait(acc_full + buf, aph);
+      const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
+      if (!all) {
+        if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+      epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile, half);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  // neither CTA frees its TMEM or exits while the other's MMAs, loads or arrivals may still target it
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
 // ---- host side ---------------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -679,6 +876,47 @@ static cudaError_t launch_cfg(const GemmArgs& g, cudaStream_t stream, uint32_t* 
   return cudaGetLastError();
 }
 
+template <int OPK>
+static cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, uint32_t* err, int num_sms) {
+  using C = CfgPair<OPK>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, g.a_hi, OPK, g.M, g.K, g.lda, C::BM) || !make_map(&mb, g.w_hi, OPK, g.N, g.K, g.ldw, C::BN / 2))
+    return cudaErrorInvalidValue;
+  const int tiles = ((g.M + 2 * C::BM - 1) / (2 * C::BM)) * ((g.N + C::BN - 1) / C::BN);
+  const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK>, ma, mb, g.M, g.N, g.K, g.ep, err);
+}
+
+// JC_GEMM_PAIR=0 in the environment keeps every GEMM on the single-CTA kernel (for comparisons).
+static bool pair_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = std::getenv("JC_GEMM_PAIR");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 static int sm_count() {
   static int count[64] = {};
   int dev = 0;
@@ -731,6 +969,19 @@ cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err)
   GemmArgs g = gin;
   g.ep.vec_ok = vector_ok(g.ep);
   const int sms = sm_count();
+  // CTA pairs for the 16-bit and TF32 modes when the 256 × 256 tiles still give every SM pair work and the
+  // tile width keeps the q|k|v|gate layout whole
+  if (pair_enabled() && g.op != kOpSplit && (g.bn == 0 || g.bn == 256) &&
+      (g.ep.mode != kEpiQKV || ((qkv_tile_choices(g.ep) >> 2) & 1))) {
+    const long long ptiles = (long long)((g.M + 255) / 256) * ((g.N + 255) / 256);
+    if (ptiles >= sms / 2) {
+      switch (g.op) {
+        case kOpBF16: return launch_pair<kOpBF16>(g, stream, err, sms);
+        case kOpF16: return launch_pair<kOpF16>(g, stream, err, sms);
+        default: return launch_pair<kOpTF32>(g, stream, err, sms);
+      }
+    }
+  }
   const int bn = choose_bn(g, sms);
 #define JC_LAUNCH(BN_)                                                  \
   switch (g.op) {                                                       \

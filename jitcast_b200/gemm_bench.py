@@ -5,7 +5,8 @@
 
 Prints one JSON line: milliseconds per call (CUDA events on the launching stream after warm-up),
 achieved TFLOP/s, and the algorithmic bytes per call (A, W, C written, C read when accumulating).
-``--cublas`` adds the same shape through torch.matmul (cuBLAS) for comparison. BASELINE config 1 is
+``--cublas`` adds the same shape through torch.matmul (cuBLAS) for comparison; ``--single`` keeps the GEMM on
+the single-CTA kernel (large shapes otherwise run on CTA pairs). BASELINE config 1 is
 ``--m 1024 --n 768 --k 256 --epilogue bias``.
 """
 
@@ -28,7 +29,12 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--epilogue", default="plain", choices=["plain", "bias", "bias_silu", "accumulate"])
     ap.add_argument("--cublas", action="store_true")
+    ap.add_argument("--single", action="store_true", help="keep the GEMM on the single-CTA kernel")
     args = ap.parse_args(argv)
+    if args.single:
+        import os
+
+        os.environ["JC_GEMM_PAIR"] = "0"
 
     import torch
 

@@ -89,6 +89,35 @@ def test_device_buffers(jc, precision, m, n, k):
     assert err < TOL[precision], f"{precision} {m}x{n}x{k}: {err:.3e}"
 
 
+@pytest.mark.parametrize("precision", ["tf32", "bf16", "fp16"])
+@pytest.mark.parametrize("m,n,k,flags", [(4133, 4160, 1000, 0),          # CTA-pair tiles, ragged M, N and K
+                                         (8192, 1024, 4096, 2),          # residual add, long K
+                                         (19000, 768, 256, 1 | 4)])      # bias + SiLU, short K
+def test_cta_pair_tiles(jc, precision, m, n, k, flags):
+    # shapes with at least one 256 × 256 tile per SM pair run on the two-CTA (cta_group::2) kernel
+    import torch
+
+    rng = np.random.default_rng(m + n + k + flags)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, n).astype(np.float32)
+    c0 = rng.standard_normal((m, n)).astype(np.float32)
+    dev = torch.device("cuda:0")
+    tx, tw, tb, tc = (torch.from_numpy(v).to(dev) for v in (x, w, b, c0))
+    jc.ops.linear_device(tx, tw, tb, tc, flags, precision=precision)
+    jc.ops.device_sync(0)
+    got = tc.cpu().numpy()
+    exp = (torch.from_numpy(x).double() @ torch.from_numpy(w).double().T)
+    if flags & 1:
+        exp = exp + torch.from_numpy(b).double()
+    if flags & 4:
+        exp = exp * torch.sigmoid(exp)
+    if flags & 2:
+        exp = exp + torch.from_numpy(c0).double()
+    err = oracle.rel_max_err(got, exp.numpy())
+    assert err < TOL[precision], f"{precision} {m}x{n}x{k} flags {flags}: {err:.3e}"
+
+
 def test_repeated_calls_reuse_scratch(jc):
     # growing and shrinking shapes through the same scratch slots, results stay exact
     for m, n, k in [(64, 64, 64), (700, 300, 520), (33, 17, 9), (700, 300, 520)]:

@@ -79,6 +79,19 @@ def test_tiny_model_matches_oracle(jc, tiny, precision, covariate_groups):
     np.testing.assert_array_equal(got, got2)
 
 
+@pytest.mark.parametrize("precision", ["bf16", "fp16"])
+def test_many_rows_on_cta_pair_tiles(jc, tiny, precision):
+    # 600 series × 18 tokens: the q|k|v|gate (fused RoPE and sigmoid) and SwiGLU GEMMs run on the two-CTA
+    # kernel's 256 × 256 tiles
+    c, w, model = tiny
+    b = mixed_block(c, series=600, covariate_groups=40, seed=21)
+    exp, _ = model.predict_block(b)
+    with ts.TimestralEngine(c, w, precision=precision) as eng:
+        got = ts.B200TimestralForward(eng).predict_block(b)
+    err = per_quantile_err(got, exp)
+    assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+
+
 def test_sharding_across_two_slots_matches_one(jc, tiny):
     # two engine slots on the same GPU exercise the shard/gather path of multi-GPU runs
     c, w, _ = tiny
