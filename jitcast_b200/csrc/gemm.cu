@@ -51,16 +51,6 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);  // warp 0 TMA, warp 1 MMA, warps
 // ---- epilogue helpers ---------------------------------------------------------------------
 // vec_ok levels: 2 = every pointer and pitch 32-byte aligned (256-bit accesses, whole 32-byte
 // sectors), 1 = 16-byte aligned, 0 = scalar.
-__device__ __forceinline__ float apply_act(int act, float v) {
-  switch (act) {
-    case kActSilu: return silu_f(v);
-    case kActRelu: return fmaxf(v, 0.0f);
-    case kActGelu: return gelu_f(v);
-    case kActSigmoid: return sigmoid_f(v);
-    case kActSiluRelu: return fmaxf(silu_f(v), 0.0f);
-    default: return v;
-  }
-}
 
 __device__ __forceinline__ void st8_f32(float* p, const float* v) {
   asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
@@ -213,9 +203,29 @@ __device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int
     for (int j = 0; j < 32; ++j) v[j] *= s;
   }
   if (p.bias_on) add_bias(p, col0, nv, v);
-  if (p.act != kActNone) {
+  switch (p.act) {  // one branch per chunk, not per element
+    case kActSilu:
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = apply_act(p.act, v[j]);
+      for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+      break;
+    case kActRelu:
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(v[j], 0.0f);
+      break;
+    case kActGelu:
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = gelu_f(v[j]);
+      break;
+    case kActSigmoid:
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = sigmoid_f(v[j]);
+      break;
+    case kActSiluRelu:
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fmaxf(silu_f(v[j]), 0.0f);
+      break;
+    default:
+      break;
   }
   if (p.accumulate) {
     const float* src = p.cin + (long long)orow * p.ldcin + col0;
