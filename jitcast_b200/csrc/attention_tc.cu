@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   float* tq = reinterpret_cast<float*>(qs);                 // [kTailQ][64]
   float* tsc = tq + kTailQ * 64;                            // [kTailQ][kTcMaxTokens]
   float* tl = tsc + kTailQ * kTcMaxTokens;                  // [kTailQ]
+  float* tred = tl + kTailQ;                                // [kTcThreads][8] partial P·V sums
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hh = blockIdx.x % a.heads;
@@ -270,14 +271,39 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
         if (lane == 0) tl[j] = l;
       }
       __syncthreads();
+      // P·V: a thread owns 8 dims (one 16-byte chunk of a V row) of one query over every G-th key; the G
+      // partial sums are then added in a fixed order
+      const int items = nt * 8;
+      const int groups = kTcThreads / items;  // ≥ 2 for nt ≤ kTailQ
+      if (tid < items * groups) {
+        const int item = tid % items, g = tid / items;
+        const int j = item >> 3, c = item & 7;
+        const float* pj = tsc + j * kTcMaxTokens;
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
+        for (int k = g; k < sh.nkl; k += groups) {
+          const float p = pj[k];
+          if (p != 0.0f) {
+            const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(k, 8 * c));
+            const float2 v0 = unpack2<__half>(vv.x), v1 = unpack2<__half>(vv.y), v2 = unpack2<__half>(vv.z),
+                         v3 = unpack2<__half>(vv.w);
+            acc[0] = fmaf(p, v0.x, acc[0]), acc[1] = fmaf(p, v0.y, acc[1]);
+            acc[2] = fmaf(p, v1.x, acc[2]), acc[3] = fmaf(p, v1.y, acc[3]);
+            acc[4] = fmaf(p, v2.x, acc[4]), acc[5] = fmaf(p, v2.y, acc[5]);
+            acc[6] = fmaf(p, v3.x, acc[6]), acc[7] = fmaf(p, v3.y, acc[7]);
+          }
+        }
+        float4* red = reinterpret_cast<float4*>(tred + (g * items + item) * 8);
+        red[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        red[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      }
+      __syncthreads();
       for (int i = tid; i < nt * 64; i += kTcThreads) {
         const int j = i >> 6, e = i & 63;
-        const float* pj = tsc + j * kTcMaxTokens;
+        const int item = j * 8 + (e >> 3);
         float o = 0.0f;
-        for (int k = 0; k < sh.nkl; ++k) {
-          const float p = pj[k];
-          if (p != 0.0f) o = fmaf(p, __half2float(*reinterpret_cast<const __half*>(vs + sw128(k, e))), o);
-        }
+        for (int g = 0; g < groups; ++g) o += tred[(g * items + item) * 8 + (e & 7)];
         const float l = tl[j];
         o *= l > 0.0f ? 1.0f / l : 0.0f;
         const long long tok = row0 + t0 + j;

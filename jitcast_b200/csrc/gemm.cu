@@ -260,15 +260,21 @@ __device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int
   }
 }
 
-// Pulls the thread's share of a tile's residual input (the 128-byte lines of its row in the tile's columns it
-// will add) into L2, issued before the epilogue waits for the tile's accumulator so that the HBM reads
-// overlap the tile's MMAs instead of the epilogue.
+// Pulls what the thread's epilogue of a tile will read from memory into L2 — the residual input (the 128-byte
+// lines of its row in the tile's columns it will add) or its row's RoPE table entries — issued before the
+// epilogue waits for the tile's accumulator so that those reads overlap the tile's MMAs.
 template <int BN>
 __device__ __forceinline__ void prefetch_residual(const EpiParams& p, int M, int N, int m0, int n0, int row_in_tile,
                                                   int half) {
-  if (!p.accumulate || p.mode != kEpiPlain) return;
   const int row = m0 + row_in_tile;
   if (row >= M) return;
+  if (p.mode == kEpiQKV && n0 < p.rope_cols) {
+    // the row's RoPE table entries (cos and sin halves), fetched into L2 while the tile's MMAs run
+    const float* tc = p.rope_table + (long long)p.pos[row] * p.head_dim;
+    for (int off = 0; off < p.head_dim; off += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(tc + off));
+    return;
+  }
+  if (!p.accumulate || p.mode != kEpiPlain) return;
   const int rr = row % p.rg;
   const int orow = (row / p.rg) * p.rg_stride + rr + p.rg_off + (rr >= p.rg_split ? p.rg_shift : 0);
   const float* base = p.cin + (long long)orow * p.ldcin;
