@@ -287,6 +287,19 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams& p, int M, int
     }
 }
 
+// Two 32-column chunks of the thread's accumulator row with a single wait, so their TMEM latencies overlap.
+__device__ __forceinline__ void load_chunk_pair(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(ta, ra);
+  tmem_ld_32x32b_x32(tb, rb);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    a[j] = __uint_as_float(ra[j]);
+    b[j] = __uint_as_float(rb[j]);
+  }
+}
+
 __device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   tmem_ld_32x32b_x32(taddr, r);
@@ -340,8 +353,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
       const int col0 = n0 + 64 * u;
       if (col0 >= N) break;
       float a[32], b[32];
-      load_chunk(tbase + 64 * u, a);
-      load_chunk(tbase + 64 * u + 32, b);
+      load_chunk_pair(tbase + 64 * u, tbase + 64 * u + 32, a, b);
       if (!live) continue;
       if (p.bias_on) {
         add_bias(p, col0, 32, a);
@@ -362,8 +374,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
         const int ca = h0 + s, cb = h0 + hh + s;
         if (n0 + ca >= N) break;
         float a[32], b[32];
-        load_chunk(tbase + ca, a);
-        load_chunk(tbase + cb, b);
+        load_chunk_pair(tbase + ca, tbase + cb, a, b);
         if (!live) continue;
         if (p.bias_on) {
           add_bias(p, n0 + ca, 32, a);
@@ -565,6 +576,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
+      // the next tile's residual / table lines, a whole epilogue ahead of their use
+      const int tn = t + gridDim.x;
+      if (tn < tiles) prefetch_residual<BN>(ep, M, N, (tn / n_blks) * C::BM, (tn % n_blks) * BN, row_in_tile, half);
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
       epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile, half);
       tc_fence_before();
@@ -758,6 +772,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      const int tn = t + pairs;
+      if (tn < tiles)
+        prefetch_residual<BN>(ep, M, N, (tn / n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM,
+                              (tn % n_blks) * BN, row_in_tile, half);
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
       epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile, half);
       tc_fence_before();
