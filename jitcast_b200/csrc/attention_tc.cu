@@ -336,9 +336,14 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
       uint32_t r[32];
       tmem_ld_32x32b_x32(lane_base + 32 * c, r);
       tmem_ld_wait();
+      if (__all_sync(0xffffffffu, mw == ~0u)) {  // every key of the chunk open to every query of the warp
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if ((mw >> j) & 1u) mx = fmaxf(mx, __uint_as_float(r[j]));
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if ((mw >> j) & 1u) mx = fmaxf(mx, __uint_as_float(r[j]));
+      }
     }
     const float mo = mx == -INFINITY ? 0.0f : mx * sl2;
 #pragma unroll
@@ -350,12 +355,22 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
         uint32_t r[32];
         tmem_ld_32x32b_x32(lane_base + 32 * c, r);
         tmem_ld_wait();
+        if (__all_sync(0xffffffffu, mw == ~0u)) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float p0 = (mw >> j) & 1u ? ex2f(fmaf(__uint_as_float(r[j]), sl2, -mo)) : 0.0f;
-          const float p1 = (mw >> (j + 1)) & 1u ? ex2f(fmaf(__uint_as_float(r[j + 1]), sl2, -mo)) : 0.0f;
-          l += p0 + p1;
-          pk[j >> 1] = pack2<__half>(p0, p1);
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 = ex2f(fmaf(__uint_as_float(r[j]), sl2, -mo));
+            const float p1 = ex2f(fmaf(__uint_as_float(r[j + 1]), sl2, -mo));
+            l += p0 + p1;
+            pk[j >> 1] = pack2<__half>(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const float p0 = (mw >> j) & 1u ? ex2f(fmaf(__uint_as_float(r[j]), sl2, -mo)) : 0.0f;
+            const float p1 = (mw >> (j + 1)) & 1u ? ex2f(fmaf(__uint_as_float(r[j + 1]), sl2, -mo)) : 0.0f;
+            l += p0 + p1;
+            pk[j >> 1] = pack2<__half>(p0, p1);
+          }
         }
       } else {
 #pragma unroll
