@@ -35,6 +35,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "series forecasts/sec (Timestral-style config-3 model, box-scale batch of config 5)"
+GEMM_BYTES_PER_LAUNCH_1024 = 1.674e9
 UNIT = "series/s"
 
 
@@ -277,10 +278,10 @@ def main():
     pk, pk_kind = peaks()
     peak_tf = pk.get("bf16_tflops_sustained", 1400.0)
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
-    traffic = None
-    tf = ROOT / "profiles" / "gemm_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+    # DRAM bytes (read + written) per GEMM launch, from one ncu capture of every GEMM launch of a 1,024-series
+    # forward (dram__bytes_read.sum + dram__bytes_write.sum: 113.9 GB over 68 launches = 1.674 GB each, FP16
+    # operands), scaled by the chunk's series: the activations are all but a few MB of it and grow with the rows.
+    traffic = GEMM_BYTES_PER_LAUNCH_1024 * min(args.chunk, per_rank) / 1024.0 if args.precision == "fp16" else None
 
     if rank != 0:
         engine.close()
@@ -302,7 +303,7 @@ def main():
                     "d2h_bytes_per_step": d2h // args.steps},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic,
-                         "kernel": "gemm_tc_kernel (tcgen05, all linear layers)",
+                         "kernel": "gemm_pair_kernel / gemm_tc_kernel (tcgen05, all linear layers)",
                          "peak_kind": f"{pk_kind} bf16 dense, sustained",
                          "gemm_time_share": total_gemm_share},
             "cpu_baseline": cpu, "clocks": clocks.summary(),
