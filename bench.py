@@ -16,6 +16,8 @@ chunk shape). Prints one JSON line on rank 0:
               Java and no JDK exists here) on a bounded sample, rank 0 at N = 1.
 
 ``--impl reference`` times that CPU forward on the host cores instead (rank 0; other ranks exit).
+``--workload config2|config4`` times BASELINE configs 2 (Chronos-2, 256 series) and 4 (TiRex-2, 512 series) on one
+GPU with the same rules (a step is one forward of the config's batch).
 """
 
 from __future__ import annotations
@@ -57,6 +59,9 @@ def parse():
     ap.add_argument("--precision", default="fp16", choices=["fp16", "bf16", "tf32", "fp32"])
     ap.add_argument("--cpu-series", type=int, default=2, help="series in the CPU baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="config5", choices=["config5", "config2", "config4"],
+                    help="config5 (default: the headline box-scale Timestral batch), config2 (Chronos-2, 256 "
+                         "series) or config4 (TiRex-2, 512 series), one GPU")
     return ap.parse_args()
 
 
@@ -162,6 +167,144 @@ def reference_arm(args, rank, world):
     return 0
 
 
+# GEMM FLOPs per series of one forward (2·M·K·N over the model's linear layers; SURVEY-style accounting of the
+# configs: Chronos-2 config 2 with 128 context + [REG] + 4 future tokens, TiRex-2 config 4 with headwise gates)
+WORKLOAD_GEMM_FLOPS = {"config2": 30.82e9, "config4": 5.02e9}
+
+
+def engine_profile(L, handle):
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    cap = 32
+    names = (ctypes.c_char_p * cap)()
+    ms = (ctypes.c_double * cap)()
+    launches = (ctypes.c_longlong * cap)()
+    flops = (ctypes.c_double * cap)()
+    n = ctypes.c_int()
+    _lib.check(L.jc_engine_profile(handle, 0, names, ms, launches, flops, cap, ctypes.byref(n)))
+    return {names[i].decode(): {"ms": ms[i], "launches": launches[i], "flops": flops[i]} for i in range(n.value)}
+
+
+def workload_bench(args, world):
+    """Configs 2 and 4 on one GPU, with config 5's timing rules: a step is one forward of the config's batch."""
+    import ctypes
+
+    import torch
+
+    from jitcast_b200 import _lib
+    from jitcast_b200 import workloads
+
+    if world > 1:
+        print(json.dumps({"error": f"--workload {args.workload} runs on one GPU"}))
+        return 2
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    L = _lib.lib()
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    if args.workload == "config2":
+        from jitcast_b200 import chronos2 as c2
+
+        cfg = c2.config2()
+        batch = 256
+        weights = c2.random_checkpoint(cfg, seed=0)
+        engine = c2.Chronos2Engine(cfg, weights, precision=args.precision)
+        x = workloads.random_walk(batch, 2048, seed=0)
+        inp = c2.ModelInput(x, np.arange(batch, dtype=np.int32), 4)
+        lay = c2.ModelLayout.of(cfg, inp)
+        prep = c2.ModelPrep.of(cfg, lay)
+        gs, ge = c2.group_ranges(np.asarray(inp.group))
+        d = {"tok": t(np.asarray(prep.tokens, np.float32)), "live": t(np.asarray(lay.live, np.int32)),
+             "gs": t(gs), "ge": t(ge)}
+        out = torch.empty(lay.rows * lay.output_patches, cfg.num_quantiles * cfg.patch_size, device=dev)
+        blk = c2.Block(lay.rows, lay.context_patches, lay.output_patches, d["tok"].data_ptr(), d["live"].data_ptr(),
+                       d["gs"].data_ptr(), d["ge"].data_ptr())
+        device_fwd = lambda: L.jc_forward_chronos2_device(engine.handle, 0, ctypes.byref(blk), out.data_ptr(),
+                                                          stream.cuda_stream)
+        host_fwd = lambda: engine.forward_raw(lay, prep, gs, ge)
+        h2d = prep.tokens.nbytes + np.asarray(lay.live, np.int32).nbytes + gs.nbytes + ge.nbytes
+        d2h = out.numel() * 4
+        desc = ("config2: Chronos-2-style T5 encoder (d 768, 12 layers, 12 heads, d_ff 3072 ReLU, patch 16, 128 "
+                "context + [REG] + 4 future tokens, 21 quantiles), random-init weights")
+        data = "synthetic random walks x_t = x_{t-1} + N(0,1), seed 0"
+    else:
+        from jitcast_b200 import tirex2 as tx
+
+        cfg = tx.config4()
+        batch = 512
+        weights = tx.random_checkpoint(cfg, seed=0)
+        engine = tx.TiRex2Engine(cfg, weights, precision=args.precision)
+        x = workloads.ar2(batch, cfg.padded_length, seed=0)
+        x[:, cfg.context_len:] = np.nan
+        b = tx.ModelBatch(x, np.arange(batch, dtype=np.float32), np.ones(batch, bool))
+        di = tx.DeviceInputs.of(cfg, b)
+        st = di.st
+        d = {k: t(v) for k, v in dict(x=di.x, present=di.present, known=st.known, kept=st.kept, gs=st.group_start,
+                                     ge=st.group_end, kt=st.kept_target).items()}
+        out = torch.empty(batch, cfg.num_quantiles, cfg.padded_length, device=dev)
+        blk = tx.Batch(batch, d["x"].data_ptr(), d["present"].data_ptr(), len(st.known), d["known"].data_ptr(),
+                       len(st.kept), d["kept"].data_ptr(), d["gs"].data_ptr(), d["ge"].data_ptr(), d["kt"].data_ptr())
+        device_fwd = lambda: L.jc_forward_tirex2_device(engine.handle, 0, ctypes.byref(blk), out.data_ptr(),
+                                                        stream.cuda_stream)
+        host_fwd = lambda: engine.forward_inputs(di)
+        h2d = di.x.nbytes + di.present.nbytes
+        d2h = out.numel() * 4
+        desc = ("config4: TiRex-style xLSTM stack (d 512, 12 blocks, sLSTM at 3, 7, 11, 4 heads, patch 32, 64 "
+                "patches, 9 quantiles, input/output FF 2048), random-init weights")
+        data = "synthetic AR(2) phi1 0.6 phi2 0.3 sigma 1, 200-step burn-in, seed 0"
+    for _ in range(max(args.warmup, 3)):
+        _lib.check(device_fwd())
+    torch.cuda.synchronize()
+    engine.sync()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            _lib.check(device_fwd())
+        stop.record(stream)
+        torch.cuda.synchronize()
+    engine.sync()
+    ms = start.elapsed_time(stop) / args.steps
+    host_fwd()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        host_fwd()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    engine.set_option("profile", 1)
+    _lib.check(device_fwd())
+    torch.cuda.synchronize()
+    prof = engine_profile(L, engine.handle)
+    engine.set_option("profile", 0)
+    gemms = {k: v for k, v in prof.items() if k.startswith("gemm")}
+    g = {f: sum(v[f] for v in gemms.values()) for f in ("ms", "launches", "flops")}
+    pk, pk_kind = peaks()
+    peak_tf = pk.get("bf16_tflops_sustained", 1400.0)
+    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] else 0.0
+    line = {"metric": f"series forecasts/sec ({args.workload})", "value": batch / (ms / 1000.0), "unit": UNIT,
+            "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.precision,
+            "data": data, "config": {"workload": desc, "series_per_step": batch, "precision": args.precision,
+                                     "l2": "no flush: every forward's working set is far larger than the L2"},
+            "e2e": {"value": batch / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tf, "traffic": None,
+                         "kernel": "gemm_pair_kernel / gemm_tc_kernel (tcgen05, all linear layers)",
+                         "peak_kind": f"{pk_kind} bf16 dense, sustained",
+                         "gemm_time_share": g["ms"] / sum(v["ms"] for v in prof.values()),
+                         "gemm_flops_per_series": WORKLOAD_GEMM_FLOPS[args.workload]},
+            "cpu_baseline": None, "clocks": clocks.summary(),
+            "gpu_launches": sum(v["launches"] for v in prof.values()) * args.steps,
+            "kernel_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
+                                   **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {})}
+                               for k, v in prof.items()}}
+    print(json.dumps(line), flush=True)
+    engine.close()
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", 0))
@@ -169,6 +312,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.workload != "config5":
+        return workload_bench(args, world)
 
     import ctypes
     import datetime

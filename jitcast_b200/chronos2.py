@@ -379,6 +379,9 @@ class Chronos2Engine:
     def set_option(self, key: str, value: int) -> None:
         check(_lib.lib().jc_engine_set_option(self.handle, key.encode(), int(value)))
 
+    def sync(self) -> None:
+        check(_lib.lib().jc_engine_sync(self.handle))
+
     def close(self) -> None:
         if self._h:
             _lib.lib().jc_engine_destroy(self._h)
