@@ -30,6 +30,28 @@ __device__ __forceinline__ float ld_gate(const AttnArgs& a, long long i) {
   return static_cast<const float*>(a.gate)[i];
 }
 
+template <typename T>
+__device__ __forceinline__ float2 h2f2(uint32_t u);
+template <>
+__device__ __forceinline__ float2 h2f2<__half>(uint32_t u) { return __half22float2(*reinterpret_cast<__half2*>(&u)); }
+template <>
+__device__ __forceinline__ float2 h2f2<__nv_bfloat16>(uint32_t u) {
+  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t f22h(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t f22h<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(fminf(fmaxf(a, -65504.0f), 65504.0f), fminf(fmaxf(b, -65504.0f), 65504.0f));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t f22h<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 __device__ __forceinline__ void put_op(int kind, void* hi, void* lo, long long i, float v) {
   switch (kind) {
     case kOutBF16: static_cast<__nv_bfloat16*>(hi)[i] = __float2bfloat16_rn(v); break;
@@ -186,6 +208,114 @@ __global__ void variate_attention_kernel(AttnArgs a) {
       if (a.gate) v *= ld_gate(a, go + e);
       put_op(a.out_kind, a.out_hi, a.out_lo, o + e, v);
     }
+  }
+}
+
+// The same attention for 16-bit q/k/v/gate/output, vectorised: DH / 8 threads per (row, slot, head), each
+// owning 8 dims read and written as one 16-byte vector, so an item's q, k, v and output rows are single
+// coalesced 128-byte (DH 64) segments. Dot products are reduced across the item's threads with shuffles.
+template <typename T, int DH>
+__global__ void variate_attention_vec_kernel(AttnArgs a) {
+  constexpr int TPI = DH / 8;  // threads per item: 8 (DH 64) or 4 (DH 32), a power of two dividing 32
+  const long long items = (long long)a.rows * a.n * a.heads;
+  const T* qkv = static_cast<const T*>(a.qkv);
+  const int sub = threadIdx.x % TPI;
+  const long long stride = (long long)gridDim.x * blockDim.x / TPI;
+  for (long long id = (blockIdx.x * (long long)blockDim.x + threadIdx.x) / TPI;; id += stride) {
+    // the loop bound is per group of TPI lanes; whole warps leave together only at the end, so the
+    // shuffles below always have every lane of the warp present
+    const bool active = id < items;
+    if (!__any_sync(0xffffffffu, active)) break;
+    const long long item = active ? id : 0;
+    const int hh = static_cast<int>(item % a.heads);
+    const int t = static_cast<int>((item / a.heads) % a.n);
+    const int i = static_cast<int>(item / ((long long)a.heads * a.n));
+    const int gs = active ? a.group_start[i] : 0, ge = active ? a.group_end[i] : 0;
+    const long long row_i = (long long)i * a.n + t;
+    float q[8], acc[8];
+    {
+      const uint4 u = *reinterpret_cast<const uint4*>(qkv + row_i * a.ld_qkv + hh * DH + 8 * sub);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float2 f = h2f2<T>(w[c]);
+        q[2 * c] = f.x * a.scale;
+        q[2 * c + 1] = f.y * a.scale;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    // every lane of the warp runs the same number of iterations (the longest group among its items)
+    int gmax = ge - gs;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) gmax = max(gmax, __shfl_xor_sync(0xffffffffu, gmax, off));
+    for (int jj = 0; jj < gmax; ++jj) {
+      const int j = gs + jj;
+      bool ok = active && j < ge;
+      if (ok) {
+        if (a.mask_mode == 1) {
+          ok = a.live[(long long)j * a.n + t] != 0;
+        } else if (j != i) {
+          if (t < a.enc && !a.key_valid[(long long)j * a.enc + t]) ok = false;
+          if (ok && a.covariates) {
+            if (a.role[i] != 0 && a.role[j] == 0) ok = false;
+            if (a.role[i] == 2 && a.role[j] != 2) ok = false;
+          }
+        }
+      }
+      float kv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, vv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (ok) {
+        const T* kp = qkv + ((long long)j * a.n + t) * a.ld_qkv + a.d + hh * DH + 8 * sub;
+        const uint4 uk = *reinterpret_cast<const uint4*>(kp);
+        const uint4 uv = *reinterpret_cast<const uint4*>(kp + a.d);
+        const uint32_t wk[4] = {uk.x, uk.y, uk.z, uk.w}, wv[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float2 fk = h2f2<T>(wk[c]), fv = h2f2<T>(wv[c]);
+          kv[2 * c] = fk.x, kv[2 * c + 1] = fk.y, vv[2 * c] = fv.x, vv[2 * c + 1] = fv.y;
+        }
+      }
+      float sdot = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sdot = fmaf(q[e], kv[e], sdot);
+#pragma unroll
+      for (int off = TPI / 2; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
+      if (!ok) continue;  // lanes of one item agree on ok (same i, j, t)
+      if (sdot > m) {
+        const float corr = __expf(m - sdot);
+        l *= corr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] *= corr;
+        m = sdot;
+      }
+      const float p = __expf(sdot - m);
+      l += p;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(p, vv[e], acc[e]);
+    }
+    if (!active) continue;
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;  // no live row in the group: zeros
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = acc[e] * inv;
+    if (a.gate) {
+      const uint4 ug = *reinterpret_cast<const uint4*>(static_cast<const T*>(a.gate) + row_i * a.ld_gate + hh * DH +
+                                                       8 * sub);
+      const uint32_t wg[4] = {ug.x, ug.y, ug.z, ug.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float2 g = h2f2<T>(wg[c]);
+        o[2 * c] *= g.x;
+        o[2 * c + 1] *= g.y;
+      }
+    }
+    uint4 out;
+    out.x = f22h<T>(o[0], o[1]);
+    out.y = f22h<T>(o[2], o[3]);
+    out.z = f22h<T>(o[4], o[5]);
+    out.w = f22h<T>(o[6], o[7]);
+    *reinterpret_cast<uint4*>(static_cast<T*>(a.out_hi) + row_i * a.ld_out + hh * DH + 8 * sub) = out;
   }
 }
 
@@ -461,6 +591,23 @@ cudaError_t launch_time_t(const AttnArgs& a, cudaStream_t s) {
 
 template <typename T>
 cudaError_t launch_variate_t(const AttnArgs& a, cudaStream_t s) {
+  if constexpr (!std::is_same<T, float>::value) {
+    const bool vec = !a.cuda_cores && a.out_kind == a.qkv_kind && (!a.gate || a.gate_kind == a.qkv_kind) &&
+                     (a.head_dim == 64 || a.head_dim == 32) && a.ld_qkv % 8 == 0 && a.d % 8 == 0 &&
+                     a.ld_out % 8 == 0 && (!a.gate || a.ld_gate % 8 == 0) &&
+                     (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.out_hi) & 15) == 0 &&
+                     (!a.gate || (reinterpret_cast<uintptr_t>(a.gate) & 15) == 0);
+    if (vec) {
+      const long long threads = (long long)a.rows * a.n * a.heads * (a.head_dim / 8);
+      long long blocks = (threads + 255) / 256;
+      if (blocks > 148 * 16) blocks = 148 * 16;
+      if (a.head_dim == 64)
+        variate_attention_vec_kernel<T, 64><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+      else
+        variate_attention_vec_kernel<T, 32><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a);
+      return cudaGetLastError();
+    }
+  }
   const long long total = (long long)a.rows * a.n * a.heads;
   long long blocks = (total + 127) / 128;
   if (blocks > 148 * 32) blocks = 148 * 32;
