@@ -22,11 +22,21 @@ enum DeviceError : uint32_t {
   kErrTimeoutAcc = 1u << 2,    // epilogue waited too long for an accumulator
   kErrTimeoutAccFree = 1u << 3,// MMA issuer waited too long for the epilogue
   kErrTimeoutFlag = 1u << 4,   // a flag wait (tests of the bounded-wait path)
+  kErrTimeoutPeer = 1u << 5,   // a recurrent cell waited too long for its cluster peers' state
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// 16-byte asynchronous global-to-shared copy through L2 only; src_bytes 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
@@ -190,6 +200,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
+}
+
+// Two floats stored asynchronously into a peer CTA's shared memory; the store's 8 bytes complete on the
+// peer's mbarrier `bar` (both shared::cluster addresses, from mapa_shared).
+__device__ __forceinline__ void st_async_v2(uint32_t addr, float2 v, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(v.x), "f"(v.y), "r"(bar)
+               : "memory");
+}
+
+// Two floats stored at a shared::cluster address (a peer CTA's shared memory, from mapa_shared).
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+
+// Four floats stored at a shared::cluster address (a peer CTA's shared memory, from mapa_shared).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
 }
 
 // Every thread of both CTAs: release this CTA's prior shared-memory writes to the cluster and wait

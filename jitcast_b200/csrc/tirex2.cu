@@ -20,6 +20,7 @@
 // dispatch (:910-1085) and TiRexKernels (scalePatch :48, mlstmChunk :283, slstmRecurrence* :447-700,
 // headLayerNorm :133, gather/scatter/concat :1004-1036, qkNorm :1065, variateAttention :1110, unpatch
 // :979); the arithmetic is CpuReference.forward's (tirex2/cpu/CpuReference.java:67-266, Cells.java).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <thread>
@@ -27,6 +28,7 @@
 #include "engine.h"
 #include "kernels.cuh"
 #include "opstore.cuh"
+#include "ptx.cuh"
 #include "runtime.h"
 
 namespace jc {
@@ -126,219 +128,350 @@ __device__ __forceinline__ float soft_cap(float z) {
   return static_cast<float>(static_cast<double>(kGateCap) * tanh(static_cast<double>(z / kGateCap)));
 }
 
-constexpr int kMlT = 64;       // query and key tokens per block
-constexpr int kMlThreads = 256;
-constexpr int kMlPad = kMlT + 1;
+constexpr int kMlT = 64;          // query and key tokens per block
+constexpr int kMlThreads = 256;   // 16 × 16: ty owns 4 query tokens, tx 4 keys (q·k) or 8 value dims (C·v)
+constexpr int kMlPitch = kMlT + 4;  // q, k and C row pitch in floats: 16-byte rows, conflict-free 128-bit reads
 
 // Dynamic shared memory of the mLSTM kernel for a sequence of S tokens.
 size_t mlstm_smem(int S) {
-  return sizeof(float) * (kMlT * kMlPad * 3 + kMlT * kDv) + sizeof(double) * 2 * S;
+  return sizeof(float) * (3 * kMlT * kMlPitch + kMlT * kDv) + sizeof(double) * (2 * S + 2 * kMlT);
+}
+
+// Starts the asynchronous copy of a 64-token × W-float slab of proj (token rows t0.., zeros past S) into
+// shared memory with row pitch P.
+template <int W, int P>
+__device__ __forceinline__ void mlstm_stage(float* dst, const float* __restrict__ src, long long ldp, int t0, int S) {
+  constexpr int V = W / 4, N = kMlT * V / kMlThreads;
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    const int i = threadIdx.x + k * kMlThreads, t = i / V, c = i % V;
+    const bool in = t0 + t < S;
+    cp_async16(dst + t * P + 4 * c, in ? src + (t0 + t) * ldp + 4 * c : src, in ? 16 : 0);
+  }
 }
 
 // The stabilised parallel mLSTM of one (row, head, 64-query block) (Cells.mlstmCore, Cells.java:74-118)
 // with Cells.mlstm's per-head LayerNorm and σ(o) gate (:58-69) as its epilogue. proj [(r·S + t), ldp]
-// holds q (heads·64) | k (heads·64) | v (heads·128) | o (heads·128) | i (heads) | f (heads).
+// (ldp a multiple of 4, 16-byte aligned) holds q (heads·64) | k (heads·64) | v (heads·128) | o (heads·128) |
+// i (heads) | f (heads).
 //   F[t] = Σ_{u≤t} logσ(cap(f_u)),  a[s] = cap(i_s) − F[s],  M[t] = max(0, max_{s≤t} a[s]),  m[t] = F[t] + M[t]
 //   C[t,s] = (q_t·k_s)/8 · exp(a[s] − M[t])   (= exp(F[t] − F[s] + i_s − m[t]), s ≤ t)
 //   h_t = Σ_s C[t,s] v_s / (max(|Σ_s C[t,s]|, exp(−m[t])) + eps)
-// Keys stream through shared memory 64 at a time, so any S fits.
-__global__ void __launch_bounds__(kMlThreads) mlstm_kernel(const float* __restrict__ proj, long long ldp, int rows,
-                                                           int S, int heads, const float* __restrict__ norm_w,
-                                                           int out_kind, void* out_hi, void* out_lo, long long ld_out) {
+// The gate transcendentals run one token per thread while q, k and v copy in; warp 0 then scans them
+// (double, 32 tokens per step with a carry). Keys stream through shared memory 64 at a time, so any S fits. Both products are register-tiled from 16-byte shared-memory reads: q·k as
+// 4 tokens × 4 keys per thread, C·v as 4 tokens × 8 value dims, the latter stopping at the warp's last
+// token on the diagonal block.
+__global__ void __launch_bounds__(kMlThreads, 2) mlstm_kernel(const float* __restrict__ proj, long long ldp, int rows,
+                                                              int S, int heads, const float* __restrict__ norm_w,
+                                                              int out_kind, void* out_hi, void* out_lo, long long ld_out) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
-  float* qs = reinterpret_cast<float*>(sm_raw);  // [64][65]
-  float* ks = qs + kMlT * kMlPad;               // [64][65]
-  float* cs = ks + kMlT * kMlPad;               // [64][65]
-  float* vs = cs + kMlT * kMlPad;               // [64][128]
-  double* cumf = reinterpret_cast<double*>(vs + kMlT * kDv);  // [S]: F, then reused
-  double* aa = cumf + S;                                       // [S]: a[s], then prefix max
-  const int rh = blockIdx.x;
-  const int r = rh / heads, head = rh % heads;
-  const int qb = blockIdx.y;
-  const int tid = threadIdx.x;
+  float* qs = reinterpret_cast<float*>(sm_raw);  // [64 t][68]
+  float* ks = qs + kMlT * kMlPitch;             // [64 s][68]
+  float* cs = ks + kMlT * kMlPitch;             // [64 s][68]: C transposed (key-major)
+  float* vs = cs + kMlT * kMlPitch;             // [64 s][128]
+  double* aa = reinterpret_cast<double*>(vs + kMlT * kDv);  // [S]: cap(i_s), then a[s]
+  double* lf = aa + S;                                       // [S]: logσ(cap(f_s))
+  double* fq = lf + S;                                       // [64]: F[t] of the query block
+  double* mq = fq + kMlT;                                    // [64]: M[t] of the query block
+  const int r = blockIdx.x / heads, head = blockIdx.x % heads;
+  const int qb = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ty = tid >> 4, tx = tid & 15;
   if (r >= rows) return;
-  const long long row0 = static_cast<long long>(r) * S;
+  const float* base = proj + static_cast<long long>(r) * S * ldp;
   const int k_off = heads * kDqk, v_off = 2 * heads * kDqk, o_off = v_off + heads * kDv, i_off = o_off + heads * kDv,
             f_off = i_off + heads;
-  // gates over the whole prefix this query block needs
-  const int t_end = min(S, (qb + 1) * kMlT);
+  const int q0 = qb * kMlT;
+  const int t_end = min(S, q0 + kMlT);  // the gates of every key this query block reads
+  // q and the first key block's k, v in flight while the gates are computed; the epilogue's o rows
+  // (64 tokens × 512 bytes, one 128-byte line per thread) are pulled into L2
+  mlstm_stage<kDqk, kMlPitch>(qs, base + head * kDqk, ldp, q0, S);
+  mlstm_stage<kDqk, kMlPitch>(ks, base + k_off + head * kDqk, ldp, 0, S);
+  mlstm_stage<kDv, kDv>(vs, base + v_off + head * kDv, ldp, 0, S);
+  cp_async_commit();
+  if (q0 + (tid >> 2) < S) prefetch_l2(base + (q0 + (tid >> 2)) * ldp + o_off + head * kDv + 32 * (tid & 3));
   for (int s = tid; s < t_end; s += kMlThreads) {
-    const float* ps = proj + (row0 + s) * ldp;
-    cumf[s] = log_sigmoid_d(static_cast<double>(soft_cap(ps[f_off + head])));
+    const float* ps = base + s * ldp;
+    lf[s] = log_sigmoid_d(static_cast<double>(soft_cap(ps[f_off + head])));
     aa[s] = static_cast<double>(soft_cap(ps[i_off + head]));
   }
   __syncthreads();
-  // inclusive prefix sum of F (Hillis-Steele over t_end ≤ S elements)
-  for (int off = 1; off < t_end; off <<= 1) {
-    double v[4];
-    int c = 0;
-    for (int s = tid; s < t_end; s += kMlThreads) v[c++] = s >= off ? cumf[s - off] : 0.0;
-    __syncthreads();
-    c = 0;
-    for (int s = tid; s < t_end; s += kMlThreads) cumf[s] += v[c++];
-    __syncthreads();
-  }
-  for (int s = tid; s < t_end; s += kMlThreads) aa[s] -= cumf[s];
-  __syncthreads();
-  // m[t] needs the prefix max of a; the key weights need a itself, kept in ks-sized scratch per key block
-  // below, so the prefix max goes into a second pass stored in cumf (F is only needed as F[t] + M[t]).
-  // First store F[t] for the query block's tokens, then overwrite cumf with the prefix max of a.
-  __shared__ double fq[kMlT];
-  for (int t = tid; t < kMlT; t += kMlThreads) fq[t] = qb * kMlT + t < S ? cumf[qb * kMlT + t] : 0.0;
-  __syncthreads();
-  for (int s = tid; s < t_end; s += kMlThreads) cumf[s] = aa[s];
-  __syncthreads();
-  for (int off = 1; off < t_end; off <<= 1) {
-    double v[4];
-    int c = 0;
-    for (int s = tid; s < t_end; s += kMlThreads) v[c++] = s >= off ? cumf[s - off] : -INFINITY;
-    __syncthreads();
-    c = 0;
-    for (int s = tid; s < t_end; s += kMlThreads) cumf[s] = fmax(cumf[s], v[c++]);
-    __syncthreads();
-  }
-  // query block
-  const int tq = tid >> 2, lq = tid & 3;
-  const int tglob = qb * kMlT + tq;
-  const bool tlive = tglob < S;
-  for (int i = tid; i < kMlT * kDqk; i += kMlThreads) {
-    const int t = i / kDqk, j = i % kDqk;
-    const int tg = qb * kMlT + t;
-    qs[t * kMlPad + j] = tg < S ? proj[(row0 + tg) * ldp + head * kDqk + j] : 0.0f;
-  }
-  const double Mt = tlive ? fmax(0.0, cumf[tglob]) : 0.0;
-  const double mt = tlive ? fq[tq] + Mt : 0.0;
-  float num[32];
+  // F and the prefix max of a, 32 tokens per step with a carry
+  if (warp == 0) {
+    double carry_f = 0.0, carry_m = -INFINITY;
+    for (int c0 = 0; c0 < t_end; c0 += 32) {
+      const int s = c0 + lane;
+      double F = s < t_end ? lf[s] : 0.0;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) num[i] = 0.0f;
-  float den = 0.0f;
-  const float scale = 0.125f;  // 1/√64
-  for (int kb = 0; kb <= qb; ++kb) {
-    __syncthreads();
-    for (int i = tid; i < kMlT * kDqk; i += kMlThreads) {
-      const int s = i / kDqk, j = i % kDqk;
-      const int sg = kb * kMlT + s;
-      ks[s * kMlPad + j] = sg < S ? proj[(row0 + sg) * ldp + k_off + head * kDqk + j] : 0.0f;
-    }
-    for (int i = tid; i < kMlT * kDv / 4; i += kMlThreads) {
-      const int s = i / (kDv / 4), j4 = i % (kDv / 4);
-      const int sg = kb * kMlT + s;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (sg < S) v = *reinterpret_cast<const float4*>(proj + (row0 + sg) * ldp + v_off + head * kDv + 4 * j4);
-      *reinterpret_cast<float4*>(vs + s * kDv + 4 * j4) = v;
-    }
-    __syncthreads();
-    // C[t, s] for this thread's token and keys s ≡ lq (mod 4)
-#pragma unroll 4
-    for (int i = 0; i < 16; ++i) {
-      const int s = lq + 4 * i;
-      const int sg = kb * kMlT + s;
-      float c = 0.0f;
-      if (tlive && sg <= tglob) {
-        float dot = 0.0f;
-#pragma unroll 16
-        for (int j = 0; j < kDqk; ++j) dot = fmaf(qs[tq * kMlPad + j], ks[s * kMlPad + j], dot);
-        c = dot * scale * expf(static_cast<float>(aa[sg] - Mt));
+      for (int off = 1; off < 32; off <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, F, off);
+        if (lane >= off) F += y;
       }
-      cs[tq * kMlPad + s] = c;
-      den += c;
+      F += carry_f;
+      carry_f = __shfl_sync(0xffffffffu, F, 31);
+      const double a = s < t_end ? aa[s] - F : -INFINITY;
+      double M = a;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, M, off);
+        if (lane >= off) M = fmax(M, y);
+      }
+      M = fmax(M, carry_m);
+      carry_m = __shfl_sync(0xffffffffu, M, 31);
+      if (s < t_end) {
+        aa[s] = a;
+        if (s >= q0) {
+          fq[s - q0] = F;
+          mq[s - q0] = fmax(0.0, M);
+        }
+      }
+    }
+  }
+  cp_async_wait_all();
+  const float scale = 0.125f;  // 1/√64
+  float num[4][8], den[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    den[a] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) num[a][e] = 0.0f;
+  }
+  __syncthreads();
+  for (int kb = 0; kb <= qb; ++kb) {
+    if (kb > 0) {
+      __syncthreads();  // the previous key block's k, v and C are consumed
+      mlstm_stage<kDqk, kMlPitch>(ks, base + k_off + head * kDqk, ldp, kb * kMlT, S);
+      mlstm_stage<kDv, kDv>(vs, base + v_off + head * kDv, ldp, kb * kMlT, S);
+      cp_async_commit();
+      cp_async_wait_all();
+      __syncthreads();
+    }
+    // C[t, s] for tokens 4ty + a and keys tx + 16b
+    {
+      float c[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) c[a][b] = 0.0f;
+#pragma unroll 4
+      for (int j = 0; j < kDqk; j += 4) {
+        float4 q4[4], k4[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) q4[a] = *reinterpret_cast<const float4*>(qs + (4 * ty + a) * kMlPitch + j);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) k4[b] = *reinterpret_cast<const float4*>(ks + (tx + 16 * b) * kMlPitch + j);
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            c[a][b] = fmaf(q4[a].x, k4[b].x, c[a][b]);
+            c[a][b] = fmaf(q4[a].y, k4[b].y, c[a][b]);
+            c[a][b] = fmaf(q4[a].z, k4[b].z, c[a][b]);
+            c[a][b] = fmaf(q4[a].w, k4[b].w, c[a][b]);
+          }
+      }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int sg = kb * kMlT + tx + 16 * b;
+        float w[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          const int tg = q0 + 4 * ty + a;
+          w[a] = tg < S && sg <= tg ? c[a][b] * scale * expf(static_cast<float>(aa[sg] - mq[4 * ty + a])) : 0.0f;
+          den[a] += w[a];
+        }
+        *reinterpret_cast<float4*>(cs + (tx + 16 * b) * kMlPitch + 4 * ty) = make_float4(w[0], w[1], w[2], w[3]);
+      }
     }
     __syncthreads();
-    // num[t, j] += Σ_s C[t, s] v[s, j] for j ≡ lq (mod 4)
-    for (int s = 0; s < kMlT; ++s) {
-      const float c = cs[tq * kMlPad + s];
+    // num[t, :] += Σ_s C[t, s] v[s, :] over dims 4tx.. and 64 + 4tx.. (C is zero past each token)
+    const int smax = kb == qb ? min(kMlT - 1, 8 * warp + 7) : kMlT - 1;
+    for (int s = 0; s <= smax; ++s) {
+      const float4 cc = *reinterpret_cast<const float4*>(cs + s * kMlPitch + 4 * ty);
+      const float4 v0 = *reinterpret_cast<const float4*>(vs + s * kDv + 4 * tx);
+      const float4 v1 = *reinterpret_cast<const float4*>(vs + s * kDv + 64 + 4 * tx);
+      const float cv[4] = {cc.x, cc.y, cc.z, cc.w};
+      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-      for (int i = 0; i < 32; ++i) num[i] = fmaf(c, vs[s * kDv + lq + 4 * i], num[i]);
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) num[a][e] = fmaf(cv[a], vv[e], num[a][e]);
     }
   }
-  den += __shfl_xor_sync(0xffffffffu, den, 1);
-  den += __shfl_xor_sync(0xffffffffu, den, 2);
-  const float norm = static_cast<float>(fmax(fabs(static_cast<double>(den)), exp(-mt)) + static_cast<double>(kMlstmEps));
-  float mean = 0.0f;
+  // epilogue per token: normaliser, LayerNorm over the head's 128 dims (16 lanes × 8), σ(o) gate
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    num[i] /= norm;
-    mean += num[i];
-  }
-  mean += __shfl_xor_sync(0xffffffffu, mean, 1);
-  mean += __shfl_xor_sync(0xffffffffu, mean, 2);
-  mean *= 1.0f / kDv;
-  float var = 0.0f;
+  for (int a = 0; a < 4; ++a) {
+    const int tl = 4 * ty + a, tg = q0 + tl;
+    float dn = den[a];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float dv = num[i] - mean;
-    var = fmaf(dv, dv, var);
-  }
-  var += __shfl_xor_sync(0xffffffffu, var, 1);
-  var += __shfl_xor_sync(0xffffffffu, var, 2);
-  var *= 1.0f / kDv;
-  const float inv = rsqrtf(var + kNormEps);
-  if (!tlive) return;
-  const float* og = proj + (row0 + tglob) * ldp + o_off + head * kDv;
-  const long long orow = (row0 + tglob) * ld_out + head * kDv;
+    for (int off = 1; off < 16; off <<= 1) dn += __shfl_xor_sync(0xffffffffu, dn, off);
+    const double mt = tg < S ? fq[tl] + mq[tl] : 0.0;
+    const float rnorm =
+        1.0f / static_cast<float>(fmax(fabs(static_cast<double>(dn)), exp(-mt)) + static_cast<double>(kMlstmEps));
+    float mean = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const int j = lq + 4 * i;
-    const float v = (num[i] - mean) * inv * norm_w[head * kDv + j];
-    const float g = 1.0f / (1.0f + expf(-og[j]));
-    put_op(out_kind, out_hi, out_lo, orow + j, g * v);
+    for (int e = 0; e < 8; ++e) {
+      num[a][e] *= rnorm;
+      mean += num[a][e];
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) mean += __shfl_xor_sync(0xffffffffu, mean, off);
+    mean *= 1.0f / kDv;
+    float var = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float dv = num[a][e] - mean;
+      var = fmaf(dv, dv, var);
+    }
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) var += __shfl_xor_sync(0xffffffffu, var, off);
+    var *= 1.0f / kDv;
+    const float inv = rsqrtf(var + kNormEps);
+    if (tg >= S) continue;
+    const float* og = base + tg * ldp + o_off + head * kDv;
+    const long long orow = (static_cast<long long>(r) * S + tg) * ld_out + head * kDv;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j0 = 64 * h + 4 * tx;
+      const float4 o4 = __ldg(reinterpret_cast<const float4*>(og + j0));
+      const float4 w4 = __ldg(reinterpret_cast<const float4*>(norm_w + head * kDv + j0));
+      const float ov[4] = {o4.x, o4.y, o4.z, o4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      float r4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v = (num[a][4 * h + e] - mean) * inv * wv[e];
+        const float g = 1.0f / (1.0f + expf(-ov[e]));
+        r4[e] = g * v;
+      }
+      put_op4(out_kind, out_hi, out_lo, orow + j0, make_float4(r4[0], r4[1], r4[2], r4[3]));
+    }
   }
 }
 
-constexpr int kSlRows = 16;  // rows per block: one warp per row in the state update
-constexpr int kSlThreads = 4 * kDh;
+constexpr int kSlRows = 16;           // rows per cluster
+constexpr int kSlCta = 4;             // CTAs per cluster, each owning 32 of the head's 128 cell dims
+constexpr int kSlE = kDh / kSlCta;    // cell dims per CTA
+constexpr int kSlThreads = 256;
+constexpr int kSlCols = 4 * kSlE;     // gate columns per CTA: 4 gates × its 32 cell dims
+constexpr int kSlYPitch = kDh + 4;    // y row pitch in floats (16-byte rows, conflict-free row quads)
+constexpr int kSlRawPitch = kSlCols + 4;
 
-// The sLSTM recurrence of kSlRows rows and one head (Cells.slstmRecurrence, Cells.java:170-218) with the
-// per-head LayerNorm of its output (Cells.slstm :139-140) in the epilogue. wx [(r·S + t), ldwx] holds the
+// Dynamic shared memory of the sLSTM kernel: the CTA's quarter of R, two y buffers and the raw gates
+// (≈ 89 KB, so two CTAs of different clusters share an SM).
+size_t slstm_smem() {
+  return sizeof(float) * (static_cast<size_t>(kDh) * kSlCols + 2 * kSlRows * kSlYPitch + kSlRows * kSlRawPitch) +
+         2 * sizeof(uint64_t);
+}
+
+// The sLSTM recurrence of kSlRows rows and one head (Cells.slstmRecurrence, Cells.java:170-218) on a cluster
+// of 4 CTAs, each owning 32 of the head's 128 cell dims: its quarter of the recurrent weights R
+// (128 × 4 gates × 32, 64 KB) stays in shared memory for all S steps, and each step's y quarter is stored
+// asynchronously into the other CTAs' y buffers (distributed shared memory), completing on the receiver's
+// mbarrier of that buffer, so a step waits only for its peers' y and never for a cluster-wide fence. Two
+// such CTAs share an SM, so one's gate update and waits hide behind the other's y·R. The per-head LayerNorm of the output
+// (Cells.slstm :139-140) runs after the last step from y parked in ybuf. wx [(r·S + t), ldwx] holds the
 // headwise gate pre-activations at columns head·512 + g·128 + e (g = i, f, z, o); R [H, 128, 4, 128],
-// bias [H, 4, 128]. out (+)= LN(y)·w at columns head·128 + e.
-__global__ void __launch_bounds__(kSlThreads) slstm_kernel(const float* __restrict__ wx, long long ldwx, int rows,
-                                                           int S, int heads, const float* __restrict__ R,
-                                                           const float* __restrict__ bias,
-                                                           const float* __restrict__ norm_w, float* out,
-                                                           long long ld_out, int accumulate) {
-  __shared__ __align__(16) float ys[kSlRows][kDh];
-  __shared__ float raws[kSlRows][4 * kDh];
+// bias [H, 4, 128]; ybuf [(r·S + t), ld_y] at columns head·128 + e; out (+)= LN(y)·w at columns
+// head·128 + e.
+__global__ void __launch_bounds__(kSlThreads, 2) slstm_kernel(const float* __restrict__ wx, long long ldwx, int rows,
+                                                              int S, const float* __restrict__ R,
+                                                              const float* __restrict__ bias,
+                                                              const float* __restrict__ norm_w, float* ybuf,
+                                                              long long ld_y, float* out, long long ld_out,
+                                                              int accumulate, uint32_t* err) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  float* rs = reinterpret_cast<float*>(sm_raw);  // [128 p][128]: column 32g + e' = R[head][p][g][32q + e']
+  float* ys = rs + kDh * kSlCols;                // [2][16][132]: y of the previous step, all 128 dims
+  float* raws = ys + 2 * kSlRows * kSlYPitch;    // [16][132]: y·R of this step
+  uint64_t* ybar = reinterpret_cast<uint64_t*>(raws + kSlRows * kSlRawPitch);  // [2]: peers' y landed in buffer b
+  const uint32_t q = cluster_ctarank();
   const int head = blockIdx.y;
-  const int r0 = blockIdx.x * kSlRows;
+  const int r0 = (blockIdx.x / kSlCta) * kSlRows;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < kSlRows * kDh; i += kSlThreads) ys[i / kDh][i % kDh] = 0.0f;
   const float* Rh = R + static_cast<long long>(head) * kDh * 4 * kDh;
-  const float bcol = bias[head * 4 * kDh + tid];
-  float c[4] = {0, 0, 0, 0}, n[4] = {0, 0, 0, 0}, m[4] = {0, 0, 0, 0};
-  const int row = r0 + warp;
-  const bool live = row < rows;
-  __syncthreads();
+  for (int i = tid; i < kDh * kSlCols / 4; i += kSlThreads) {
+    const int pp = i / (kSlCols / 4), c4 = i % (kSlCols / 4), g = c4 >> 3, e4 = c4 & 7;
+    *reinterpret_cast<float4*>(rs + pp * kSlCols + 4 * c4) = __ldg(reinterpret_cast<const float4*>(
+        Rh + (static_cast<long long>(pp) * 4 + g) * kDh + kSlE * static_cast<int>(q) + 4 * e4));
+  }
+  for (int i = tid; i < kSlRows * kSlYPitch; i += kSlThreads) ys[i] = 0.0f;  // y before the first step
+  // y·R tile: columns 4·cq .. 4·cq + 3, rows rq and rq + 8
+  const int cq = 8 * (warp & 3) + (lane & 7), rq = 4 * (warp >> 2) + (lane >> 3);
+  // gate update: row br, cell dims ecol, ecol + 1 of the head
+  const int br = tid >> 4, el = 2 * (tid & 15), ecol = kSlE * static_cast<int>(q) + el;
+  const int brow = r0 + br;
+  const bool blive = brow < rows;
+  float bcol[4][2], gx[4][2];
+  const float* wrow = wx + static_cast<long long>(blive ? brow : 0) * S * ldwx + head * 4 * kDh + ecol;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const float2 b2 = __ldg(reinterpret_cast<const float2*>(bias + head * 4 * kDh + g * kDh + ecol));
+    const float2 x2 = blive ? *reinterpret_cast<const float2*>(wrow + g * kDh) : make_float2(0.f, 0.f);
+    bcol[g][0] = b2.x, bcol[g][1] = b2.y, gx[g][0] = x2.x, gx[g][1] = x2.y;
+  }
+  float c[2] = {0, 0}, n[2] = {0, 0}, m[2] = {0, 0};
+  // each use of ybar[b] expects the other CTAs' quarters of one step's y: 3 × 16 rows × 32 dims × 4 bytes
+  constexpr uint32_t kPeerBytes = (kSlCta - 1) * kSlRows * kSlE * sizeof(float);
+  if (tid == 0) {
+    mbar_init(&ybar[0], 1);
+    mbar_init(&ybar[1], 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&ybar[1], kPeerBytes);  // y of step 0 lands in buffer 1
+  }
+  bool ok = true;
+  cluster_sync();  // every CTA running with its y buffers cleared and barriers set before any remote store
   for (int t = 0; t < S; ++t) {
-    // phase A: raw[rb][col] = (wx + b) + Σ_p y[rb][p]·R[p][col], col = tid
-    float acc[kSlRows];
+    const float* yb = ys + (t & 1) * kSlRows * kSlYPitch;
+    // the peers' quarters of y(t - 1): the ((t - 1) / 2)-th completion of ybar[t & 1]
+    if (t > 0 && !mbar_wait(&ybar[t & 1], ((t - 1) >> 1) & 1)) ok = false;
+    float acc[2][4];
 #pragma unroll
-    for (int rb = 0; rb < kSlRows; ++rb) acc[rb] = 0.0f;
-    for (int p = 0; p < kDh; p += 4) {
-      const float w0 = __ldg(Rh + (p + 0) * 4 * kDh + tid);
-      const float w1 = __ldg(Rh + (p + 1) * 4 * kDh + tid);
-      const float w2 = __ldg(Rh + (p + 2) * 4 * kDh + tid);
-      const float w3 = __ldg(Rh + (p + 3) * 4 * kDh + tid);
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
-      for (int rb = 0; rb < kSlRows; ++rb) {
-        const float4 y4 = *reinterpret_cast<const float4*>(&ys[rb][p]);
-        acc[rb] = fmaf(y4.x, w0, fmaf(y4.y, w1, fmaf(y4.z, w2, fmaf(y4.w, w3, acc[rb]))));
+      for (int j = 0; j < 4; ++j) acc[a][j] = 0.0f;
+#pragma unroll 4
+    for (int pp = 0; pp < kDh; pp += 4) {
+      float yv[2][4];
+#pragma unroll
+      for (int a = 0; a < 2; ++a) {
+        const float4 v = *reinterpret_cast<const float4*>(yb + (rq + 8 * a) * kSlYPitch + pp);
+        yv[a][0] = v.x, yv[a][1] = v.y, yv[a][2] = v.z, yv[a][3] = v.w;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 w = *reinterpret_cast<const float4*>(rs + (pp + k) * kSlCols + 4 * cq);
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          acc[a][0] = fmaf(yv[a][k], w.x, acc[a][0]);
+          acc[a][1] = fmaf(yv[a][k], w.y, acc[a][1]);
+          acc[a][2] = fmaf(yv[a][k], w.z, acc[a][2]);
+          acc[a][3] = fmaf(yv[a][k], w.w, acc[a][3]);
+        }
       }
     }
 #pragma unroll
-    for (int rb = 0; rb < kSlRows; ++rb) {
-      const int rr = r0 + rb;
-      const float g = rr < rows ? wx[(static_cast<long long>(rr) * S + t) * ldwx + head * 4 * kDh + tid] : 0.0f;
-      raws[rb][tid] = (g + bcol) + acc[rb];
+    for (int a = 0; a < 2; ++a)
+      *reinterpret_cast<float4*>(raws + (rq + 8 * a) * kSlRawPitch + 4 * cq) =
+          make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
+    // the next step's gate pre-activations, in flight across the barrier
+    float gn[4][2];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const float2 x2 =
+          blive && t + 1 < S ? *reinterpret_cast<const float2*>(wrow + (t + 1) * ldwx + g * kDh) : make_float2(0.f, 0.f);
+      gn[g][0] = x2.x, gn[g][1] = x2.y;
     }
     __syncthreads();
-    // phase B: warp `warp` updates row r0 + warp, lanes own e = 4·lane .. 4·lane + 3
-    float y[4];
+    float rw[4][2];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = 4 * lane + u;
-      const float ir = raws[warp][e], fr = raws[warp][kDh + e], zr = raws[warp][2 * kDh + e],
-                  orw = raws[warp][3 * kDh + e];
+    for (int g = 0; g < 4; ++g) {
+      const float2 v = *reinterpret_cast<const float2*>(raws + br * kSlRawPitch + kSlE * g + el);
+      rw[g][0] = v.x, rw[g][1] = v.y;
+    }
+    float y[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const float ir = (gx[0][u] + bcol[0][u]) + rw[0][u], fr = (gx[1][u] + bcol[1][u]) + rw[1][u],
+                  zr = (gx[2][u] + bcol[2][u]) + rw[2][u], orw = (gx[3][u] + bcol[3][u]) + rw[3][u];
       const float logf_ = (fminf(fr, 0.0f) - log1pf(expf(-fabsf(fr)))) + m[u];
       const float mn = t == 0 ? ir : fmaxf(ir, logf_);
       const float ig = expf(ir - mn), fg = expf(logf_ - mn);
@@ -346,36 +479,65 @@ __global__ void __launch_bounds__(kSlThreads) slstm_kernel(const float* __restri
       n[u] = fmaxf(fg * n[u] + ig, 1.0f);
       y[u] = (1.0f / (1.0f + expf(-orw))) * c[u] / n[u];
       m[u] = mn;
-      ys[warp][e] = y[u];
     }
-    float mean = y[0] + y[1] + y[2] + y[3];
+    const float2 y2 = make_float2(y[0], y[1]);
+    const int nb = (t + 1) & 1;
+    float* yn = ys + nb * kSlRows * kSlYPitch + br * kSlYPitch + ecol;
+    *reinterpret_cast<float2*>(yn) = y2;
+    // a peer stores into buffer nb only after it has waited for this CTA's y(t - 1), i.e. after this CTA's
+    // y·R of step t - 1 finished reading that buffer
+#pragma unroll
+    for (uint32_t k = 1; k < kSlCta; ++k) {
+      const uint32_t peer = (q + k) % kSlCta;
+      st_async_v2(mapa_shared(smem_u32(yn), peer), y2, mapa_shared(smem_u32(&ybar[nb]), peer));
+    }
+    if (blive) *reinterpret_cast<float2*>(ybuf + (static_cast<long long>(brow) * S + t) * ld_y + head * kDh + ecol) = y2;
+    // the next use of ybar[nb] (y(t + 2)) opens once this one has completed, which step t + 1 waits for
+    if (tid == 0 && t + 2 < S + 1) mbar_arrive_expect_tx(&ybar[t & 1], kPeerBytes);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) gx[g][0] = gn[g][0], gx[g][1] = gn[g][1];
+    __syncthreads();  // this CTA's quarter of y(t) in its own buffer; raws free again
+  }
+  // the peers' last quarters must have landed before this CTA may exit
+  if (!mbar_wait(&ybar[S & 1], ((S - 1) >> 1) & 1)) ok = false;
+  if (!ok) atomicOr(err, kErrTimeoutPeer);
+  __threadfence();
+  cluster_sync();  // every quarter of every y row in ybuf
+  // LayerNorm over the head's 128 dims: this CTA takes rows 4q .. 4q + 3 of the cluster, warps 0-3 the even
+  // steps and warps 4-7 the odd ones
+  const int er = r0 + 4 * static_cast<int>(q) + (warp & 3);
+  if (er >= rows) return;
+  const float4 w4 = __ldg(reinterpret_cast<const float4*>(norm_w + head * kDh + 4 * lane));
+  for (int t = warp >> 2; t < S; t += 2) {
+    const long long tok = static_cast<long long>(er) * S + t;
+    const float4 v4 = *reinterpret_cast<const float4*>(ybuf + tok * ld_y + head * kDh + 4 * lane);
+    float mean = v4.x + v4.y + v4.z + v4.w;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mean += __shfl_xor_sync(0xffffffffu, mean, o);
     mean *= 1.0f / kDh;
     float var = 0.0f;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) var = fmaf(y[u] - mean, y[u] - mean, var);
+    var = fmaf(v4.x - mean, v4.x - mean, var);
+    var = fmaf(v4.y - mean, v4.y - mean, var);
+    var = fmaf(v4.z - mean, v4.z - mean, var);
+    var = fmaf(v4.w - mean, v4.w - mean, var);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
     var *= 1.0f / kDh;
     const float inv = rsqrtf(var + kNormEps);
-    if (live) {
-      float* dst = out + (static_cast<long long>(row) * S + t) * ld_out + head * kDh + 4 * lane;
-      float4 v;
-      v.x = (y[0] - mean) * inv * norm_w[head * kDh + 4 * lane];
-      v.y = (y[1] - mean) * inv * norm_w[head * kDh + 4 * lane + 1];
-      v.z = (y[2] - mean) * inv * norm_w[head * kDh + 4 * lane + 2];
-      v.w = (y[3] - mean) * inv * norm_w[head * kDh + 4 * lane + 3];
-      if (accumulate) {
-        const float4 o = *reinterpret_cast<const float4*>(dst);
-        v.x += o.x;
-        v.y += o.y;
-        v.z += o.z;
-        v.w += o.w;
-      }
-      *reinterpret_cast<float4*>(dst) = v;
+    float* dst = out + tok * ld_out + head * kDh + 4 * lane;
+    float4 v;
+    v.x = (v4.x - mean) * inv * w4.x;
+    v.y = (v4.y - mean) * inv * w4.y;
+    v.z = (v4.z - mean) * inv * w4.z;
+    v.w = (v4.w - mean) * inv * w4.w;
+    if (accumulate) {
+      const float4 o = *reinterpret_cast<const float4*>(dst);
+      v.x += o.x;
+      v.y += o.y;
+      v.z += o.z;
+      v.w += o.w;
     }
-    __syncthreads();
+    *reinterpret_cast<float4*>(dst) = v;
   }
 }
 
@@ -550,7 +712,7 @@ struct TxPlan {
   int *known = nullptr, *kept = nullptr, *gs = nullptr, *ge = nullptr, *kt = nullptr;
   OpBuf tok, emb_h, xn, hn, rev_in, cat, act, vatt, vhid, oh;
   float *h = nullptr, *proj = nullptr, *yc = nullptr, *rev_out = nullptr, *comb = nullptr, *xk = nullptr,
-        *vqkv = nullptr, *y = nullptr, *out = nullptr;
+        *vqkv = nullptr, *y = nullptr, *out = nullptr, *sy = nullptr;
   GraphRunner graph;
 };
 
@@ -765,6 +927,8 @@ std::unique_ptr<TxPlan> make_plan(const Tirex2Engine& e, int rows, int nk, int n
             alloc_op(m, op, TC, d, &p->hn) && (p->proj = f32(TC * cell_cols)) && alloc_op(m, op, T, e.F, &p->act) &&
             alloc_op(m, op, T, e.out_ff, &p->oh) && (p->y = f32(T * e.Q * e.P)) &&
             (p->out = f32(static_cast<long long>(rows) * e.Q * L));
+  if (ok && std::count(e.kinds.begin(), e.kinds.end(), static_cast<int>(JC_TIREX_SLSTM)) > 0)
+    ok = (p->sy = f32(TC * d)) != nullptr;  // the sLSTM cells' y before their LayerNorm
   if (ok && nk > 0)
     ok = (p->yc = f32(T * d)) && alloc_op(m, op, TK, d, &p->rev_in) && (p->rev_out = f32(TK * d)) &&
          alloc_op(m, op, TK, 2 * d, &p->cat) && (p->comb = f32(TK * d));
@@ -871,10 +1035,23 @@ cudaError_t run_cell(const Tirex2Engine& e, TxDevice& dv, TxPlan& p, const TxBlo
       into_f32(g, p.proj + h * 4 * kDh, ldw, false);
       JC_TRY(gemm(dv, g, s, "gemm.gates"));
     }
-    dim3 grid((rows + kSlRows - 1) / kSlRows, e.SH);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kSlCta * ((rows + kSlRows - 1) / kSlRows), e.SH);
+    cfg.blockDim = dim3(kSlThreads);
+    cfg.dynamicSmemBytes = slstm_smem();
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kSlCta;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     prof.begin(s, "slstm", 2.0 * T * e.SH * kDh * 4 * kDh);
-    slstm_kernel<<<grid, kSlThreads, 0, s>>>(p.proj, ldw, rows, S, e.SH, B.rec, B.sbias, B.group_norm, dst, d,
-                                               accumulate ? 1 : 0);
+    JC_TRY(cudaLaunchKernelEx(&cfg, slstm_kernel, static_cast<const float*>(p.proj), ldw, rows, S,
+                              static_cast<const float*>(B.rec), static_cast<const float*>(B.sbias),
+                              static_cast<const float*>(B.group_norm), p.sy, static_cast<long long>(d), dst,
+                              static_cast<long long>(d), accumulate ? 1 : 0, dv.err));
     prof.end(s);
     JC_TRY(cudaGetLastError());
   }
@@ -1217,14 +1394,16 @@ jc_status jc_engine_create_tirex2(const jc_tirex2_desc* desc, const jc_tensor_vi
         cudaEventCreateWithFlags(&dv->ev_in, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&dv->ev_out, cudaEventDisableTiming) != cudaSuccess)
       return fail_cuda(cudaGetLastError(), "engine device setup");
-    // the mLSTM kernel's prefix scans hold 4 tokens per thread, and its gate prefix lives in shared memory
+    // the mLSTM kernel's gate prefix lives in shared memory
     const size_t smem = mlstm_smem(e->S());
-    if (e->S() > 4 * kMlThreads || smem > 227 * 1024)
-      return fail(JC_ERR_UNSUPPORTED_SHAPE, "sequence of " + std::to_string(e->S()) + " patches is too long (max " +
-                                                std::to_string(4 * kMlThreads) + ")");
+    if (smem > 227 * 1024)
+      return fail(JC_ERR_UNSUPPORTED_SHAPE, "sequence of " + std::to_string(e->S()) +
+                                                " patches is too long for the mLSTM kernel's shared-memory gate prefix");
     if (cudaFuncSetAttribute(mlstm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-        cudaSuccess)
-      return fail_cuda(cudaGetLastError(), "mLSTM kernel setup");
+            cudaSuccess ||
+        cudaFuncSetAttribute(slstm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(slstm_smem())) != cudaSuccess)
+      return fail_cuda(cudaGetLastError(), "mLSTM / sLSTM kernel setup");
     std::string err;
     if (!upload(*e, hw, *dv, &err)) return fail(JC_ERR_OOM, err);
     e->devs.push_back(std::move(dv));
