@@ -42,10 +42,6 @@ struct TcShape {
   int k_off, v_off, p_off, bar_off;  // byte offsets into the 1024-aligned dynamic shared memory
 };
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -347,198 +347,272 @@ __global__ void __launch_bounds__(kMlThreads, 2) mlstm_kernel(const float* __res
   }
 }
 
-constexpr int kSlRows = 16;           // rows per cluster
-constexpr int kSlCta = 4;             // CTAs per cluster, each owning 32 of the head's 128 cell dims
-constexpr int kSlE = kDh / kSlCta;    // cell dims per CTA
+constexpr int kSlRows = 64;            // rows per cluster: the MMA's N
+constexpr int kSlCta = 4;              // CTAs per cluster, each owning 32 of the head's 128 cell dims
+constexpr int kSlE = kDh / kSlCta;     // cell dims per CTA
 constexpr int kSlThreads = 256;
-constexpr int kSlCols = 4 * kSlE;     // gate columns per CTA: 4 gates × its 32 cell dims
-constexpr int kSlYPitch = kDh + 4;    // y row pitch in floats (16-byte rows, conflict-free row quads)
-constexpr int kSlRawPitch = kSlCols + 4;
+constexpr int kSlM = 4 * kSlE;         // gate columns per CTA (4 gates × 32 dims): the MMA's M
+constexpr uint32_t kSlTmemCols = 512;  // R hi [0, 128) | R lo [128, 256) | raw gates [256, 320)
+constexpr int kSlYPitch = kSlE + 4;
+// shared memory (bytes from a 1024-aligned base): y(t-1) as the MMA's B operand in TF32 hi and lo parts
+// ([64 rows × 128] K-major, 128-byte swizzle), two inboxes the cluster's y(t) lands in, the raw gates
+// [4][64][32], this CTA's y(t) [64][36], mbarriers and the TMEM address
+constexpr int kSlBHi = 0;
+constexpr int kSlBLo = kSlBHi + kSlRows * kDh * 4;
+constexpr int kSlInbox = kSlBLo + kSlRows * kDh * 4;
+constexpr int kSlRaw = kSlInbox + 2 * kSlRows * kDh * 4;
+constexpr int kSlYs = kSlRaw + 4 * kSlRows * kSlE * 4;
+constexpr int kSlBar = kSlYs + kSlRows * kSlYPitch * 4;
+constexpr int kSlSmem = kSlBar + 64 + 1024;
+constexpr uint32_t kSlInBytes = kSlCta * kSlRows * kSlE * 4;  // one step's y of the whole cluster
+// A step's waits take microseconds; one that has not completed after 50 ms gives up (and flags the error),
+// so even a broken exchange ends a launch in seconds.
+constexpr uint64_t kSlWaitNs = 50000000ull;
 
-// Dynamic shared memory of the sLSTM kernel: the CTA's quarter of R, two y buffers and the raw gates
-// (≈ 89 KB, so two CTAs of different clusters share an SM).
-size_t slstm_smem() {
-  return sizeof(float) * (static_cast<size_t>(kDh) * kSlCols + 2 * kSlRows * kSlYPitch + kSlRows * kSlRawPitch) +
-         2 * sizeof(uint64_t);
+// Dynamic shared memory of the sLSTM kernel.
+size_t slstm_smem() { return kSlSmem; }
+
+// Byte offset of element (n, k) (k a multiple of 4) in a [64 × 128] fp32 K-major operand stored with the
+// 128-byte swizzle: 32-element K blocks of 64 rows × 128 bytes, 8-row groups 1024 bytes apart, the 16-byte
+// chunks of row n permuted by XOR with n mod 8.
+__device__ __forceinline__ uint32_t sl_sw128(int n, int k) {
+  return static_cast<uint32_t>((k >> 5) * (kSlRows * 128) + (n >> 3) * 1024 + (n & 7) * 128 +
+                               ((((k & 31) >> 2) ^ (n & 7)) << 4));
 }
 
-// The sLSTM recurrence of kSlRows rows and one head (Cells.slstmRecurrence, Cells.java:170-218) on a cluster
-// of 4 CTAs, each owning 32 of the head's 128 cell dims: its quarter of the recurrent weights R
-// (128 × 4 gates × 32, 64 KB) stays in shared memory for all S steps, and each step's y quarter is stored
-// asynchronously into the other CTAs' y buffers (distributed shared memory), completing on the receiver's
-// mbarrier of that buffer, so a step waits only for its peers' y and never for a cluster-wide fence. Two
-// such CTAs share an SM, so one's gate update and waits hide behind the other's y·R. The per-head LayerNorm of the output
-// (Cells.slstm :139-140) runs after the last step from y parked in ybuf. wx [(r·S + t), ldwx] holds the
-// headwise gate pre-activations at columns head·512 + g·128 + e (g = i, f, z, o); R [H, 128, 4, 128],
-// bias [H, 4, 128]; ybuf [(r·S + t), ld_y] at columns head·128 + e; out (+)= LN(y)·w at columns
-// head·128 + e.
-__global__ void __launch_bounds__(kSlThreads, 2) slstm_kernel(const float* __restrict__ wx, long long ldwx, int rows,
+// LayerNorm over the head's 128 dims of one y row (Cells.slstm :139-140), out (+)= LN(y)·w; one warp, lane
+// holding dims 4·lane .. 4·lane + 3. `prev` is out's current value (read only when accumulating).
+__device__ __forceinline__ float4 sl_layernorm(float4 v4, float4 w4, float4 prev, int accumulate) {
+  float mean = v4.x + v4.y + v4.z + v4.w;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mean += __shfl_xor_sync(0xffffffffu, mean, o);
+  mean *= 1.0f / kDh;
+  float var = 0.0f;
+  var = fmaf(v4.x - mean, v4.x - mean, var);
+  var = fmaf(v4.y - mean, v4.y - mean, var);
+  var = fmaf(v4.z - mean, v4.z - mean, var);
+  var = fmaf(v4.w - mean, v4.w - mean, var);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+  var *= 1.0f / kDh;
+  const float inv = rsqrtf(var + kNormEps);
+  float4 v;
+  v.x = (v4.x - mean) * inv * w4.x;
+  v.y = (v4.y - mean) * inv * w4.y;
+  v.z = (v4.z - mean) * inv * w4.z;
+  v.w = (v4.w - mean) * inv * w4.w;
+  if (accumulate) {
+    v.x += prev.x;
+    v.y += prev.y;
+    v.z += prev.z;
+    v.w += prev.w;
+  }
+  return v;
+}
+
+// The sLSTM recurrence (Cells.slstmRecurrence, Cells.java:170-218) as a per-step GEMM on the tensor cores.
+// A cluster of 4 CTAs takes 64 rows and one head; CTA q owns cell dims 32q .. 32q + 31, i.e. 128 of the
+// head's 512 gate columns. Per step, raw[m][n] = wx + b + Σ_p R[p][m]·y(t-1)[n][p] is one tcgen05 MMA
+// chain (M = 128 gate columns, N = 64 rows, K = 128) in three TF32 passes (R_hi·y_hi + R_hi·y_lo +
+// R_lo·y_hi, FP32-grade products), with R^T resident in tensor memory as the A operand and the
+// accumulator pre-loaded with wx + b. The gate update follows on the CUDA cores (gate order i, f, z, o),
+// and each CTA's y(t) quarter is stored into every CTA's inbox with st.async, completing on the
+// receiver's mbarrier. While step t's MMAs run, each CTA applies the per-head LayerNorm (Cells.slstm
+// :139-140) to its 16 rows of y(t-1) straight from the inbox. wx [(r·S + t), ldwx] holds the headwise
+// gate pre-activations at columns head·512 + g·128 + e; R [H, 128, 4, 128], bias [H, 4, 128];
+// out (+)= LN(y)·w at columns head·128 + e.
+__global__ void __launch_bounds__(kSlThreads, 1) slstm_kernel(const float* __restrict__ wx, long long ldwx, int rows,
                                                               int S, const float* __restrict__ R,
                                                               const float* __restrict__ bias,
-                                                              const float* __restrict__ norm_w, float* ybuf,
-                                                              long long ld_y, float* out, long long ld_out,
-                                                              int accumulate, uint32_t* err) {
-  extern __shared__ __align__(16) uint8_t sm_raw[];
-  float* rs = reinterpret_cast<float*>(sm_raw);  // [128 p][128]: column 32g + e' = R[head][p][g][32q + e']
-  float* ys = rs + kDh * kSlCols;                // [2][16][132]: y of the previous step, all 128 dims
-  float* raws = ys + 2 * kSlRows * kSlYPitch;    // [16][132]: y·R of this step
-  uint64_t* ybar = reinterpret_cast<uint64_t*>(raws + kSlRows * kSlRawPitch);  // [2]: peers' y landed in buffer b
+                                                              const float* __restrict__ norm_w, float* out,
+                                                              long long ld_out, int accumulate, uint32_t* err) {
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = sm_raw + (((smem_u32(sm_raw) + 1023u) & ~1023u) - smem_u32(sm_raw));
+  float* bhi = reinterpret_cast<float*>(sm + kSlBHi);
+  float* blo = reinterpret_cast<float*>(sm + kSlBLo);
+  float* inbox = reinterpret_cast<float*>(sm + kSlInbox);  // [2][64][128]
+  float* raw = reinterpret_cast<float*>(sm + kSlRaw);      // [4][64][32]
+  float* ys = reinterpret_cast<float*>(sm + kSlYs);        // [64][36]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kSlBar);  // [2]: the cluster's y landed in inbox b
+  uint64_t* mma_bar = full + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_bar + 1);
   const uint32_t q = cluster_ctarank();
   const int head = blockIdx.y;
   const int r0 = (blockIdx.x / kSlCta) * kSlRows;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const float* Rh = R + static_cast<long long>(head) * kDh * 4 * kDh;
-  for (int i = tid; i < kDh * kSlCols / 4; i += kSlThreads) {
-    const int pp = i / (kSlCols / 4), c4 = i % (kSlCols / 4), g = c4 >> 3, e4 = c4 & 7;
-    *reinterpret_cast<float4*>(rs + pp * kSlCols + 4 * c4) = __ldg(reinterpret_cast<const float4*>(
-        Rh + (static_cast<long long>(pp) * 4 + g) * kDh + kSlE * static_cast<int>(q) + 4 * e4));
+  const int sp = warp & 3, half = warp >> 2;  // the TMEM lane quarter (= gate) and row half this warp moves
+  const int e = kSlE * static_cast<int>(q) + lane;
+
+  for (int i = tid; i < 2 * kSlRows * kDh / 4; i += kSlThreads)  // y(-1) = 0 in both B parts
+    reinterpret_cast<float4*>(bhi)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (warp == 0) {
+    tmem_alloc(tslot, kSlTmemCols);
+    tmem_relinquish();
   }
-  for (int i = tid; i < kSlRows * kSlYPitch; i += kSlThreads) ys[i] = 0.0f;  // y before the first step
-  // y·R tile: columns 4·cq .. 4·cq + 3, rows rq and rq + 8
-  const int cq = 8 * (warp & 3) + (lane & 7), rq = 4 * (warp >> 2) + (lane >> 3);
-  // gate update: row br, cell dims ecol, ecol + 1 of the head
-  const int br = tid >> 4, el = 2 * (tid & 15), ecol = kSlE * static_cast<int>(q) + el;
-  const int brow = r0 + br;
-  const bool blive = brow < rows;
-  float bcol[4][2], gx[4][2];
-  const float* wrow = wx + static_cast<long long>(blive ? brow : 0) * S * ldwx + head * 4 * kDh + ecol;
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    const float2 b2 = __ldg(reinterpret_cast<const float2*>(bias + head * 4 * kDh + g * kDh + ecol));
-    const float2 x2 = blive ? *reinterpret_cast<const float2*>(wrow + g * kDh) : make_float2(0.f, 0.f);
-    bcol[g][0] = b2.x, bcol[g][1] = b2.y, gx[g][0] = x2.x, gx[g][1] = x2.y;
-  }
-  float c[2] = {0, 0}, n[2] = {0, 0}, m[2] = {0, 0};
-  // each use of ybar[b] expects the other CTAs' quarters of one step's y: 3 × 16 rows × 32 dims × 4 bytes
-  constexpr uint32_t kPeerBytes = (kSlCta - 1) * kSlRows * kSlE * sizeof(float);
   if (tid == 0) {
-    mbar_init(&ybar[0], 1);
-    mbar_init(&ybar[1], 1);
+    mbar_init(&full[0], 1);
+    mbar_init(&full[1], 1);
+    mbar_init(mma_bar, 1);
     fence_mbar_init();
-    mbar_arrive_expect_tx(&ybar[1], kPeerBytes);  // y of step 0 lands in buffer 1
+    mbar_arrive_expect_tx(&full[0], kSlInBytes);              // y(0)
+    if (S >= 2) mbar_arrive_expect_tx(&full[1], kSlInBytes);  // y(1)
   }
-  bool ok = true;
-  cluster_sync();  // every CTA running with its y buffers cleared and barriers set before any remote store
-  for (int t = 0; t < S; ++t) {
-    const float* yb = ys + (t & 1) * kSlRows * kSlYPitch;
-    // the peers' quarters of y(t - 1): the ((t - 1) / 2)-th completion of ybar[t & 1]
-    if (t > 0 && !mbar_wait(&ybar[t & 1], ((t - 1) >> 1) & 1)) ok = false;
-    float acc[2][4];
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tlane = static_cast<uint32_t>(32 * sp) << 16;
+  // R^T of this CTA's gate columns into TMEM lanes 32g + e' (g = sp), K = p along the columns
+  if (half == 0) {
+    const float* rp = R + static_cast<long long>(head) * kDh * 4 * kDh + sp * kDh + e;
+    for (int k0 = 0; k0 < kDh; k0 += 32) {
+      uint32_t hi[32], lo[32];
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[a][j] = 0.0f;
-#pragma unroll 4
-    for (int pp = 0; pp < kDh; pp += 4) {
-      float yv[2][4];
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        const float4 v = *reinterpret_cast<const float4*>(yb + (rq + 8 * a) * kSlYPitch + pp);
-        yv[a][0] = v.x, yv[a][1] = v.y, yv[a][2] = v.z, yv[a][3] = v.w;
+      for (int i = 0; i < 32; ++i) {
+        const float v = __ldg(rp + static_cast<long long>(k0 + i) * 4 * kDh);
+        const float h = round_tf32(v);
+        hi[i] = __float_as_uint(h);
+        lo[i] = __float_as_uint(round_tf32(v - h));
       }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float4 w = *reinterpret_cast<const float4*>(rs + (pp + k) * kSlCols + 4 * cq);
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          acc[a][0] = fmaf(yv[a][k], w.x, acc[a][0]);
-          acc[a][1] = fmaf(yv[a][k], w.y, acc[a][1]);
-          acc[a][2] = fmaf(yv[a][k], w.z, acc[a][2]);
-          acc[a][3] = fmaf(yv[a][k], w.w, acc[a][3]);
-        }
-      }
+      tmem_st_32x32b_x32(tmem + tlane + k0, hi);
+      tmem_st_32x32b_x32(tmem + tlane + 128 + k0, lo);
     }
+    tmem_st_wait();
+  }
+  const float bcol = __ldg(bias + head * 4 * kDh + sp * kDh + e);
+  const float* wcol = wx + head * 4 * kDh + sp * kDh + e;
+  float wxr[32];
+  auto load_wx = [&](int t) {
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-      *reinterpret_cast<float4*>(raws + (rq + 8 * a) * kSlRawPitch + 4 * cq) =
-          make_float4(acc[a][0], acc[a][1], acc[a][2], acc[a][3]);
-    // the next step's gate pre-activations, in flight across the barrier
-    float gn[4][2];
+    for (int i = 0; i < 32; ++i) {
+      const int row = r0 + 32 * half + i;
+      wxr[i] = row < rows ? wcol[(static_cast<long long>(row) * S + t) * ldwx] : 0.0f;
+    }
+  };
+  load_wx(0);
+  // LayerNorm rows of this CTA: 16q + 2·warp + j; out's previous value fetched a step ahead
+  const float4 w4 = __ldg(reinterpret_cast<const float4*>(norm_w + head * kDh + 4 * lane));
+  const int lrow = 16 * static_cast<int>(q) + 2 * warp;
+  float4 prev[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  auto out_at = [&](int j, int t) {
+    return out + (static_cast<long long>(r0 + lrow + j) * S + t) * ld_out + head * kDh + 4 * lane;
+  };
+  auto load_prev = [&](int t) {
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const float2 x2 =
-          blive && t + 1 < S ? *reinterpret_cast<const float2*>(wrow + (t + 1) * ldwx + g * kDh) : make_float2(0.f, 0.f);
-      gn[g][0] = x2.x, gn[g][1] = x2.y;
+    for (int j = 0; j < 2; ++j)
+      if (accumulate && r0 + lrow + j < rows) prev[j] = *reinterpret_cast<const float4*>(out_at(j, t));
+  };
+  auto layernorm = [&](int t) {  // y(t), complete in inbox t & 1
+    const float* ib = inbox + (t & 1) * kSlRows * kDh;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float4 v4 = *reinterpret_cast<const float4*>(ib + (lrow + j) * kDh + 4 * lane);
+      const float4 o = sl_layernorm(v4, w4, prev[j], accumulate);
+      if (r0 + lrow + j < rows) *reinterpret_cast<float4*>(out_at(j, t)) = o;
+    }
+  };
+  load_prev(0);
+  float c[8], n[8], m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) c[i] = n[i] = m[i] = 0.0f;
+  bool ok = true;
+  cluster_sync();  // every CTA's barriers set before any st.async reaches them
+  const uint32_t idesc = idesc_f32acc(2, kSlM, kSlRows);
+  for (int t = 0; t < S; ++t) {
+    if (t > 0) {
+      // y(t-1) of the whole cluster → the B operand, split into TF32 hi and lo parts
+      const int b = (t - 1) & 1;
+      if (!mbar_wait(&full[b], ((t - 1) >> 1) & 1, kSlWaitNs)) ok = false;
+      if (tid == 0 && t + 1 < S) mbar_arrive_expect_tx(&full[b], kSlInBytes);  // y(t+1) lands in inbox b
+      const float* ib = inbox + b * kSlRows * kDh;
+#pragma unroll
+      for (int j = 0; j < kSlRows * kDh / 4 / kSlThreads; ++j) {
+        const int cidx = tid + j * kSlThreads, nn = cidx >> 5, k = 4 * (cidx & 31);
+        const float4 v = *reinterpret_cast<const float4*>(ib + nn * kDh + k);
+        const float4 h = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+        const float4 l = make_float4(round_tf32(v.x - h.x), round_tf32(v.y - h.y), round_tf32(v.z - h.z),
+                                     round_tf32(v.w - h.w));
+        const uint32_t off = sl_sw128(nn, k);
+        *reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(bhi) + off) = h;
+        *reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(blo) + off) = l;
+      }
+      fence_proxy_async_smem();
+    }
+    {  // accumulator = wx(t) + b for this warp's (gate columns, rows)
+      uint32_t d[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) d[i] = __float_as_uint(wxr[i] + bcol);
+      tmem_st_32x32b_x32(tmem + tlane + 256 + 32 * half, d);
+      tmem_st_wait();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int pass = 0; pass < 3; ++pass) {
+        const uint32_t a = tmem + (pass == 2 ? 128u : 0u);
+        const uint32_t bb = smem_u32(pass == 1 ? blo : bhi);
+#pragma unroll
+        for (int k = 0; k < kDh / 8; ++k)
+          umma_tf32_ts(tmem + 256, a + 8 * k, sdesc_k_sw128(bb + (k >> 2) * (kSlRows * 128) + (k & 3) * 32), idesc,
+                       1);
+      }
+      umma_commit(mma_bar);
+    }
+    // while the MMAs run: the next step's wx and the LayerNorm of y(t-1)
+    if (t + 1 < S) load_wx(t + 1);
+    if (t > 0) {
+      layernorm(t - 1);
+      load_prev(t);
+    }
+    if (!mbar_wait(mma_bar, t & 1, kSlWaitNs)) ok = false;
+    tc_fence_after();
+    {  // raw gates out of TMEM: gate sp of cell dim e for rows 32·half .. 32·half + 31
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem + tlane + 256 + 32 * half, v);
+      tmem_ld_wait();
+      float* rg = raw + sp * kSlRows * kSlE;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) rg[(32 * half + i) * kSlE + lane] = __uint_as_float(v[i]);
     }
     __syncthreads();
-    float rw[4][2];
+    // gate update of cell dim e for rows warp + 8i; the exponentials of the bounded terms and the
+    // divisions by n ≥ 1 use the fast intrinsics (errors of a few ulp, below the TF32-split products')
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const float2 v = *reinterpret_cast<const float2*>(raws + br * kSlRawPitch + kSlE * g + el);
-      rw[g][0] = v.x, rw[g][1] = v.y;
-    }
-    float y[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const float ir = (gx[0][u] + bcol[0][u]) + rw[0][u], fr = (gx[1][u] + bcol[1][u]) + rw[1][u],
-                  zr = (gx[2][u] + bcol[2][u]) + rw[2][u], orw = (gx[3][u] + bcol[3][u]) + rw[3][u];
-      const float logf_ = (fminf(fr, 0.0f) - log1pf(expf(-fabsf(fr)))) + m[u];
+    for (int i = 0; i < 8; ++i) {
+      const int rl = warp + 8 * i;
+      const float ir = raw[(0 * kSlRows + rl) * kSlE + lane], fr = raw[(1 * kSlRows + rl) * kSlE + lane],
+                  zr = raw[(2 * kSlRows + rl) * kSlE + lane], orw = raw[(3 * kSlRows + rl) * kSlE + lane];
+      const float logf_ = (fminf(fr, 0.0f) - __logf(1.0f + __expf(-fabsf(fr)))) + m[i];
       const float mn = t == 0 ? ir : fmaxf(ir, logf_);
-      const float ig = expf(ir - mn), fg = expf(logf_ - mn);
-      c[u] = fg * c[u] + ig * tanhf(zr);
-      n[u] = fmaxf(fg * n[u] + ig, 1.0f);
-      y[u] = (1.0f / (1.0f + expf(-orw))) * c[u] / n[u];
-      m[u] = mn;
+      const float ig = __expf(ir - mn), fg = __expf(logf_ - mn);
+      c[i] = fg * c[i] + ig * tanhf(zr);
+      n[i] = fmaxf(fg * n[i] + ig, 1.0f);
+      m[i] = mn;
+      ys[rl * kSlYPitch + lane] = __fdividef(__fdividef(c[i], n[i]), 1.0f + __expf(-orw));
     }
-    const float2 y2 = make_float2(y[0], y[1]);
-    const int nb = (t + 1) & 1;
-    float* yn = ys + nb * kSlRows * kSlYPitch + br * kSlYPitch + ecol;
-    *reinterpret_cast<float2*>(yn) = y2;
-    // a peer stores into buffer nb only after it has waited for this CTA's y(t - 1), i.e. after this CTA's
-    // y·R of step t - 1 finished reading that buffer
+    __syncthreads();
+    // y(t) quarter → every CTA's inbox (t & 1)
 #pragma unroll
-    for (uint32_t k = 1; k < kSlCta; ++k) {
-      const uint32_t peer = (q + k) % kSlCta;
-      st_async_v2(mapa_shared(smem_u32(yn), peer), y2, mapa_shared(smem_u32(&ybar[nb]), peer));
+    for (int j = 0; j < kSlRows * kSlE / 4 / kSlThreads; ++j) {
+      const int cidx = tid + j * kSlThreads, nn = cidx >> 3, k = 4 * (cidx & 7);
+      const float4 v = *reinterpret_cast<const float4*>(ys + nn * kSlYPitch + k);
+      float* dst = inbox + (t & 1) * kSlRows * kDh + nn * kDh + kSlE * static_cast<int>(q) + k;
+#pragma unroll
+      for (uint32_t p = 0; p < kSlCta; ++p)
+        st_async_v4(mapa_shared(smem_u32(dst), p), v, mapa_shared(smem_u32(&full[t & 1]), p));
     }
-    if (blive) *reinterpret_cast<float2*>(ybuf + (static_cast<long long>(brow) * S + t) * ld_y + head * kDh + ecol) = y2;
-    // the next use of ybar[nb] (y(t + 2)) opens once this one has completed, which step t + 1 waits for
-    if (tid == 0 && t + 2 < S + 1) mbar_arrive_expect_tx(&ybar[t & 1], kPeerBytes);
-#pragma unroll
-    for (int g = 0; g < 4; ++g) gx[g][0] = gn[g][0], gx[g][1] = gn[g][1];
-    __syncthreads();  // this CTA's quarter of y(t) in its own buffer; raws free again
   }
-  // the peers' last quarters must have landed before this CTA may exit
-  if (!mbar_wait(&ybar[S & 1], ((S - 1) >> 1) & 1)) ok = false;
-  if (!ok) atomicOr(err, kErrTimeoutPeer);
-  __threadfence();
-  cluster_sync();  // every quarter of every y row in ybuf
-  // LayerNorm over the head's 128 dims: this CTA takes rows 4q .. 4q + 3 of the cluster, warps 0-3 the even
-  // steps and warps 4-7 the odd ones
-  const int er = r0 + 4 * static_cast<int>(q) + (warp & 3);
-  if (er >= rows) return;
-  const float4 w4 = __ldg(reinterpret_cast<const float4*>(norm_w + head * kDh + 4 * lane));
-  for (int t = warp >> 2; t < S; t += 2) {
-    const long long tok = static_cast<long long>(er) * S + t;
-    const float4 v4 = *reinterpret_cast<const float4*>(ybuf + tok * ld_y + head * kDh + 4 * lane);
-    float mean = v4.x + v4.y + v4.z + v4.w;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mean += __shfl_xor_sync(0xffffffffu, mean, o);
-    mean *= 1.0f / kDh;
-    float var = 0.0f;
-    var = fmaf(v4.x - mean, v4.x - mean, var);
-    var = fmaf(v4.y - mean, v4.y - mean, var);
-    var = fmaf(v4.z - mean, v4.z - mean, var);
-    var = fmaf(v4.w - mean, v4.w - mean, var);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    var *= 1.0f / kDh;
-    const float inv = rsqrtf(var + kNormEps);
-    float* dst = out + tok * ld_out + head * kDh + 4 * lane;
-    float4 v;
-    v.x = (v4.x - mean) * inv * w4.x;
-    v.y = (v4.y - mean) * inv * w4.y;
-    v.z = (v4.z - mean) * inv * w4.z;
-    v.w = (v4.w - mean) * inv * w4.w;
-    if (accumulate) {
-      const float4 o = *reinterpret_cast<const float4*>(dst);
-      v.x += o.x;
-      v.y += o.y;
-      v.z += o.z;
-      v.w += o.w;
-    }
-    *reinterpret_cast<float4*>(dst) = v;
-  }
+  // the last step's y: wait for it and normalise it
+  if (!mbar_wait(&full[(S - 1) & 1], ((S - 1) >> 1) & 1, kSlWaitNs)) ok = false;
+  layernorm(S - 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kSlTmemCols);
+  if (!ok && tid == 0) atomicOr(err, kErrTimeoutPeer);
+  cluster_sync();  // no st.async in flight into any CTA of the cluster
 }
 
 // Attention across the kept rows of a group at one patch and head (CpuReference.variateMixer,
@@ -712,7 +786,7 @@ struct TxPlan {
   int *known = nullptr, *kept = nullptr, *gs = nullptr, *ge = nullptr, *kt = nullptr;
   OpBuf tok, emb_h, xn, hn, rev_in, cat, act, vatt, vhid, oh;
   float *h = nullptr, *proj = nullptr, *yc = nullptr, *rev_out = nullptr, *comb = nullptr, *xk = nullptr,
-        *vqkv = nullptr, *y = nullptr, *out = nullptr, *sy = nullptr;
+        *vqkv = nullptr, *y = nullptr, *out = nullptr;
   GraphRunner graph;
 };
 
@@ -927,8 +1001,6 @@ std::unique_ptr<TxPlan> make_plan(const Tirex2Engine& e, int rows, int nk, int n
             alloc_op(m, op, TC, d, &p->hn) && (p->proj = f32(TC * cell_cols)) && alloc_op(m, op, T, e.F, &p->act) &&
             alloc_op(m, op, T, e.out_ff, &p->oh) && (p->y = f32(T * e.Q * e.P)) &&
             (p->out = f32(static_cast<long long>(rows) * e.Q * L));
-  if (ok && std::count(e.kinds.begin(), e.kinds.end(), static_cast<int>(JC_TIREX_SLSTM)) > 0)
-    ok = (p->sy = f32(TC * d)) != nullptr;  // the sLSTM cells' y before their LayerNorm
   if (ok && nk > 0)
     ok = (p->yc = f32(T * d)) && alloc_op(m, op, TK, d, &p->rev_in) && (p->rev_out = f32(TK * d)) &&
          alloc_op(m, op, TK, 2 * d, &p->cat) && (p->comb = f32(TK * d));
@@ -1050,8 +1122,8 @@ cudaError_t run_cell(const Tirex2Engine& e, TxDevice& dv, TxPlan& p, const TxBlo
     prof.begin(s, "slstm", 2.0 * T * e.SH * kDh * 4 * kDh);
     JC_TRY(cudaLaunchKernelEx(&cfg, slstm_kernel, static_cast<const float*>(p.proj), ldw, rows, S,
                               static_cast<const float*>(B.rec), static_cast<const float*>(B.sbias),
-                              static_cast<const float*>(B.group_norm), p.sy, static_cast<long long>(d), dst,
-                              static_cast<long long>(d), accumulate ? 1 : 0, dv.err));
+                              static_cast<const float*>(B.group_norm), dst, static_cast<long long>(d),
+                              accumulate ? 1 : 0, dv.err));
     prof.end(s);
     JC_TRY(cudaGetLastError());
   }
