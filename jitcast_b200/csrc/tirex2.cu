@@ -350,19 +350,24 @@ __global__ void __launch_bounds__(kMlThreads, 2) mlstm_kernel(const float* __res
 constexpr int kSlRows = 64;            // rows per cluster: the MMA's N
 constexpr int kSlCta = 4;              // CTAs per cluster, each owning 32 of the head's 128 cell dims
 constexpr int kSlE = kDh / kSlCta;     // cell dims per CTA
-constexpr int kSlThreads = 256;
+constexpr int kSlThreads = 512;      // 16 warps: warp w moves TMEM lane quarter w % 4, rows 16·(w / 4) ..
 constexpr int kSlM = 4 * kSlE;         // gate columns per CTA (4 gates × 32 dims): the MMA's M
-constexpr uint32_t kSlTmemCols = 512;  // R hi [0, 128) | R lo [128, 256) | raw gates [256, 320)
+// TMEM columns: R hi [0, 64) and R lo·2^11 [64, 128) as FP16 pairs (two K elements per 32-bit column),
+// the main accumulator D1 [128, 192) and the correction accumulator D2 [192, 256)
+constexpr uint32_t kSlTmemCols = 256;
 constexpr int kSlYPitch = kSlE + 4;
-// shared memory (bytes from a 1024-aligned base): y(t-1) as the MMA's B operand in TF32 hi and lo parts
-// ([64 rows × 128] K-major, 128-byte swizzle), two inboxes the cluster's y(t) lands in, the raw gates
-// [4][64][32], this CTA's y(t) [64][36], mbarriers and the TMEM address
+constexpr float kSlLoScale = 2048.0f;  // 2^11: lo parts scaled into FP16's normal range
+// shared memory (bytes from a 1024-aligned base): y(t-1) as the MMA's B operand in FP16 hi and lo·2^11
+// parts ([64 rows × 128] K-major, 128-byte swizzle), two inboxes the cluster's y(t) lands in, the raw
+// gates [4][64][32], this CTA's y(t) [64][36], the wx of the next two steps [2][64][128], mbarriers and
+// the TMEM address
 constexpr int kSlBHi = 0;
-constexpr int kSlBLo = kSlBHi + kSlRows * kDh * 4;
-constexpr int kSlInbox = kSlBLo + kSlRows * kDh * 4;
+constexpr int kSlBLo = kSlBHi + kSlRows * kDh * 2;
+constexpr int kSlInbox = kSlBLo + kSlRows * kDh * 2;
 constexpr int kSlRaw = kSlInbox + 2 * kSlRows * kDh * 4;
 constexpr int kSlYs = kSlRaw + 4 * kSlRows * kSlE * 4;
-constexpr int kSlBar = kSlYs + kSlRows * kSlYPitch * 4;
+constexpr int kSlWx = kSlYs + kSlRows * kSlYPitch * 4;  // wx slices of the next two steps [2][64][128]
+constexpr int kSlBar = kSlWx + 2 * kSlRows * kSlM * 4;
 constexpr int kSlSmem = kSlBar + 64 + 1024;
 constexpr uint32_t kSlInBytes = kSlCta * kSlRows * kSlE * 4;  // one step's y of the whole cluster
 // A step's waits take microseconds; one that has not completed after 50 ms gives up (and flags the error),
@@ -372,12 +377,30 @@ constexpr uint64_t kSlWaitNs = 50000000ull;
 // Dynamic shared memory of the sLSTM kernel.
 size_t slstm_smem() { return kSlSmem; }
 
-// Byte offset of element (n, k) (k a multiple of 4) in a [64 × 128] fp32 K-major operand stored with the
-// 128-byte swizzle: 32-element K blocks of 64 rows × 128 bytes, 8-row groups 1024 bytes apart, the 16-byte
+// Byte offset of element (n, k) (k a multiple of 8) in a [64 × 128] FP16 K-major operand stored with the
+// 128-byte swizzle: 64-element K blocks of 64 rows × 128 bytes, 8-row groups 1024 bytes apart, the 16-byte
 // chunks of row n permuted by XOR with n mod 8.
 __device__ __forceinline__ uint32_t sl_sw128(int n, int k) {
-  return static_cast<uint32_t>((k >> 5) * (kSlRows * 128) + (n >> 3) * 1024 + (n & 7) * 128 +
-                               ((((k & 31) >> 2) ^ (n & 7)) << 4));
+  return static_cast<uint32_t>((k >> 6) * (kSlRows * 128) + (n >> 3) * 1024 + (n & 7) * 128 +
+                               ((((k & 63) >> 3) ^ (n & 7)) << 4));
+}
+
+// x split as hi + lo·2^-11 with hi and lo FP16: hi = fp16(x), lo = fp16((x − hi)·2^11). The products of
+// two such splits, hi·hi + 2^-11(hi·lo + lo·hi), carry 22-bit operands like a three-pass TF32 split.
+__device__ __forceinline__ void sl_split(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn((x - __half2float(hi)) * kSlLoScale);
+}
+__device__ __forceinline__ uint32_t sl_pack(__half a, __half b) {
+  return static_cast<uint32_t>(__half_as_ushort(a)) | (static_cast<uint32_t>(__half_as_ushort(b)) << 16);
+}
+// The same split of two values with packed conversions; a in the low halves.
+__device__ __forceinline__ void sl_split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  const __half2 l = __floats2half2_rn((a - hf.x) * kSlLoScale, (b - hf.y) * kSlLoScale);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
 // LayerNorm over the head's 128 dims of one y row (Cells.slstm :139-140), out (+)= LN(y)·w; one warp, lane
@@ -412,10 +435,11 @@ __device__ __forceinline__ float4 sl_layernorm(float4 v4, float4 w4, float4 prev
 
 // The sLSTM recurrence (Cells.slstmRecurrence, Cells.java:170-218) as a per-step GEMM on the tensor cores.
 // A cluster of 4 CTAs takes 64 rows and one head; CTA q owns cell dims 32q .. 32q + 31, i.e. 128 of the
-// head's 512 gate columns. Per step, raw[m][n] = wx + b + Σ_p R[p][m]·y(t-1)[n][p] is one tcgen05 MMA
-// chain (M = 128 gate columns, N = 64 rows, K = 128) in three TF32 passes (R_hi·y_hi + R_hi·y_lo +
-// R_lo·y_hi, FP32-grade products), with R^T resident in tensor memory as the A operand and the
-// accumulator pre-loaded with wx + b. The gate update follows on the CUDA cores (gate order i, f, z, o),
+// head's 512 gate columns. Per step, raw[m][n] = wx + b + Σ_p R[p][m]·y(t-1)[n][p] is a tcgen05 MMA
+// chain (M = 128 gate columns, N = 64 rows, K = 128) over FP16 splits of both operands: D1 = wx + b +
+// R_hi·y_hi and D2 = R_hi·y_lo + R_lo·y_hi (lo parts scaled by 2^11), raw = D1 + 2^-11·D2, which keeps
+// 22-bit operands (FP32-grade products) in 24 MMAs of K = 16. R^T stays resident in tensor memory as the
+// A operand. The gate update follows on the CUDA cores (gate order i, f, z, o),
 // and each CTA's y(t) quarter is stored into every CTA's inbox with st.async, completing on the
 // receiver's mbarrier. While step t's MMAs run, each CTA applies the per-head LayerNorm (Cells.slstm
 // :139-140) to its 16 rows of y(t-1) straight from the inbox. wx [(r·S + t), ldwx] holds the headwise
@@ -440,7 +464,7 @@ __global__ void __launch_bounds__(kSlThreads, 1) slstm_kernel(const float* __res
   const int head = blockIdx.y;
   const int r0 = (blockIdx.x / kSlCta) * kSlRows;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int sp = warp & 3, half = warp >> 2;  // the TMEM lane quarter (= gate) and row half this warp moves
+  const int sp = warp & 3, rq = warp >> 2;  // the TMEM lane quarter (= gate) and row quarter this warp moves
   const int e = kSlE * static_cast<int>(q) + lane;
 
   for (int i = tid; i < 2 * kSlRows * kDh / 4; i += kSlThreads)  // y(-1) = 0 in both B parts
@@ -463,136 +487,161 @@ __global__ void __launch_bounds__(kSlThreads, 1) slstm_kernel(const float* __res
   tc_fence_after();
   const uint32_t tmem = *tslot;
   const uint32_t tlane = static_cast<uint32_t>(32 * sp) << 16;
-  // R^T of this CTA's gate columns into TMEM lanes 32g + e' (g = sp), K = p along the columns
-  if (half == 0) {
+  // R^T of this CTA's gate columns into TMEM lanes 32g + e' (g = sp), K = p along the columns, two FP16
+  // K elements per column (the lower K in the low half)
+  if (rq == 0) {
     const float* rp = R + static_cast<long long>(head) * kDh * 4 * kDh + sp * kDh + e;
     for (int k0 = 0; k0 < kDh; k0 += 32) {
-      uint32_t hi[32], lo[32];
+      uint32_t hi[16], lo[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float v = __ldg(rp + static_cast<long long>(k0 + i) * 4 * kDh);
-        const float h = round_tf32(v);
-        hi[i] = __float_as_uint(h);
-        lo[i] = __float_as_uint(round_tf32(v - h));
+      for (int i = 0; i < 16; ++i) {
+        __half h0, l0, h1, l1;
+        sl_split(__ldg(rp + static_cast<long long>(k0 + 2 * i) * 4 * kDh), h0, l0);
+        sl_split(__ldg(rp + static_cast<long long>(k0 + 2 * i + 1) * 4 * kDh), h1, l1);
+        hi[i] = sl_pack(h0, h1);
+        lo[i] = sl_pack(l0, l1);
       }
-      tmem_st_32x32b_x32(tmem + tlane + k0, hi);
-      tmem_st_32x32b_x32(tmem + tlane + 128 + k0, lo);
+      tmem_st_32x32b_x16(tmem + tlane + k0 / 2, hi);
+      tmem_st_32x32b_x16(tmem + tlane + 64 + k0 / 2, lo);
     }
     tmem_st_wait();
   }
   const float bcol = __ldg(bias + head * 4 * kDh + sp * kDh + e);
-  const float* wcol = wx + head * 4 * kDh + sp * kDh + e;
-  float wxr[32];
-  auto load_wx = [&](int t) {
+  // wx of a step: this CTA's 128 gate columns (4 gates × 32 dims) of the cluster's 64 rows, copied
+  // asynchronously into shared memory two steps ahead (8 × 16 bytes per thread); every step commits one
+  // cp.async group (empty past the last step), so waiting for all but the newest group means step t+1's
+  // slice has landed
+  auto wxs = [&](int t) { return reinterpret_cast<float*>(sm + kSlWx) + (t & 1) * kSlRows * kSlM; };
+  auto stage_wx = [&](int t) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int row = r0 + 32 * half + i;
-      wxr[i] = row < rows ? wcol[(static_cast<long long>(row) * S + t) * ldwx] : 0.0f;
+    for (int j = 0; j < kSlRows * kSlM / 4 / kSlThreads; ++j) {
+      if (t >= S) break;
+      const int cidx = tid + j * kSlThreads, nn = cidx >> 5, c4 = cidx & 31, g = c4 >> 3, e4 = c4 & 7;
+      const int row = r0 + nn;
+      const float* src = wx + (static_cast<long long>(row < rows ? row : 0) * S + t) * ldwx + head * 4 * kDh +
+                         g * kDh + kSlE * static_cast<int>(q) + 4 * e4;
+      cp_async16(wxs(t) + nn * kSlM + 4 * c4, src, row < rows ? 16 : 0);
     }
+    cp_async_commit();
   };
-  load_wx(0);
-  // LayerNorm rows of this CTA: 16q + 2·warp + j; out's previous value fetched a step ahead
+  stage_wx(0);
+  stage_wx(1);
+  // LayerNorm rows of this CTA: 16q + (warp - 1) + 15j (j < 2, below 16) on warps 1-15, so that warp 0,
+  // whose lane 0 issues the MMAs, has none; out's previous value is fetched a step ahead
   const float4 w4 = __ldg(reinterpret_cast<const float4*>(norm_w + head * kDh + 4 * lane));
-  const int lrow = 16 * static_cast<int>(q) + 2 * warp;
   float4 prev[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  auto lrow = [&](int j) { return warp - 1 + 15 * j; };  // within the cluster's 64 rows: + 16q
+  auto has_row = [&](int j) { return warp > 0 && lrow(j) < 16 && r0 + 16 * static_cast<int>(q) + lrow(j) < rows; };
   auto out_at = [&](int j, int t) {
-    return out + (static_cast<long long>(r0 + lrow + j) * S + t) * ld_out + head * kDh + 4 * lane;
+    return out + (static_cast<long long>(r0 + 16 * static_cast<int>(q) + lrow(j)) * S + t) * ld_out + head * kDh +
+           4 * lane;
   };
   auto load_prev = [&](int t) {
 #pragma unroll
     for (int j = 0; j < 2; ++j)
-      if (accumulate && r0 + lrow + j < rows) prev[j] = *reinterpret_cast<const float4*>(out_at(j, t));
+      if (accumulate && has_row(j)) prev[j] = *reinterpret_cast<const float4*>(out_at(j, t));
   };
   auto layernorm = [&](int t) {  // y(t), complete in inbox t & 1
-    const float* ib = inbox + (t & 1) * kSlRows * kDh;
+    const float* ib = inbox + (t & 1) * kSlRows * kDh + 16 * static_cast<int>(q) * kDh;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
-      const float4 v4 = *reinterpret_cast<const float4*>(ib + (lrow + j) * kDh + 4 * lane);
+      if (warp == 0 || lrow(j) >= 16) break;  // warp-uniform
+      const float4 v4 = *reinterpret_cast<const float4*>(ib + lrow(j) * kDh + 4 * lane);
       const float4 o = sl_layernorm(v4, w4, prev[j], accumulate);
-      if (r0 + lrow + j < rows) *reinterpret_cast<float4*>(out_at(j, t)) = o;
+      if (has_row(j)) *reinterpret_cast<float4*>(out_at(j, t)) = o;
     }
   };
   load_prev(0);
-  float c[8], n[8], m[8];
+  float c[4], n[4], m[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) c[i] = n[i] = m[i] = 0.0f;
+  for (int i = 0; i < 4; ++i) c[i] = n[i] = m[i] = 0.0f;
   bool ok = true;
-  cluster_sync();  // every CTA's barriers set before any st.async reaches them
-  const uint32_t idesc = idesc_f32acc(2, kSlM, kSlRows);
+  cp_async_wait_all();
+  cluster_sync();  // every CTA's barriers set before any st.async reaches them; wx(0) staged
+  const uint32_t idesc = idesc_f32acc(0, kSlM, kSlRows);  // FP16 A and B
   for (int t = 0; t < S; ++t) {
     if (t > 0) {
-      // y(t-1) of the whole cluster → the B operand, split into TF32 hi and lo parts
+      // y(t-1) of the whole cluster → the B operand, split into FP16 hi and lo·2^11 parts
       const int b = (t - 1) & 1;
       if (!mbar_wait(&full[b], ((t - 1) >> 1) & 1, kSlWaitNs)) ok = false;
       if (tid == 0 && t + 1 < S) mbar_arrive_expect_tx(&full[b], kSlInBytes);  // y(t+1) lands in inbox b
       const float* ib = inbox + b * kSlRows * kDh;
 #pragma unroll
-      for (int j = 0; j < kSlRows * kDh / 4 / kSlThreads; ++j) {
-        const int cidx = tid + j * kSlThreads, nn = cidx >> 5, k = 4 * (cidx & 31);
-        const float4 v = *reinterpret_cast<const float4*>(ib + nn * kDh + k);
-        const float4 h = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
-        const float4 l = make_float4(round_tf32(v.x - h.x), round_tf32(v.y - h.y), round_tf32(v.z - h.z),
-                                     round_tf32(v.w - h.w));
+      for (int j = 0; j < kSlRows * kDh / 8 / kSlThreads; ++j) {
+        const int cidx = tid + j * kSlThreads, nn = cidx >> 4, k = 8 * (cidx & 15);
+        const float4 v0 = *reinterpret_cast<const float4*>(ib + nn * kDh + k);
+        const float4 v1 = *reinterpret_cast<const float4*>(ib + nn * kDh + k + 4);
+        const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sl_split2(x[2 * u], x[2 * u + 1], h[u], l[u]);
         const uint32_t off = sl_sw128(nn, k);
-        *reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(bhi) + off) = h;
-        *reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(blo) + off) = l;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(bhi) + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(blo) + off) = make_uint4(l[0], l[1], l[2], l[3]);
       }
       fence_proxy_async_smem();
     }
-    {  // accumulator = wx(t) + b for this warp's (gate columns, rows)
-      uint32_t d[32];
+    {  // main accumulator = wx(t) + b for this warp's (gate columns, rows)
+      uint32_t d[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) d[i] = __float_as_uint(wxr[i] + bcol);
-      tmem_st_32x32b_x32(tmem + tlane + 256 + 32 * half, d);
+      for (int i = 0; i < 16; ++i) d[i] = __float_as_uint(wxs(t)[(16 * rq + i) * kSlM + 32 * sp + lane] + bcol);
+      tmem_st_32x32b_x16(tmem + tlane + 128 + 16 * rq, d);
       tmem_st_wait();
     }
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
+      // D1 += R_hi·y_hi; D2 = R_hi·y_lo + R_lo·y_hi (K = 16 per MMA: 8 TMEM columns of A, 32 bytes of B)
 #pragma unroll
       for (int pass = 0; pass < 3; ++pass) {
-        const uint32_t a = tmem + (pass == 2 ? 128u : 0u);
+        const uint32_t a = tmem + (pass == 2 ? 64u : 0u);
         const uint32_t bb = smem_u32(pass == 1 ? blo : bhi);
+        const uint32_t d = tmem + (pass == 0 ? 128u : 192u);
 #pragma unroll
-        for (int k = 0; k < kDh / 8; ++k)
-          umma_tf32_ts(tmem + 256, a + 8 * k, sdesc_k_sw128(bb + (k >> 2) * (kSlRows * 128) + (k & 3) * 32), idesc,
-                       1);
+        for (int k = 0; k < kDh / 16; ++k)
+          umma_f16_ts(d, a + 8 * k, sdesc_k_sw128(bb + (k >> 2) * (kSlRows * 128) + (k & 3) * 32), idesc,
+                      pass == 1 && k == 0 ? 0u : 1u);
       }
       umma_commit(mma_bar);
     }
     // while the MMAs run: the next step's wx and the LayerNorm of y(t-1)
-    if (t + 1 < S) load_wx(t + 1);
+    stage_wx(t + 2);  // into the slice read before the barrier above
     if (t > 0) {
       layernorm(t - 1);
       load_prev(t);
     }
     if (!mbar_wait(mma_bar, t & 1, kSlWaitNs)) ok = false;
     tc_fence_after();
-    {  // raw gates out of TMEM: gate sp of cell dim e for rows 32·half .. 32·half + 31
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem + tlane + 256 + 32 * half, v);
+    {  // raw gates out of TMEM: gate sp of cell dim e for rows 16·rq .. 16·rq + 15, D1 + 2^-11·D2
+      uint32_t v[16], w[16];
+      tmem_ld_32x32b_x16(tmem + tlane + 128 + 16 * rq, v);
+      tmem_ld_32x32b_x16(tmem + tlane + 192 + 16 * rq, w);
       tmem_ld_wait();
       float* rg = raw + sp * kSlRows * kSlE;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) rg[(32 * half + i) * kSlE + lane] = __uint_as_float(v[i]);
+      for (int i = 0; i < 16; ++i)
+        rg[(16 * rq + i) * kSlE + lane] = fmaf(__uint_as_float(w[i]), 1.0f / kSlLoScale, __uint_as_float(v[i]));
     }
     __syncthreads();
-    // gate update of cell dim e for rows warp + 8i; the exponentials of the bounded terms and the
-    // divisions by n ≥ 1 use the fast intrinsics (errors of a few ulp, below the TF32-split products')
+    // gate update of cell dim e for rows warp + 16i; the exponentials of the bounded terms and the
+    // divisions by n ≥ 1 use the fast intrinsics (errors of a few ulp, below the split products')
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int rl = warp + 8 * i;
+    for (int i = 0; i < 4; ++i) {
+      const int rl = warp + 16 * i;
       const float ir = raw[(0 * kSlRows + rl) * kSlE + lane], fr = raw[(1 * kSlRows + rl) * kSlE + lane],
                   zr = raw[(2 * kSlRows + rl) * kSlE + lane], orw = raw[(3 * kSlRows + rl) * kSlE + lane];
       const float logf_ = (fminf(fr, 0.0f) - __logf(1.0f + __expf(-fabsf(fr)))) + m[i];
       const float mn = t == 0 ? ir : fmaxf(ir, logf_);
       const float ig = __expf(ir - mn), fg = __expf(logf_ - mn);
-      c[i] = fg * c[i] + ig * tanhf(zr);
+      // tanh(z) = sign(z)·(1 − 2/(e^{2|z|} + 1)) on the fast exponential (absolute error ~1e-7)
+      const float th = copysignf(1.0f - __fdividef(2.0f, __expf(2.0f * fabsf(zr)) + 1.0f), zr);
+      c[i] = fg * c[i] + ig * th;
       n[i] = fmaxf(fg * n[i] + ig, 1.0f);
       m[i] = mn;
       ys[rl * kSlYPitch + lane] = __fdividef(__fdividef(c[i], n[i]), 1.0f + __expf(-orw));
     }
+    cp_async_wait_group<1>();  // wx(t + 1) staged by every thread once past the barrier
     __syncthreads();
     // y(t) quarter → every CTA's inbox (t & 1)
 #pragma unroll
