@@ -78,16 +78,6 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return static_cast<uint32_t>(r * 128 + ((((c >> 3) ^ r) & 7) << 4) + ((c & 7) << 1));
 }
 
-// BlockLayout.timeAllowed (mode 0) or key liveness (mode 1) for query q and key k; `bits` holds the
-// row's key_valid (mode 0) or live (mode 1) flags, one bit per key.
-__device__ __forceinline__ bool allowed(const AttnArgs& a, const uint32_t* bits, bool known, int q, int k) {
-  const bool flag = (bits[k >> 5] >> (k & 31)) & 1u;
-  if (a.mask_mode == 1) return k < a.n && flag;
-  if (q < a.enc) return k < a.enc && (k == q || (flag && (k <= q || known)));
-  if (k < a.enc) return k < a.ll && flag;
-  return k <= q && k < a.n;
-}
-
 // Bits of the keys in [lo, hi) that fall in 32-key word w.
 __device__ __forceinline__ uint32_t range_bits(int w, int lo, int hi) {
   const int a = max(lo - 32 * w, 0), b = min(hi - 32 * w, 32);
@@ -169,6 +159,15 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
     tma_load_2d(ks, &tmKV, &bars[0], a.d + hh * 64, static_cast<int>(row0));
     tma_load_2d(vs, &tmKV, &bars[0], 2 * a.d + hh * 64, static_cast<int>(row0));
   }
+  // the first tail round's q and gate rows (queries past the MMA tile), one 16-byte chunk per thread,
+  // in flight during the TMA wait
+  uint4 pq = make_uint4(0u, 0u, 0u, 0u), pg = make_uint4(0u, 0u, 0u, 0u);
+  if (tid < min(kTailQ, n - kTcQ) * 8) {
+    const long long tok = row0 + kTcQ + (tid >> 3);
+    pq = __ldg(reinterpret_cast<const uint4*>(qkv + tok * a.ld_qkv + hh * 64) + (tid & 7));
+    if (a.gate)
+      pg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.gate) + tok * a.ld_gate + hh * 64) + (tid & 7));
+  }
   // this thread's query and its allowed keys as bit words
   const int q = tid;
   const bool my_row = q < n;
@@ -211,42 +210,41 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   const float sl2 = a.scale * 1.4426950408889634f;
 
   // queries past the MMA tile, kTailQ at a time by all threads on the CUDA cores: scores with a thread
-  // per key, softmax with a warp per query, P·V with a thread per (query, dim)
+  // per key (its K row in registers), softmax with a warp per query, P·V with a thread per (query, 8 dims)
+  // over a share of the keys, then the shares summed in a fixed order
   if (ok1) {
     for (int t0 = kTcQ; t0 < n; t0 += kTailQ) {
       const int nt = min(kTailQ, n - t0);
-      for (int i = tid; i < nt * 64; i += kTcThreads) {
-        const int j = i >> 6, e = i & 63;
-        tq[i] = unpack2<T>(*reinterpret_cast<const uint32_t*>(qkv + (row0 + t0 + j) * a.ld_qkv + hh * 64 + (e & ~1)))
-                    .x * (e & 1 ? 0.0f : 1.0f) +
-                unpack2<T>(*reinterpret_cast<const uint32_t*>(qkv + (row0 + t0 + j) * a.ld_qkv + hh * 64 + (e & ~1)))
-                    .y * (e & 1 ? 1.0f : 0.0f);
+      if (tid < nt * 8) {
+        uint4 u = pq;
+        if (t0 != kTcQ)
+          u = __ldg(reinterpret_cast<const uint4*>(qkv + (row0 + t0 + (tid >> 3)) * a.ld_qkv + hh * 64) + (tid & 7));
+        const float2 f0 = unpack2<T>(u.x), f1 = unpack2<T>(u.y), f2 = unpack2<T>(u.z), f3 = unpack2<T>(u.w);
+        float4* dst = reinterpret_cast<float4*>(tq + (tid >> 3) * 64 + 8 * (tid & 7));
+        dst[0] = make_float4(f0.x, f0.y, f1.x, f1.y);
+        dst[1] = make_float4(f2.x, f2.y, f3.x, f3.y);
       }
       __syncthreads();
       for (int k = tid; k < sh.nkl; k += kTcThreads) {
-        float acc[kTailQ];
+        float kv[64];
 #pragma unroll
-        for (int j = 0; j < kTailQ; ++j) acc[j] = 0.0f;
-#pragma unroll 2
         for (int c = 0; c < 8; ++c) {
           const uint4 u = *reinterpret_cast<const uint4*>(ks + sw128(k, 8 * c));
           const float2 f0 = unpack2<T>(u.x), f1 = unpack2<T>(u.y), f2 = unpack2<T>(u.z), f3 = unpack2<T>(u.w);
-#pragma unroll
-          for (int j = 0; j < kTailQ; ++j) {
-            if (j < nt) {
-              const float4 qa = *reinterpret_cast<const float4*>(tq + j * 64 + 8 * c);
-              const float4 qb = *reinterpret_cast<const float4*>(tq + j * 64 + 8 * c + 4);
-              acc[j] = fmaf(qa.x, f0.x, fmaf(qa.y, f0.y, fmaf(qa.z, f1.x, fmaf(qa.w, f1.y, acc[j]))));
-              acc[j] = fmaf(qb.x, f2.x, fmaf(qb.y, f2.y, fmaf(qb.z, f3.x, fmaf(qb.w, f3.y, acc[j]))));
-            }
-          }
+          kv[8 * c + 0] = f0.x, kv[8 * c + 1] = f0.y, kv[8 * c + 2] = f1.x, kv[8 * c + 3] = f1.y;
+          kv[8 * c + 4] = f2.x, kv[8 * c + 5] = f2.y, kv[8 * c + 6] = f3.x, kv[8 * c + 7] = f3.y;
         }
+        for (int j = 0; j < nt; ++j) {
+          const float4* qj = reinterpret_cast<const float4*>(tq + j * 64);
+          float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll
-        for (int j = 0; j < kTailQ; ++j) {
-          if (j < nt) {
-            const bool al = k < n && ((allowed_word(a, bits, known, t0 + j, k >> 5) >> (k & 31)) & 1u);
-            tsc[j * kTcMaxTokens + k] = al ? acc[j] * sl2 : -INFINITY;
+          for (int c = 0; c < 16; c += 2) {
+            const float4 qa = qj[c], qb = qj[c + 1];
+            acc0 = fmaf(qa.x, kv[4 * c + 0], fmaf(qa.y, kv[4 * c + 1], fmaf(qa.z, kv[4 * c + 2], fmaf(qa.w, kv[4 * c + 3], acc0))));
+            acc1 = fmaf(qb.x, kv[4 * c + 4], fmaf(qb.y, kv[4 * c + 5], fmaf(qb.z, kv[4 * c + 6], fmaf(qb.w, kv[4 * c + 7], acc1))));
           }
+          const bool al = k < n && ((allowed_word(a, bits, known, t0 + j, k >> 5) >> (k & 31)) & 1u);
+          tsc[j * kTcMaxTokens + k] = al ? (acc0 + acc1) * sl2 : -INFINITY;
         }
       }
       __syncthreads();
@@ -267,53 +265,82 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
         if (lane == 0) tl[j] = l;
       }
       __syncthreads();
-      // P·V: a thread owns 8 dims (one 16-byte chunk of a V row) of one query over every G-th key; the G
-      // partial sums are then added in a fixed order
+      // P·V: a thread owns 8 dims (one 16-byte chunk of a V row) of one query over every G-th key, two keys
+      // per iteration into separate accumulators; keys with p = 0 are skipped by select (their V rows may
+      // hold another row's values)
       const int items = nt * 8;
       const int groups = kTcThreads / items;  // ≥ 2 for nt ≤ kTailQ
       if (tid < items * groups) {
         const int item = tid % items, g = tid / items;
         const int j = item >> 3, c = item & 7;
         const float* pj = tsc + j * kTcMaxTokens;
-        float acc[8];
+        float acc[2][8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u] = 0.0f;
-        for (int k = g; k < sh.nkl; k += groups) {
-          const float p = pj[k];
-          if (p != 0.0f) {
-            const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(k, 8 * c));
+        for (int u = 0; u < 8; ++u) acc[0][u] = acc[1][u] = 0.0f;
+        int k = g;
+        for (; k + groups < sh.nkl; k += 2 * groups) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int kk = k + h * groups;
+            const float p = pj[kk];
+            const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(kk, 8 * c));
             const float2 v0 = unpack2<__half>(vv.x), v1 = unpack2<__half>(vv.y), v2 = unpack2<__half>(vv.z),
                          v3 = unpack2<__half>(vv.w);
-            acc[0] = fmaf(p, v0.x, acc[0]), acc[1] = fmaf(p, v0.y, acc[1]);
-            acc[2] = fmaf(p, v1.x, acc[2]), acc[3] = fmaf(p, v1.y, acc[3]);
-            acc[4] = fmaf(p, v2.x, acc[4]), acc[5] = fmaf(p, v2.y, acc[5]);
-            acc[6] = fmaf(p, v3.x, acc[6]), acc[7] = fmaf(p, v3.y, acc[7]);
+            const float vf[8] = {v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, v3.x, v3.y};
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[h][u] = p != 0.0f ? fmaf(p, vf[u], acc[h][u]) : acc[h][u];
           }
         }
+        if (k < sh.nkl) {
+          const float p = pj[k];
+          const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(k, 8 * c));
+          const float2 v0 = unpack2<__half>(vv.x), v1 = unpack2<__half>(vv.y), v2 = unpack2<__half>(vv.z),
+                       v3 = unpack2<__half>(vv.w);
+          const float vf[8] = {v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, v3.x, v3.y};
+#pragma unroll
+          for (int u = 0; u < 8; ++u) acc[0][u] = p != 0.0f ? fmaf(p, vf[u], acc[0][u]) : acc[0][u];
+        }
         float4* red = reinterpret_cast<float4*>(tred + (g * items + item) * 8);
-        red[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        red[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        red[0] = make_float4(acc[0][0] + acc[1][0], acc[0][1] + acc[1][1], acc[0][2] + acc[1][2], acc[0][3] + acc[1][3]);
+        red[1] = make_float4(acc[0][4] + acc[1][4], acc[0][5] + acc[1][5], acc[0][6] + acc[1][6], acc[0][7] + acc[1][7]);
       }
       __syncthreads();
-      for (int i = tid; i < nt * 64; i += kTcThreads) {
-        const int j = i >> 6, e = i & 63;
-        const int item = j * 8 + (e >> 3);
-        float o = 0.0f;
-        for (int g = 0; g < groups; ++g) o += tred[(g * items + item) * 8 + (e & 7)];
+      // output: a thread per (query, 16-byte chunk): the shares in order, 1/l, the gate, one vector store
+      if (tid < items) {
+        const int j = tid >> 3, c = tid & 7;
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = 0.0f;
+        for (int g = 0; g < groups; ++g) {
+          const float4* r = reinterpret_cast<const float4*>(tred + (g * items + tid) * 8);
+          const float4 r0 = r[0], r1 = r[1];
+          o[0] += r0.x, o[1] += r0.y, o[2] += r0.z, o[3] += r0.w;
+          o[4] += r1.x, o[5] += r1.y, o[6] += r1.z, o[7] += r1.w;
+        }
         const float l = tl[j];
-        o *= l > 0.0f ? 1.0f / l : 0.0f;
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
         const long long tok = row0 + t0 + j;
-        if (a.gate) o *= unpack2<T>(*reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.gate) +
-                                                                      tok * a.ld_gate + hh * 64 + (e & ~1)))
-                             .x * (e & 1 ? 0.0f : 1.0f) +
-                         unpack2<T>(*reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.gate) +
-                                                                      tok * a.ld_gate + hh * 64 + (e & ~1)))
-                             .y * (e & 1 ? 1.0f : 0.0f);
-        T* op = static_cast<T*>(a.out_hi) + tok * a.ld_out + hh * 64 + e;
-        if constexpr (std::is_same<T, __half>::value)
-          *op = __float2half_rn(fminf(fmaxf(o, -65504.0f), 65504.0f));
-        else
-          *op = __float2bfloat16_rn(o);
+        uint4 gu = pg;
+        if (a.gate && t0 != kTcQ)
+          gu = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.gate) + tok * a.ld_gate + hh * 64) + c);
+        const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+        uint32_t pk[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float x0 = o[2 * u] * inv, x1 = o[2 * u + 1] * inv;
+          if (a.gate) {
+            const float2 g2 = unpack2<T>(gw[u]);
+            x0 *= g2.x;
+            x1 *= g2.y;
+          }
+          if constexpr (std::is_same<T, __half>::value) {
+            x0 = fminf(fmaxf(x0, -65504.0f), 65504.0f);
+            x1 = fminf(fmaxf(x1, -65504.0f), 65504.0f);
+          }
+          pk[u] = pack2<T>(x0, x1);
+        }
+        *reinterpret_cast<uint4*>(static_cast<T*>(a.out_hi) + tok * a.ld_out + hh * 64 + 8 * c) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       __syncthreads();
     }
