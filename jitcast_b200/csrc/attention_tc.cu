@@ -32,11 +32,12 @@ namespace {
 constexpr int kTcThreads = 128;
 constexpr int kTcQ = 128;        // queries per MMA tile (TMEM lanes)
 constexpr int kTcMaxTokens = 256;
-constexpr uint32_t kErrAttnWait = 1u << 5;
+constexpr int kTcExtraKeys = 8;  // keys past a 128-key S MMA the main rows may score on the CUDA cores
 
 struct TcShape {
   int nkl;        // K/V rows staged (round_up(n, 16))
   int nkm;        // keys in the S = Q·Kᵀ MMA (multiple of 16, ≤ nkl)
+  int nx;         // live keys past the MMA's 128 (mode 1, at most kTcExtraKeys): CUDA-core scores and P·V
   int o_col;      // first TMEM column of O
   int tmem_cols;  // TMEM columns allocated (power of two)
   int k_off, v_off, p_off, bar_off;  // byte offsets into the 1024-aligned dynamic shared memory
@@ -209,6 +210,35 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   const bool ok1 = *abort_flag == 0;
   const float sl2 = a.scale * 1.4426950408889634f;
 
+  // keys past a 128-key S MMA (Chronos-2's [REG] and future tokens, mode 1): raw scores from this thread's
+  // Q row, taken before the tail rounds reuse Q's tile; they join the softmax's max and sum, and their P·V
+  // is added on the CUDA cores in the epilogue
+  float xs[kTcExtraKeys];  // scores, then probabilities
+#pragma unroll
+  for (int i = 0; i < kTcExtraKeys; ++i) xs[i] = -INFINITY;
+  if (ok1 && sh.nx > 0) {
+    float xa[kTcExtraKeys];
+#pragma unroll
+    for (int i = 0; i < kTcExtraKeys; ++i) xa[i] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 qu = *reinterpret_cast<const uint4*>(qs + sw128(tid, 8 * c));
+      const float2 q0 = unpack2<T>(qu.x), q1 = unpack2<T>(qu.y), q2 = unpack2<T>(qu.z), q3 = unpack2<T>(qu.w);
+#pragma unroll
+      for (int i = 0; i < kTcExtraKeys; ++i) {
+        if (i >= sh.nx) break;
+        const uint4 ku = *reinterpret_cast<const uint4*>(ks + sw128(kTcQ + i, 8 * c));
+        const float2 k0 = unpack2<T>(ku.x), k1 = unpack2<T>(ku.y), k2 = unpack2<T>(ku.z), k3 = unpack2<T>(ku.w);
+        xa[i] = fmaf(q0.x, k0.x, fmaf(q0.y, k0.y, fmaf(q1.x, k1.x, fmaf(q1.y, k1.y, xa[i]))));
+        xa[i] = fmaf(q2.x, k2.x, fmaf(q2.y, k2.y, fmaf(q3.x, k3.x, fmaf(q3.y, k3.y, xa[i]))));
+      }
+    }
+    const uint32_t xw = bits[kTcQ / 32];
+#pragma unroll
+    for (int i = 0; i < kTcExtraKeys; ++i) xs[i] = i < sh.nx && ((xw >> i) & 1u) ? xa[i] : -INFINITY;
+  }
+  if (sh.nx > 0) __syncthreads();  // every Q row read before the tail rounds overwrite Q's tile
+
   // queries past the MMA tile, kTailQ at a time by all threads on the CUDA cores: scores with a thread
   // per key (its K row in registers), softmax with a warp per query, P·V with a thread per (query, 8 dims)
   // over a share of the keys, then the shares summed in a fixed order
@@ -368,7 +398,18 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
           if ((mw >> j) & 1u) mx = fmaxf(mx, __uint_as_float(r[j]));
       }
     }
+    if (sh.nx > 0) {
+#pragma unroll
+      for (int i = 0; i < kTcExtraKeys; ++i) mx = fmaxf(mx, xs[i]);
+    }
     const float mo = mx == -INFINITY ? 0.0f : mx * sl2;
+    if (sh.nx > 0) {
+#pragma unroll
+      for (int i = 0; i < kTcExtraKeys; ++i) {
+        xs[i] = xs[i] == -INFINITY ? 0.0f : ex2f(fmaf(xs[i], sl2, -mo));
+        l += xs[i];
+      }
+    }
 #pragma unroll
     for (int c = 0; c < kTcMaxTokens / 32; ++c) {
       if (32 * c >= sh.nkm) continue;
@@ -443,6 +484,23 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
       tmem_ld_32x32b_x32(lane_base + static_cast<uint32_t>(32 * half), r);
       tmem_ld_wait();
       if (!my_row) continue;
+      if (sh.nx > 0) {  // P·V of the keys past the S MMA, from the (FP16) V tile
+#pragma unroll
+        for (int i = 0; i < kTcExtraKeys; ++i) {
+          if (i >= sh.nx || xs[i] == 0.0f) continue;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(kTcQ + i, 32 * half + 8 * u));
+            const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int w = 0; w < 4; ++w) {
+              const float2 v2 = unpack2<__half>(vw[w]);
+              r[8 * u + 2 * w] = __float_as_uint(fmaf(xs[i], v2.x, __uint_as_float(r[8 * u + 2 * w])));
+              r[8 * u + 2 * w + 1] = __float_as_uint(fmaf(xs[i], v2.y, __uint_as_float(r[8 * u + 2 * w + 1])));
+            }
+          }
+        }
+      }
       uint32_t pk[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
@@ -484,6 +542,13 @@ cudaError_t launch_time_attention_tc(const AttnArgs& a, cudaStream_t s) {
   // encoder queries of mask mode 0 read encoder keys only
   sh.nkm = (a.mask_mode == 0 && a.enc >= first) ? ((a.enc + 15) & ~15) : sh.nkl;
   if (sh.nkm > sh.nkl) sh.nkm = sh.nkl;
+  // mode 1 rows a few keys past 128 (Chronos-2: 128 context + [REG] + 4 future tokens): a 128-key S MMA and
+  // the rest on the CUDA cores keep TMEM at 128 columns, i.e. four CTAs per SM instead of two
+  sh.nx = 0;
+  if (a.mask_mode == 1 && a.n > kTcQ && a.n <= kTcQ + kTcExtraKeys) {
+    sh.nkm = kTcQ;
+    sh.nx = a.n - kTcQ;
+  }
   sh.o_col = 0;  // O reuses S's columns once the softmax has read S
   sh.tmem_cols = sh.nkm <= 128 ? 128 : 256;
   sh.k_off = kTcQ * 128;

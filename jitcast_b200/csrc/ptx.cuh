@@ -22,7 +22,8 @@ enum DeviceError : uint32_t {
   kErrTimeoutAcc = 1u << 2,    // epilogue waited too long for an accumulator
   kErrTimeoutAccFree = 1u << 3,// MMA issuer waited too long for the epilogue
   kErrTimeoutFlag = 1u << 4,   // a flag wait (tests of the bounded-wait path)
-  kErrTimeoutPeer = 1u << 5,   // a recurrent cell waited too long for its cluster peers' state
+  kErrAttnWait = 1u << 5,      // the attention kernel waited too long for a TMA load or an MMA
+  kErrTimeoutPeer = 1u << 6,   // a recurrent cell waited too long for its cluster peers' state
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
