@@ -664,6 +664,346 @@ __global__ void __launch_bounds__(kSlThreads, 1) slstm_kernel(const float* __res
   cluster_sync();  // no st.async in flight into any CTA of the cluster
 }
 
+constexpr int kMtThreads = 256;        // 8 warps: warp w moves TMEM lane quarter w % 4 and column half w / 4
+constexpr uint32_t kMtTmemCols = 256;  // S, then O: main [0, 128) and correction [128, 256)
+// shared memory (bytes from a 1024-aligned base): Q hi | Q lo | K hi | K lo ([128 rows × 64] FP16 K-major with
+// the 128-byte swizzle, 16 KB each), overlaid after the q·kᵀ MMA by C hi | C lo ([128 × 128 keys], two
+// 64-key atoms, 32 KB each); Vᵀ hi | Vᵀ lo ([128 dims × 128 keys], 32 KB each), which first holds the fp32
+// q|k rows as copied ([128][128], 512-byte pitch); the fp32 v rows as copied, later the o rows ([128][128],
+// 528-byte pitch so a warp reading one 16-byte chunk of 32 rows hits distinct banks); the gate arrays, the
+// row-half partial sums, mbarrier, TMEM address
+constexpr int kMtQ = 0, kMtK = 32768, kMtC = 0, kMtV = 65536, kMtQKs = 65536, kMtVs = 131072;
+constexpr int kMtVPitch = 528;
+constexpr int kMtGate = kMtVs + 128 * kMtVPitch;
+constexpr int kMtRed = kMtGate + 3 * 128 * 8 + 8 * 8;
+constexpr int kMtSmem = kMtRed + 2 * 2 * 128 * 4 + 64 + 1024;
+
+// Byte offset of element (r, c) in a [rows × 64] 16-bit K-major tile with the 128-byte swizzle (1024-aligned).
+__device__ __forceinline__ uint32_t mt_sw(int r, int c) {
+  return static_cast<uint32_t>(r * 128 + ((((c >> 3) ^ r) & 7) << 4) + ((c & 7) << 1));
+}
+
+// The mLSTM core with its per-head LayerNorm and σ(o) gate (Cells.mlstmCore :74-118, Cells.mlstm :58-69) on the
+// tensor cores, for sequences of at most 64 tokens. A CTA stacks two (row, head) pairs into the 128 rows of
+// a tcgen05 tile: S = q·kᵀ (M 128 × N 128 × K 64; the two off-diagonal 64 × 64 blocks are discarded) and
+// O = C·v (M 128 × N 128 × K 128, C zero outside the pair's block) run over FP16 splits of both operands —
+// x = hi + 2^-11·lo, main = hi·hi, correction = hi·lo + lo·hi, result = main + 2^-11·correction — which
+// keeps 22-bit operands (FP32-grade products). Each C row is scaled by a power of two before its split so
+// small decay weights keep their bits. The gates (log-sigmoid, prefix sums, the stabiliser) stay in double,
+// as the reference. q, k, v and o arrive by cp.async; every stacked row is worked by two threads (TMEM column
+// halves) that exchange partial sums through shared memory. proj [(r·S + t), ldp] (16-byte aligned rows)
+// holds q (heads·64) | k | v (heads·128) | o (heads·128) | i (heads) | f (heads).
+__global__ void __launch_bounds__(kMtThreads, 1) mlstm_tc_kernel(const float* __restrict__ proj, long long ldp,
+                                                                 int rows, int S, int heads,
+                                                                 const float* __restrict__ norm_w, int out_kind,
+                                                                 void* out_hi, void* out_lo, long long ld_out,
+                                                                 uint32_t* err) {
+  extern __shared__ uint8_t sm_raw[];
+  uint8_t* sm = sm_raw + (((smem_u32(sm_raw) + 1023u) & ~1023u) - smem_u32(sm_raw));
+  double* aa = reinterpret_cast<double*>(sm + kMtGate);  // [128]: a[s] of the stacked keys
+  double* fq = aa + 128;                                  // [128]: F[t]
+  double* mq = fq + 128;                                  // [128]: M[t]
+  double* wt = mq + 128;                                  // [8]: per-warp totals of the scans
+  float* red = reinterpret_cast<float*>(sm + kMtRed);     // [2 stats][2 halves][128 rows]
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(red + 2 * 2 * 128);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ch = warp >> 2;                 // column half of this thread's TMEM row
+  const int row = 32 * (warp & 3) + lane;   // stacked row = TMEM lane this thread reads
+  const int pr = row >> 6, t = row & 63;    // pair of the CTA, token
+  const int npairs = rows * heads;
+  int prow[2], phead[2];
+  bool pval[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int pair = 2 * blockIdx.x + p;
+    pval[p] = pair < npairs;
+    prow[p] = pval[p] ? pair / heads : 0;
+    phead[p] = pval[p] ? pair % heads : 0;
+  }
+  const bool live = pval[pr] && t < S;
+  const int head = phead[pr];
+  const float* base = proj + (static_cast<long long>(prow[pr]) * S + (live ? t : 0)) * ldp;
+  const int k_off = heads * kDqk, v_off = 2 * heads * kDqk, o_off = v_off + heads * kDv, i_off = o_off + heads * kDv,
+            f_off = i_off + heads;
+  // the proj row of stacked row rr and whether it is a real token
+  auto row_base = [&](int rr, bool& ok, int& hd) {
+    const int pp = rr >> 6, tt = rr & 63;
+    ok = pval[pp] && tt < S;
+    hd = phead[pp];
+    return proj + (static_cast<long long>(prow[pp]) * S + (ok ? tt : 0)) * ldp;
+  };
+  if (warp == 0) {
+    tmem_alloc(tslot, kMtTmemCols);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(mma_bar, 1);
+    fence_mbar_init();
+  }
+  // q|k and v copied asynchronously (16 bytes per copy, zeros past the sequence): q|k rows into the Vᵀ region, v
+  // rows into their own buffer, 16 + 16 copies per thread
+  {
+    uint8_t* qks = sm + kMtQKs;
+    uint8_t* vs = sm + kMtVs;
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+      const int cidx = tid + kMtThreads * j, rr = cidx >> 5, c = cidx & 31;  // stacked row, 16-byte chunk
+      bool ok;
+      int hd;
+      const float* rb = row_base(rr, ok, hd);
+      const float* src = c < 16 ? rb + hd * kDqk + 4 * c : rb + k_off + hd * kDqk + 4 * (c - 16);
+      cp_async16(qks + rr * 512 + 16 * c, src, ok ? 16 : 0);
+    }
+    cp_async_commit();
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+      const int cidx = tid + kMtThreads * j, rr = cidx >> 5, c = cidx & 31;
+      bool ok;
+      int hd;
+      const float* rb = row_base(rr, ok, hd);
+      cp_async16(vs + rr * kMtVPitch + 16 * c, rb + v_off + hd * kDv + 4 * c, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  }
+  // gates of this row's token (double, as the reference), on the first column half; F = prefix sum of the
+  // log-sigmoid forget gates and M = max(0, prefix max of a = cap(i) − F) per pair: each warp scans 32 tokens,
+  // the pair's second warp adds the first's totals
+  double lf = 0.0, ai = 0.0;
+  if (ch == 0 && live) {
+    lf = log_sigmoid_d(static_cast<double>(soft_cap(base[f_off + head])));
+    ai = static_cast<double>(soft_cap(base[i_off + head]));
+  }
+  double F = lf;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, F, off);
+    if (lane >= off) F += y;
+  }
+  if (lane == 31) wt[warp] = F;
+  __syncthreads();
+  if (warp & 1) F += wt[warp - 1];
+  const double a = live ? ai - F : -INFINITY;
+  double M = a;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, M, off);
+    if (lane >= off) M = fmax(M, y);
+  }
+  __syncthreads();  // wt read above before it is reused
+  if (lane == 31) wt[warp] = M;
+  __syncthreads();
+  if (warp & 1) M = fmax(M, wt[warp - 1]);
+  if (ch == 0) {
+    aa[row] = a;
+    fq[row] = F;
+    mq[row] = fmax(0.0, M);
+  }
+  cp_async_wait_group<1>();  // this thread's q|k copies
+  __syncthreads();
+  // q|k rows → FP16 split tiles: a warp per row, lane l holding 4 consecutive floats (q for l < 16, k after)
+  {
+    const int hk = lane >> 4, c4 = lane & 15;
+    uint8_t* th = sm + (hk ? kMtK : kMtQ);
+    uint8_t* tl = th + 16384;
+#pragma unroll 4
+    for (int rr = warp; rr < 128; rr += kMtThreads / 32) {
+      const float4 v = *reinterpret_cast<const float4*>(sm + kMtQKs + rr * 512 + 16 * lane);
+      uint32_t h0, l0, h1, l1;
+      sl_split2(v.x, v.y, h0, l0);
+      sl_split2(v.z, v.w, h1, l1);
+      const uint32_t off = mt_sw(rr, 4 * c4);
+      *reinterpret_cast<uint2*>(th + off) = make_uint2(h0, h1);
+      *reinterpret_cast<uint2*>(tl + off) = make_uint2(l0, l1);
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t idesc = idesc_f32acc(0, 128, 128);  // FP16 A and B, M 128, N 128
+  bool ok = true;
+  if (tid == 0) {
+    const uint32_t qa = smem_u32(sm + kMtQ), ka = smem_u32(sm + kMtK);
+#pragma unroll
+    for (int pass = 0; pass < 3; ++pass) {
+      const uint32_t aop = qa + (pass == 2 ? 16384u : 0u), bop = ka + (pass == 1 ? 16384u : 0u);
+#pragma unroll
+      for (int k = 0; k < kDqk / 16; ++k)
+        umma_bf16(tmem + (pass == 0 ? 0u : 128u), sdesc_k_sw128(aop + 32 * k), sdesc_k_sw128(bop + 32 * k), idesc,
+                  pass == 2 || k > 0 ? 1u : 0u);
+    }
+    umma_commit(mma_bar);
+  }
+  // v rows → Vᵀ split tiles while the MMA runs: thread = (stacked key tid % 128, dim half tid / 128), reading
+  // 16 bytes of its row per step and writing 4 dims of its key column of atom key / 64
+  cp_async_wait_group<0>();
+  __syncthreads();
+  {
+    const int key = tid & 127, dh = tid >> 7;
+    uint8_t* vh = sm + kMtV + (key >> 6) * 16384;
+    uint8_t* vl = sm + kMtV + 32768 + (key >> 6) * 16384;
+    const uint8_t* vr = sm + kMtVs + key * kMtVPitch + 256 * dh;
+#pragma unroll 4
+    for (int d4 = 0; d4 < 16; ++d4) {
+      const float4 v = *reinterpret_cast<const float4*>(vr + 16 * d4);
+      const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        __half h, l;
+        sl_split(x[j], h, l);
+        const int d = 64 * dh + 4 * d4 + j;
+        *reinterpret_cast<__half*>(vh + mt_sw(d, key & 63)) = h;
+        *reinterpret_cast<__half*>(vl + mt_sw(d, key & 63)) = l;
+      }
+    }
+  }
+  __syncthreads();  // the v buffer is read; the o rows go there
+  {
+    uint8_t* os = sm + kMtVs;
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+      const int cidx = tid + kMtThreads * j, rr = cidx >> 5, c = cidx & 31;
+      bool okr;
+      int hd;
+      const float* rb = row_base(rr, okr, hd);
+      cp_async16(os + rr * kMtVPitch + 16 * c, rb + o_off + hd * kDv + 4 * c, okr ? 16 : 0);
+    }
+    cp_async_commit();
+  }
+  if (!mbar_wait(mma_bar, 0)) ok = false;
+  tc_fence_after();
+  // C row half: C[t, s] = (q_t·k_s)/8 · exp(a[s] − M[t]) for keys s = 32·ch + j ≤ t of this pair; the row is
+  // scaled by 2^e so its largest magnitude lies in [512, 1024) before the FP16 split (C hi/lo overlay Q and K,
+  // which the MMA above has read)
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16);
+  const double Mt = live ? mq[row] : 0.0;
+  const double mt = live ? fq[row] + Mt : 0.0;
+  float cv[32];
+  float den = 0.0f, cmax = 0.0f;
+  {
+    uint32_t sv[32], sc[32];
+    tmem_ld_32x32b_x32(lane_base + pr * 64 + 32 * ch, sv);
+    tmem_ld_32x32b_x32(lane_base + 128 + pr * 64 + 32 * ch, sc);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int s_ = 32 * ch + j;
+      float c = 0.0f;
+      if (live && s_ <= t) {
+        const float dot = fmaf(__uint_as_float(sc[j]), 1.0f / kSlLoScale, __uint_as_float(sv[j]));
+        c = dot * 0.125f * expf(static_cast<float>(aa[pr * 64 + s_] - Mt));
+      }
+      cv[j] = c;
+      den += c;
+      cmax = fmaxf(cmax, fabsf(c));
+    }
+  }
+  red[(0 * 2 + ch) * 128 + row] = den;
+  red[(1 * 2 + ch) * 128 + row] = cmax;
+  __syncthreads();
+  den = red[(0 * 2 + 0) * 128 + row] + red[(0 * 2 + 1) * 128 + row];
+  cmax = fmaxf(red[(1 * 2 + 0) * 128 + row], red[(1 * 2 + 1) * 128 + row]);
+  int ex = 0;
+  frexpf(cmax, &ex);
+  const float cscale = ldexpf(1.0f, 10 - ex);  // exact; cmax·cscale in [512, 1024)
+  {
+    uint8_t* chh = sm + kMtC + pr * 16384;
+    uint8_t* chl = sm + kMtC + 32768 + pr * 16384;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t h[4], l[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) sl_split2(cv[8 * c + 2 * u] * cscale, cv[8 * c + 2 * u + 1] * cscale, h[u], l[u]);
+      const uint32_t off = mt_sw(row, 32 * ch + 8 * c);
+      *reinterpret_cast<uint4*>(chh + off) = make_uint4(h[0], h[1], h[2], h[3]);
+      *reinterpret_cast<uint4*>(chl + off) = make_uint4(l[0], l[1], l[2], l[3]);
+      // the other pair's keys: zero
+      *reinterpret_cast<uint4*>(sm + kMtC + (1 - pr) * 16384 + off) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(sm + kMtC + 32768 + (1 - pr) * 16384 + off) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+    const uint32_t ca = smem_u32(sm + kMtC), va = smem_u32(sm + kMtV);
+#pragma unroll
+    for (int pass = 0; pass < 3; ++pass) {
+      const uint32_t aop = ca + (pass == 2 ? 32768u : 0u), bop = va + (pass == 1 ? 32768u : 0u);
+#pragma unroll
+      for (int k = 0; k < 128 / 16; ++k)
+        umma_bf16(tmem + (pass == 0 ? 0u : 128u), sdesc_k_sw128(aop + (k >> 2) * 16384 + 32 * (k & 3)),
+                  sdesc_k_sw128(bop + (k >> 2) * 16384 + 32 * (k & 3)), idesc, pass == 2 || k > 0 ? 1u : 0u);
+    }
+    umma_commit(mma_bar);
+  }
+  cp_async_wait_group<0>();  // this thread's o copies
+  if (!mbar_wait(mma_bar, 1)) ok = false;
+  tc_fence_after();
+  __syncthreads();  // every thread's o copies have landed
+  // h = O / (2^e · max(|den|, exp(−m)) + eps) over this thread's 64 dims; the head's LayerNorm with mean and
+  // variance summed over both halves; then the σ(o) gate
+  const float rnorm =
+      1.0f / (static_cast<float>(fmax(fabs(static_cast<double>(den)), exp(-mt)) + static_cast<double>(kMlstmEps)) *
+              cscale);
+  auto chunk = [&](int c, float (&v)[32]) {  // dims 64·ch + 32·c ..
+    uint32_t mv[32], cr[32];
+    tmem_ld_32x32b_x32(lane_base + 64 * ch + 32 * c, mv);
+    tmem_ld_32x32b_x32(lane_base + 128 + 64 * ch + 32 * c, cr);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(cr[j]), 1.0f / kSlLoScale, __uint_as_float(mv[j])) * rnorm;
+  };
+  float part = 0.0f;
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    float v[32];
+    chunk(c, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) part += v[j];
+  }
+  red[ch * 128 + row] = part;
+  __syncthreads();
+  const float mean = (red[row] + red[128 + row]) * (1.0f / kDv);
+  part = 0.0f;
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    float v[32];
+    chunk(c, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) part = fmaf(v[j] - mean, v[j] - mean, part);
+  }
+  red[256 + ch * 128 + row] = part;
+  __syncthreads();
+  const float var = (red[256 + row] + red[256 + 128 + row]) * (1.0f / kDv);
+  const float inv = rsqrtf(var + kNormEps);
+  const long long orow = (static_cast<long long>(prow[pr]) * S + t) * ld_out + head * kDv + 64 * ch;
+  const uint8_t* og = sm + kMtVs + row * kMtVPitch + 256 * ch;
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    float v[32];
+    chunk(c, v);  // warp-collective: every lane runs it, only live rows store
+    if (!live) continue;
+    const float4* wg = reinterpret_cast<const float4*>(norm_w + head * kDv + 64 * ch + 32 * c);
+#pragma unroll
+    for (int q4 = 0; q4 < 8; ++q4) {
+      const float4 o4 = *reinterpret_cast<const float4*>(og + 128 * c + 16 * q4), w4 = __ldg(wg + q4);
+      const float ov[4] = {o4.x, o4.y, o4.z, o4.w}, wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      float r4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) r4[e] = __fdividef((v[4 * q4 + e] - mean) * inv * wv[e], 1.0f + __expf(-ov[e]));
+      put_op4(out_kind, out_hi, out_lo, orow + 32 * c + 4 * q4, make_float4(r4[0], r4[1], r4[2], r4[3]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kMtTmemCols);
+  if (!ok && tid == 0) atomicOr(err, kErrTimeoutAcc);
+}
+
 // Attention across the kept rows of a group at one patch and head (CpuReference.variateMixer,
 // CpuReference.java:182-223): one warp per (kept query row, patch, head), 128-wide heads (4 per lane),
 // optional RMS qk-norm without weight (eps = FLT_EPSILON), covariate queries do not see targets.
@@ -1139,11 +1479,16 @@ cudaError_t run_cell(const Tirex2Engine& e, TxDevice& dv, TxPlan& p, const TxBlo
     GemmArgs g = gemm_args(op, in, T, B.proj);
     into_f32(g, p.proj, ldp, false);
     JC_TRY(gemm(dv, g, s, "gemm.proj"));
-    const size_t smem = mlstm_smem(S);
-    dim3 grid(rows * e.H, (S + kMlT - 1) / kMlT);
     prof.begin(s, "mlstm", 2.0 * rows * e.H * (0.5 * S * S) * (kDqk + kDv));
-    mlstm_kernel<<<grid, kMlThreads, smem, s>>>(p.proj, ldp, rows, S, e.H, B.head_norm, out_of_op(op), p.hn.hi,
-                                                  p.hn.lo, p.hn.ld);
+    if (S <= kMlT) {  // one 64-token block: the tensor-core kernel, two (row, head) pairs per CTA
+      const unsigned blocks = static_cast<unsigned>((static_cast<long long>(rows) * e.H + 1) / 2);
+      mlstm_tc_kernel<<<blocks, kMtThreads, kMtSmem, s>>>(p.proj, ldp, rows, S, e.H, B.head_norm, out_of_op(op),
+                                                          p.hn.hi, p.hn.lo, p.hn.ld, dv.err);
+    } else {
+      dim3 grid(rows * e.H, (S + kMlT - 1) / kMlT);
+      mlstm_kernel<<<grid, kMlThreads, mlstm_smem(S), s>>>(p.proj, ldp, rows, S, e.H, B.head_norm, out_of_op(op),
+                                                           p.hn.hi, p.hn.lo, p.hn.ld);
+    }
     prof.end(s);
     JC_TRY(cudaGetLastError());
     g = gemm_args(op, p.hn, T, B.out_proj);
@@ -1523,7 +1868,8 @@ jc_status jc_engine_create_tirex2(const jc_tirex2_desc* desc, const jc_tensor_vi
     if (cudaFuncSetAttribute(mlstm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
             cudaSuccess ||
         cudaFuncSetAttribute(slstm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(slstm_smem())) != cudaSuccess)
+                             static_cast<int>(slstm_smem())) != cudaSuccess ||
+        cudaFuncSetAttribute(mlstm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMtSmem) != cudaSuccess)
       return fail_cuda(cudaGetLastError(), "mLSTM / sLSTM kernel setup");
     std::string err;
     if (!upload(*e, hw, *dv, &err)) return fail(JC_ERR_OOM, err);
