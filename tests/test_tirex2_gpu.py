@@ -99,6 +99,27 @@ def test_qk_norm_off(jc):
     assert per_quantile_err(got, exp) < TOL["fp32"]
 
 
+@pytest.mark.parametrize("precision", ["fp32", "fp16", "bf16"])
+def test_sequence_longer_than_one_query_block(jc, precision):
+    # 72 patches: past the tensor-core mLSTM's 64-token tile (the CUDA-core kernel with two query blocks
+    # runs), and 72 sLSTM steps over two row clusters (70 rows, the second mostly empty); forget-gate biases
+    # as xLSTM initialises them
+    c = tiny_config(context_len=560, future_len=16)
+    assert (c.context_len + c.future_len) // c.patch_size > 64
+    w = tx.random_checkpoint(c, seed=11, norm_jitter=0.1, forget_bias=(3.0, 6.0))
+    b = univariate_batch(c, rows=70, seed=6)
+    exp = otx.Model(c, w).forward(b)
+    bar = TOL[precision]
+    if precision != "fp32":  # 72 recurrent steps amplify operand rounding: the module docstring's rule
+        floor = per_quantile_err(otx.Model(c, round_operands(w, precision)).forward(b), exp)
+        bar = max(bar, 1.5 * floor)
+    with tx.TiRex2Engine(c, w, precision=precision) as eng:
+        got = tx.B200TiRex2Forward(eng).forward(b)
+    err = per_quantile_err(got, exp)
+    print(f"tirex2 S=72 {precision}: per-quantile rel max err {err:.3e} (bar {bar:.3e})")
+    assert err < bar, f"{precision}: per-quantile rel max err {err:.3e} (bar {bar:.3e})"
+
+
 def test_sharded_two_slots_matches_one(jc, tiny):
     # two engine slots on one GPU exercise the shard/gather path of multi-GPU runs, groups kept whole
     c, w, _ = tiny
