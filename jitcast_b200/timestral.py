@@ -577,13 +577,18 @@ class TimestralEngine:
             raise RuntimeError("engine is closed")
         return self._h
 
-    def forward(self, inp: DeviceInputs) -> np.ndarray:
-        """raw [rows · h, P · Q] for a block's device inputs (host buffers)."""
+    def forward(self, inp: DeviceInputs, out: np.ndarray | None = None) -> np.ndarray:
+        """raw [rows · h, P · Q] for a block's device inputs (host buffers), written into ``out`` when given (a
+        C-contiguous float32 array of that shape, e.g. in pinned memory)."""
         c = self.config
-        raw = np.empty((inp.rows * inp.horizon, c.patch_size * c.num_quantiles), np.float32)
+        shape = (inp.rows * inp.horizon, c.patch_size * c.num_quantiles)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
         blk = inp.struct()
-        check(_lib.lib().jc_forward_timestral(self.handle, ctypes.byref(blk), raw.ctypes.data))
-        return raw
+        check(_lib.lib().jc_forward_timestral(self.handle, ctypes.byref(blk), out.ctypes.data))
+        return out
 
     def set_option(self, key: str, value: int) -> None:
         check(_lib.lib().jc_engine_set_option(self.handle, key.encode(), int(value)))
