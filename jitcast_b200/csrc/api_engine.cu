@@ -41,6 +41,8 @@ jc_status jc_engine_set_option(jc_engine* engine, const char* key, long long val
     if (value < 1) return fail(JC_ERR_INVALID_ARG, "max_plans must be >= 1");
     engine->max_plans = static_cast<int>(value);
     engine->drop_plans();
+  } else if (k == "buckets") {
+    engine->buckets = value != 0;
   } else if (k == "profile") {
     engine->profile = value != 0;
     for (int i = 0; i < engine->slots(); ++i) engine->profiler(i)->on = engine->profile;

@@ -157,6 +157,7 @@ struct jc_engine {
   bool use_graph = true;
   int max_plans = 8;
   bool profile = false;
+  bool buckets = true;  // plans (and graphs) for bucketed row counts (Timestral)
   virtual int slots() const = 0;
   virtual jc::DeviceSlot* slot(int i) = 0;
   virtual jc::Profiler* profiler(int i) = 0;

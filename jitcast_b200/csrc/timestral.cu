@@ -262,10 +262,36 @@ std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, i
   }
   if (cudaMemcpy(p->table, table.data(), sizeof(float) * table.size(), cudaMemcpyHostToDevice) != cudaSuccess)
     return nullptr;
+  // every row starts as a valid, independent dummy series (zero tokens, positions 0 .., all keys valid, its
+  // own group), so rows past a call's own (bucket padding) compute harmlessly and never reach a real row
+  {
+    std::vector<int> pos(static_cast<size_t>(T)), ones(static_cast<size_t>(encT), 1), gs(rows), ge(rows);
+    for (long long i = 0; i < T; ++i) pos[static_cast<size_t>(i)] = static_cast<int>(i % n) + enc;
+    for (int i = 0; i < rows; ++i) gs[i] = i, ge[i] = i + 1;
+    if (cudaMemset(p->tok_f32, 0, sizeof(float) * encT * 2 * e.P) != cudaSuccess ||
+        cudaMemcpy(p->pos, pos.data(), sizeof(int) * T, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(p->key_valid, ones.data(), sizeof(int) * encT, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemset(p->known, 0, sizeof(int) * rows) != cudaSuccess ||
+        cudaMemset(p->role, 0, sizeof(int) * rows) != cudaSuccess ||
+        cudaMemcpy(p->gs, gs.data(), sizeof(int) * rows, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(p->ge, ge.data(), sizeof(int) * rows, cudaMemcpyHostToDevice) != cudaSuccess)
+      return nullptr;
+  }
   p->h_pos.resize(T);
   p->h_gs.resize(rows);
   p->h_ge.resize(rows);
   return p;
+}
+
+// Rows a plan is built for: `x` itself up to 8, then the next multiple of a quarter of its power of two, so
+// padding adds at most 25 % and the number of shapes grows with the logarithm of the size (the reference's
+// bucket, TimestralForward.java:88-99).
+int bucket_rows(int x) {
+  if (x <= 8) return x;
+  int hb = 1;
+  while (hb <= (x - 1) / 2) hb *= 2;  // the highest power of two ≤ x − 1
+  const int step = hb / 4;
+  return (x + step - 1) / step * step;
 }
 
 TsPlan* get_plan(TimestralEngine& e, TsDevice& dv, int rows, int enc, int h, int ll, int cov, std::string* err) {
@@ -515,7 +541,8 @@ jc_status run_shard(TimestralEngine& e, TsDevice& dv, const jc_timestral_block* 
       return JC_ERR_CUDA;
     }
   }
-  TsPlan* p = get_plan(e, dv, r1 - r0, b->encoder, b->horizon, b->context_patches, b->covariates, err);
+  const int prows = e.buckets ? bucket_rows(r1 - r0) : r1 - r0;  // the plan's rows ≥ this shard's
+  TsPlan* p = get_plan(e, dv, prows, b->encoder, b->horizon, b->context_patches, b->covariates, err);
   if (!p) return JC_ERR_OOM;
   cudaError_t ce = upload_shard(b, r0, r1, *p, 2 * e.P, s, host);
   if (ce != cudaSuccess) {

@@ -92,6 +92,21 @@ def test_many_rows_on_cta_pair_tiles(jc, tiny, precision):
     assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
 
 
+def test_bucketed_plans_match_exact_plans(jc, tiny):
+    # plans are built for bucketed row counts (TimestralForward.bucket: 33-64 rows in steps of 8): blocks of 49
+    # and 51 rows both run on the same 56-row plan, whose padding rows are dummy series; every real row's
+    # outputs equal an exact-shape plan's bit for bit
+    c, w, _ = tiny
+    with ts.TimestralEngine(c, w, precision="bf16") as bucketed, ts.TimestralEngine(c, w, precision="bf16") as exact:
+        exact.set_option("buckets", 0)
+        for series, groups, seed, rows in ((30, 13, 31, 49), (32, 13, 32, 51)):
+            b = mixed_block(c, series=series, covariate_groups=groups, seed=seed)
+            assert ts.BlockLayout.of(c, b).rows == rows
+            got = ts.B200TimestralForward(bucketed).predict_block(b)
+            ref = ts.B200TimestralForward(exact).predict_block(b)
+            np.testing.assert_array_equal(got, ref)
+
+
 def test_sharding_across_two_slots_matches_one(jc, tiny):
     # two engine slots on the same GPU exercise the shard/gather path of multi-GPU runs
     c, w, _ = tiny
