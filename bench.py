@@ -188,6 +188,20 @@ def engine_profile(L, handle):
     return {names[i].decode(): {"ms": ms[i], "launches": launches[i], "flops": flops[i]} for i in range(n.value)}
 
 
+def pinned(a: np.ndarray) -> np.ndarray:
+    """A copy of ``a`` in pinned (page-locked) host memory, C-contiguous."""
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()
+
+
+def pinned_empty(shape: tuple) -> np.ndarray:
+    """An uninitialised float32 array in pinned host memory."""
+    import torch
+
+    return torch.empty(shape, dtype=torch.float32, pin_memory=True).numpy()
+
+
 def workload_bench(args, world):
     """Configs 2 and 4 on one GPU, with config 5's timing rules: a step is one forward of the config's batch."""
     import ctypes
@@ -225,9 +239,15 @@ def workload_bench(args, world):
                        d["gs"].data_ptr(), d["ge"].data_ptr())
         device_fwd = lambda: L.jc_forward_chronos2_device(engine.handle, 0, ctypes.byref(blk), out.data_ptr(),
                                                           stream.cuda_stream)
-        host_fwd = lambda: engine.forward_raw(lay, prep, gs, ge)
-        h2d = prep.tokens.nbytes + np.asarray(lay.live, np.int32).nbytes + gs.nbytes + ge.nbytes
-        d2h = out.numel() * 4
+        # e2e from pinned host buffers: the prepared tokens, live flags and group ranges in, raw out
+        ptok, plive = pinned(np.asarray(prep.tokens, np.float32)), pinned(np.asarray(lay.live, np.int32))
+        pgs, pge = pinned(gs), pinned(ge)
+        prep_p = dataclasses.replace(prep, tokens=ptok)
+        lay_p = dataclasses.replace(lay, live=plive)
+        raw_p = pinned_empty(tuple(out.shape))
+        host_fwd = lambda: engine.forward_raw(lay_p, prep_p, pgs, pge, out=raw_p)
+        h2d = ptok.nbytes + plive.nbytes + pgs.nbytes + pge.nbytes
+        d2h = raw_p.nbytes
         desc = ("config2: Chronos-2-style T5 encoder (d 768, 12 layers, 12 heads, d_ff 3072 ReLU, patch 16, 128 "
                 "context + [REG] + 4 future tokens, 21 quantiles), random-init weights")
         data = "synthetic random walks x_t = x_{t-1} + N(0,1), seed 0"
@@ -250,9 +270,12 @@ def workload_bench(args, world):
                        len(st.kept), d["kept"].data_ptr(), d["gs"].data_ptr(), d["ge"].data_ptr(), d["kt"].data_ptr())
         device_fwd = lambda: L.jc_forward_tirex2_device(engine.handle, 0, ctypes.byref(blk), out.data_ptr(),
                                                         stream.cuda_stream)
-        host_fwd = lambda: engine.forward_inputs(di)
-        h2d = di.x.nbytes + di.present.nbytes
-        d2h = out.numel() * 4
+        # e2e from pinned host buffers: values and presence flags in, quantiles out
+        di_p = dataclasses.replace(di, x=pinned(di.x), present=pinned(di.present))
+        out_p = pinned_empty(tuple(out.shape))
+        host_fwd = lambda: engine.forward_inputs(di_p, out=out_p)
+        h2d = di_p.x.nbytes + di_p.present.nbytes
+        d2h = out_p.nbytes
         desc = ("config4: TiRex-style xLSTM stack (d 512, 12 blocks, sLSTM at 3, 7, 11, 4 heads, patch 32, 64 "
                 "patches, 9 quantiles, input/output FF 2048), random-init weights")
         data = "synthetic AR(2) phi1 0.6 phi2 0.3 sigma 1, 200-step burn-in, seed 0"
@@ -395,11 +418,10 @@ def main():
     # end to end through the host C ABI: inputs from pinned host buffers, raw outputs back into pinned host
     # buffers, copies timed
     fields = ("tokens", "positions", "key_valid", "known", "role", "group_start", "group_end")
-    pinned = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()  # noqa: E731
     host_chunks = []
     for hin, _, raw, _, n in chunks:
         hp = dataclasses.replace(hin, **{k: pinned(getattr(hin, k)) for k in fields})
-        rp = torch.empty(tuple(raw.shape), dtype=torch.float32, pin_memory=True).numpy()
+        rp = pinned_empty(tuple(raw.shape))
         host_chunks.append((hp, rp, n))
     for hp, rp, _ in host_chunks[:1]:
         engine.forward(hp, out=rp)

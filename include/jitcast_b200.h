@@ -362,9 +362,10 @@ jc_status jc_engine_sync(jc_engine* engine);
  * timestral.tornado.plans in TimestralForward.java:146-160):
  *   "cuda_graph"  1 (default) replay each shape as a captured CUDA graph, 0 run eagerly
  *   "max_plans"   shape plans kept per GPU (default 8; least recently used evicted)
- *   "buckets"     1 (default) Timestral shards run on plans built for a bucketed row count (the count itself
- *                 up to 8, then the next multiple of a quarter of its power of two: at most 25 % padding,
- *                 TimestralForward.bucket, TimestralForward.java:88-99); 0 one plan per exact row count
+ *   "buckets"     1 (default) shards run on plans built for a bucketed row count (the
+ *                 count itself up to 8, then the next multiple of a quarter of its power of two: at most 25 %
+ *                 padding, TimestralForward.bucket, TimestralForward.java:88-99); 0 one plan per exact row
+ *                 count
  *   "profile"     1: run eagerly and time every kernel class with CUDA events (jc_engine_profile)
  */
 jc_status jc_engine_set_option(jc_engine* engine, const char* key, long long value);

@@ -364,13 +364,21 @@ class Chronos2Engine:
             raise RuntimeError("engine is closed")
         return self._h
 
-    def forward_raw(self, lay: ModelLayout, prep: ModelPrep, group_start, group_end) -> np.ndarray:
+    def forward_raw(self, lay: ModelLayout, prep: ModelPrep, group_start, group_end,
+                    out: np.ndarray | None = None) -> np.ndarray:
+        """raw [rows · h, Q · P] for a laid-out input, written into ``out`` when given (a C-contiguous float32 array
+        of that shape, e.g. in pinned memory). Inputs already C-contiguous in the right dtype are used in place."""
         c = self.config
         tok = np.ascontiguousarray(prep.tokens, np.float32)
         live = np.ascontiguousarray(lay.live, np.int32)
         gs = np.ascontiguousarray(group_start, np.int32)
         ge = np.ascontiguousarray(group_end, np.int32)
-        raw = np.empty((lay.rows * lay.output_patches, c.num_quantiles * c.patch_size), np.float32)
+        shape = (lay.rows * lay.output_patches, c.num_quantiles * c.patch_size)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
+        raw = out
         blk = Block(lay.rows, lay.context_patches, lay.output_patches, tok.ctypes.data, live.ctypes.data,
                     gs.ctypes.data, ge.ctypes.data)
         check(_lib.lib().jc_forward_chronos2(self.handle, ctypes.byref(blk), raw.ctypes.data))

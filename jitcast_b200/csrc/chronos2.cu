@@ -215,8 +215,16 @@ std::unique_ptr<C2Plan> make_plan(const Chronos2Engine& e, int rows, int nc, int
     }
   std::vector<int> pos(T);
   for (long long i = 0; i < T; ++i) pos[i] = static_cast<int>(i % n);
+  // every row starts as a valid, independent dummy series (zero tokens, every token live, its own group), so
+  // rows past a call's own (bucket padding) compute harmlessly and never reach a real row
+  std::vector<int> live(T, 1), gs(rows), ge(rows);
+  for (int i = 0; i < rows; ++i) gs[i] = i, ge[i] = i + 1;
   if (cudaMemcpy(p->table, table.data(), sizeof(float) * table.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(p->pos, pos.data(), sizeof(int) * T, cudaMemcpyHostToDevice) != cudaSuccess)
+      cudaMemcpy(p->pos, pos.data(), sizeof(int) * T, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(p->tok_f32, 0, sizeof(float) * EN * 3 * e.P) != cudaSuccess ||
+      cudaMemcpy(p->live, live.data(), sizeof(int) * T, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(p->gs, gs.data(), sizeof(int) * rows, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(p->ge, ge.data(), sizeof(int) * rows, cudaMemcpyHostToDevice) != cudaSuccess)
     return nullptr;
   p->h_gs.resize(rows);
   p->h_ge.resize(rows);
@@ -418,7 +426,8 @@ jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b,
     return JC_ERR_CUDA;
   }
   const int rows = r1 - r0, nc = b->context_patches, h = b->output_patches, n = nc + e.reg + h, ne = nc + h;
-  C2Plan* p = get_plan(e, dv, rows, nc, h, err);
+  const int prows = e.buckets ? bucket_rows(rows) : rows;  // the plan's rows ≥ this shard's
+  C2Plan* p = get_plan(e, dv, prows, nc, h, err);
   if (!p) return JC_ERR_OOM;
   const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
   cudaError_t ce = cudaMemcpyAsync(p->tok_f32, b->tokens + static_cast<long long>(r0) * ne * 3 * e.P,

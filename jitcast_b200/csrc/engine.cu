@@ -25,6 +25,14 @@ void DeviceMem::release() {
   total_ = 0;
 }
 
+int bucket_rows(int x) {
+  if (x <= 8) return x;
+  int hb = 1;
+  while (hb <= (x - 1) / 2) hb *= 2;  // the highest power of two ≤ x − 1
+  const int step = hb / 4;
+  return (x + step - 1) / step * step;
+}
+
 bool alloc_op(DeviceMem& mem, int op, long long rows, long long cols, OpBuf* out) {
   out->ld = round_up(cols, 64);
   out->rows = rows;

@@ -62,6 +62,11 @@ inline bool op_is_16bit(int op) { return op == kOpBF16 || op == kOpF16; }
 inline bool valid_precision_code(int p) { return p == JC_FP32 || p == JC_TF32 || p == JC_BF16 || p == JC_FP16; }
 
 // Allocates an operand buffer of rows × round_up(cols, 64) elements.
+// Rows a plan is built for: `x` itself up to 8, then the next multiple of a quarter of its power of two, so
+// padding adds at most 25 % and the number of shapes grows with the logarithm of the size (the reference's
+// bucket, TimestralForward.java:88-99).
+int bucket_rows(int x);
+
 bool alloc_op(DeviceMem& mem, int op, long long rows, long long cols, OpBuf* out);
 
 // Host weights by name with strict binding: every tensor must be taken exactly once, with the
@@ -157,7 +162,7 @@ struct jc_engine {
   bool use_graph = true;
   int max_plans = 8;
   bool profile = false;
-  bool buckets = true;  // plans (and graphs) for bucketed row counts (Timestral)
+  bool buckets = true;  // plans (and graphs) for bucketed row counts
   virtual int slots() const = 0;
   virtual jc::DeviceSlot* slot(int i) = 0;
   virtual jc::Profiler* profiler(int i) = 0;

@@ -283,17 +283,6 @@ std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, i
   return p;
 }
 
-// Rows a plan is built for: `x` itself up to 8, then the next multiple of a quarter of its power of two, so
-// padding adds at most 25 % and the number of shapes grows with the logarithm of the size (the reference's
-// bucket, TimestralForward.java:88-99).
-int bucket_rows(int x) {
-  if (x <= 8) return x;
-  int hb = 1;
-  while (hb <= (x - 1) / 2) hb *= 2;  // the highest power of two ≤ x − 1
-  const int step = hb / 4;
-  return (x + step - 1) / step * step;
-}
-
 TsPlan* get_plan(TimestralEngine& e, TsDevice& dv, int rows, int enc, int h, int ll, int cov, std::string* err) {
   for (auto it = dv.plans.begin(); it != dv.plans.end(); ++it) {
     TsPlan* p = it->get();

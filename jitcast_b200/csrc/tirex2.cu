@@ -1396,6 +1396,11 @@ std::unique_ptr<TxPlan> make_plan(const Tirex2Engine& e, int rows, int nk, int n
   if (ok && nv > 0)
     ok = (p->xk = f32(TV * d)) && (p->vqkv = f32(TV * 3 * d)) && alloc_op(m, op, TV, d, &p->vatt) &&
          alloc_op(m, op, TV, 4 * d, &p->vhid);
+  // every row starts as an empty series (nothing observed), in no known or kept list, so rows past a call's own
+  // (bucket padding) compute harmlessly and never reach a real row
+  if (ok)
+    ok = cudaMemset(p->x, 0, sizeof(float) * rows * L) == cudaSuccess &&
+         cudaMemset(p->present, 0, sizeof(float) * rows * L) == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
     return nullptr;
@@ -1722,7 +1727,8 @@ jc_status run_shard(Tirex2Engine& e, TxDevice& dv, const jc_tirex2_batch* b, int
     nk = static_cast<int>(lists.known.size());
     nv = static_cast<int>(lists.kept.size());
   }
-  TxPlan* p = get_plan(e, dv, rows, nk, nv, err);
+  const int prows = e.buckets ? bucket_rows(rows) : rows;  // the plan's rows ≥ this shard's
+  TxPlan* p = get_plan(e, dv, prows, nk, nv, err);
   if (!p) return JC_ERR_OOM;
   const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
   const size_t xbytes = sizeof(float) * static_cast<size_t>(rows) * L;

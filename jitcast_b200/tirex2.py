@@ -416,9 +416,15 @@ class TiRex2Engine:
             raise RuntimeError("engine is closed")
         return self._h
 
-    def forward_inputs(self, di: DeviceInputs) -> np.ndarray:
+    def forward_inputs(self, di: DeviceInputs, out: np.ndarray | None = None) -> np.ndarray:
+        """out [rows, Q, len] for prepared host inputs, written into ``out`` when given (a C-contiguous float32
+        array of that shape, e.g. in pinned memory)."""
         c = self.config
-        out = np.empty((di.x.shape[0], c.num_quantiles, c.padded_length), np.float32)
+        shape = (di.x.shape[0], c.num_quantiles, c.padded_length)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
         blk = di.block()
         check(_lib.lib().jc_forward_tirex2(self.handle, ctypes.byref(blk), out.ctypes.data))
         return out

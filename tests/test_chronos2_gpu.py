@@ -87,6 +87,20 @@ def test_without_reg_token(jc):
     assert per_quantile_err(got, exp) < TOL["fp32"]
 
 
+def test_bucketed_plans_match_exact_plans(jc, tiny):
+    # plans are built for bucketed row counts (33-64 rows in steps of 8): inputs of 49 and 51 rows both run on a
+    # 56-row plan whose padding rows are dummy series; every real row's outputs equal an exact-shape plan's
+    c, w, _ = tiny
+    with c2.Chronos2Engine(c, w, precision="bf16") as bucketed, c2.Chronos2Engine(c, w, precision="bf16") as exact:
+        exact.set_option("buckets", 0)
+        for series, seed, rows in ((42, 41, 49), (44, 42, 51)):
+            inp = mixed_input(c, series=series, covariate_groups=5, seed=seed)
+            assert len(inp.group) == rows
+            got = c2.B200Chronos2Forward(bucketed).forward(inp)
+            ref = c2.B200Chronos2Forward(exact).forward(inp)
+            np.testing.assert_array_equal(got, ref)
+
+
 def test_sharded_two_slots(jc, tiny):
     c, w, _ = tiny
     inp = mixed_input(c, series=9, covariate_groups=3)

@@ -120,6 +120,19 @@ def test_sequence_longer_than_one_query_block(jc, precision):
     assert err < bar, f"{precision}: per-quantile rel max err {err:.3e} (bar {bar:.3e})"
 
 
+def test_bucketed_plans_match_exact_plans(jc, tiny):
+    # plans are built for bucketed row counts (33-64 rows in steps of 8): batches of 49 and 51 rows both run on
+    # a 56-row plan whose padding rows are empty series; every real row's outputs equal an exact-shape plan's
+    c, w, _ = tiny
+    with tx.TiRex2Engine(c, w, precision="bf16") as bucketed, tx.TiRex2Engine(c, w, precision="bf16") as exact:
+        exact.set_option("buckets", 0)
+        for rows, seed in ((49, 51), (51, 52)):
+            b = univariate_batch(c, rows=rows, seed=seed)
+            got = tx.B200TiRex2Forward(bucketed).forward(b)
+            ref = tx.B200TiRex2Forward(exact).forward(b)
+            np.testing.assert_array_equal(got, ref)
+
+
 def test_sharded_two_slots_matches_one(jc, tiny):
     # two engine slots on one GPU exercise the shard/gather path of multi-GPU runs, groups kept whole
     c, w, _ = tiny
