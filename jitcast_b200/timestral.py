@@ -639,3 +639,47 @@ class B200TimestralForward:
         return prep.finish(self.config, lay, raw)
 
     predictBlock = predict_block
+
+    def predict_block_sign_flip(self, block: BlockInput) -> np.ndarray:
+        """Sign-flip test-time augmentation in one forward. The reference's pipelines forecast a series and its
+        negation as two passes and average each quantile level with the negated mirror of its complement
+        (SignFlip.average, host/SignFlip.java; TimestralPipeline.java:190-196). Here the block and its
+        negation are concatenated (the copies in groups of their own) and run as one block — half the launches
+        and weight reads — then averaged the same way: out[q] = (a[q] + −b[c(q)]) / 2."""
+        comp = sign_flip_complement(self.config.quantile_knots)
+        both = with_negation(block)
+        out = self.predict_block(both)
+        r = block.rows
+        a, b = out[:r], out[r:]
+        return ((a + -b[..., comp]) / np.float32(2)).astype(np.float32)
+
+
+def sign_flip_complement(levels) -> np.ndarray:
+    """complement[i] = the level closest to 1 − levels[i] (SignFlip.complement); a quantile set that is not
+    symmetric around 0.5 (to 1e-6) is rejected."""
+    q = np.asarray(levels, np.float32)
+    comp = np.empty(len(q), np.int64)
+    for i in range(len(q)):
+        target = np.float32(1) - q[i]
+        best = 0
+        for j in range(1, len(q)):
+            if abs(q[j] - target) < abs(q[best] - target):
+                best = j
+        if abs(q[best] - target) > 1e-6:
+            raise ValueError("sign-flip TTA needs a symmetric quantile set")
+        comp[i] = best
+    return comp
+
+
+def with_negation(block: BlockInput) -> BlockInput:
+    """The block followed by its negation (SignFlip.negate: targets and numeric covariates negated, masks and
+    roles kept); the negated rows form groups of their own after the block's."""
+    g = np.asarray(block.group)
+    offset = int(g.max()) + 1 if len(g) else 0
+    cat = lambda a, b: None if a is None else np.concatenate([a, b])  # noqa: E731
+    kf = block.known_future
+    return BlockInput(np.concatenate([block.inputs, -np.asarray(block.inputs)]),
+                      np.concatenate([block.observed, block.observed]),
+                      np.concatenate([g, g + offset]).astype(g.dtype), block.horizon_patches,
+                      cat(block.role, block.role), cat(kf, None if kf is None else -np.asarray(kf)),
+                      cat(block.known_future_mask, block.known_future_mask))

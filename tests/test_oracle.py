@@ -56,3 +56,12 @@ def test_rel_max_err_definition():
     e = np.array([1.0, -4.0, 2.0])
     assert oracle.rel_max_err(e + [0, 0.4, 0], e) == pytest.approx(0.1)
     assert oracle.rel_max_err(np.array([np.nan, 0, 0]), e) == float("inf")
+
+
+def test_sign_flip_complement():
+    from jitcast_b200 import timestral as ts
+
+    comp = ts.sign_flip_complement(ts.default_knots(9))
+    assert list(comp) == list(range(8, -1, -1))
+    with pytest.raises(ValueError):
+        ts.sign_flip_complement([0.1, 0.5, 0.8])

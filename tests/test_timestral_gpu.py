@@ -107,6 +107,28 @@ def test_bucketed_plans_match_exact_plans(jc, tiny):
             np.testing.assert_array_equal(got, ref)
 
 
+def test_sign_flip_in_one_forward_matches_two(jc, tiny):
+    # sign-flip TTA: the block and its negation as one concatenated forward equal the reference's two passes
+    # (the block, then its negation) averaged with the complement levels, bit for bit
+    c, w, _ = tiny
+    b = mixed_block(c, series=9, covariate_groups=3, seed=13)
+    comp = ts.sign_flip_complement(c.quantile_knots)
+    with ts.TimestralEngine(c, w, precision="bf16") as eng:
+        fwd = ts.B200TimestralForward(eng)
+        one = fwd.predict_block_sign_flip(b)
+        a = fwd.predict_block(b)
+        neg = ts.with_negation(b)
+        r = b.rows
+        nb = ts.BlockInput(neg.inputs[r:], neg.observed[r:], neg.group[r:], b.horizon_patches,
+                           None if neg.role is None else neg.role[r:],
+                           None if neg.known_future is None else neg.known_future[r:],
+                           None if neg.known_future_mask is None else neg.known_future_mask[r:])
+        bneg = fwd.predict_block(nb)
+    two = ((a + -bneg[..., comp]) / np.float32(2)).astype(np.float32)
+    assert one.shape == a.shape
+    np.testing.assert_array_equal(one, two)
+
+
 def test_sharding_across_two_slots_matches_one(jc, tiny):
     # two engine slots on the same GPU exercise the shard/gather path of multi-GPU runs
     c, w, _ = tiny
