@@ -323,7 +323,8 @@ def workload_bench(args, world):
             "gpu_launches": sum(v["launches"] for v in prof.values()) * args.steps,
             "kernel_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
                                    **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {})}
-                               for k, v in prof.items()}}
+                               for k, v in prof.items()},
+            "host_ends_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"]} for k, v in ends_prof.items()}}
     print(json.dumps(line), flush=True)
     engine.close()
     return 0
@@ -362,6 +363,7 @@ def main():
     per_rank = args.series // world
     first = rank * per_rank
     chunks = []
+    win_in = []  # each chunk's window and layout, for the end-to-end forecast
     for c0 in range(first, first + per_rank, args.chunk):
         n = min(args.chunk, first + per_rank - c0)
         x = workloads.sinusoid_noise(n, 4096, seed=c0)  # chunk-seeded: the same series for every N
@@ -369,6 +371,7 @@ def main():
         lay = ts.BlockLayout.of(cfg, b)
         prep = ts.BlockPrep.of(cfg, lay)
         hin = ts.DeviceInputs.of(lay, prep)
+        win_in.append(ts.WindowInputs.of(cfg, lay))
         d = {k: torch.from_numpy(np.ascontiguousarray(getattr(hin, k))).to(dev)
              for k in ("tokens", "positions", "key_valid", "known", "role", "group_start", "group_end")}
         raw = torch.empty(n * 2, cfg.patch_size * cfg.num_quantiles, device=dev)
@@ -415,25 +418,27 @@ def main():
     ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
     value = args.series / (ms / 1000.0)
 
-    # end to end through the host C ABI: inputs from pinned host buffers, raw outputs back into pinned host
-    # buffers, copies timed
-    fields = ("tokens", "positions", "key_valid", "known", "role", "group_start", "group_end")
+    # end to end through the host C ABI (jc_forecast_timestral): each chunk's window, observed flags and layout
+    # from pinned host buffers, BlockPrep's scaler and tokens, the forward and BlockPrep.finish on the GPU, the
+    # finished quantiles back into pinned host buffers, copies timed (the layout itself is built before)
+    fields = ("positions", "key_valid", "known", "role", "group_start", "group_end")
     host_chunks = []
-    for hin, _, raw, _, n in chunks:
-        hp = dataclasses.replace(hin, **{k: pinned(getattr(hin, k)) for k in fields})
-        rp = pinned_empty(tuple(raw.shape))
-        host_chunks.append((hp, rp, n))
-    for hp, rp, _ in host_chunks[:1]:
-        engine.forward(hp, out=rp)
+    for wi, (_, _, _, _, n) in zip(win_in, chunks):
+        lp = dataclasses.replace(wi.layout, **{k: pinned(getattr(wi.layout, k)) for k in fields})
+        hp = dataclasses.replace(wi, layout=lp, window=pinned(wi.window), observed=pinned(wi.observed))
+        qp = pinned_empty((n, 2 * cfg.patch_size, cfg.num_quantiles))
+        host_chunks.append((hp, qp, n))
+    for hp, qp, _ in host_chunks[:1]:
+        engine.forecast(hp, out=qp)
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     h2d = d2h = 0
     for _ in range(args.steps):
-        for hp, rp, n in host_chunks:
-            engine.forward(hp, out=rp)
-            h2d += sum(getattr(hp, k).nbytes for k in fields)
-            d2h += rp.nbytes
+        for hp, qp, n in host_chunks:
+            engine.forecast(hp, out=qp)
+            h2d += hp.window.nbytes + hp.observed.nbytes + sum(getattr(hp.layout, k).nbytes for k in fields)
+            d2h += qp.nbytes
     e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
     barrier()
 
@@ -444,6 +449,9 @@ def main():
                                              stream.cuda_stream))
     torch.cuda.synchronize()
     prof = engine.profile()
+    # the host ends on the GPU (scaler, tokens, finish) of one chunk's forecast, timed the same way
+    engine.forecast(host_chunks[0][0], out=host_chunks[0][1])
+    ends_prof = {k: v for k, v in engine.profile().items() if k.startswith(("prep", "finish"))}
     engine.set_option("profile", 0)
     launches_per_forward = sum(v["launches"] for v in prof.values()) + 3  # + the 3 index-rebasing kernels
     gemms = {k: v for k, v in prof.items() if k.startswith("gemm")}
@@ -485,7 +493,8 @@ def main():
             "gpu_launches": launches_per_forward * len(chunks) * args.steps,
             "kernel_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
                                    **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {})}
-                               for k, v in prof.items()}}
+                               for k, v in prof.items()},
+            "host_ends_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"]} for k, v in ends_prof.items()}}
     print(json.dumps(line), flush=True)
     engine.close()
     if world > 1:

@@ -13,6 +13,8 @@
  *   - timestral/BlockForward.java:20-24 and timestral/tornado/TimestralForward.java:187-642
  *       BlockForward.predictBlock's device forward (TimestralForward)   → jc_engine_create_timestral,
  *                                                                          jc_forward_timestral
+ *   - timestral/BlockPrep.java:40-101 BlockPrep.of / BlockPrep.finish   → jc_forecast_timestral (the
+ *       host ends on the GPU around the same forward)
  *   - chronos2/ModelForward.java and chronos2/tornado/Chronos2Forward.java:148-494
  *       ModelForward.forward's device forward (Chronos2Forward)         → jc_engine_create_chronos2,
  *                                                                          jc_forward_chronos2
@@ -244,6 +246,38 @@ jc_status jc_forward_timestral(jc_engine* engine, const jc_timestral_block* bloc
  */
 jc_status jc_forward_timestral_device(jc_engine* engine, int slot, const jc_timestral_block* block, float* raw_out,
                                       void* stream);
+
+/*
+ * One decode block with BlockPrep's host ends moved onto the GPU (timestral/BlockPrep.java:40-101):
+ * the layout fields of `layout` as for jc_forward_timestral (its `tokens` is not read and may be
+ * NULL), and the raw window they are computed from instead of the tokens. The GPU runs the scaler
+ * (Scaler.causalPatchLocScale, Scaler.instanceNorm on known-covariate rows), assembles the
+ * tokens, runs the forward, then BlockPrep.finish (Quantiles.apply, Scaler.invert,
+ * Scaler.clampNonFinite) with the reference's arithmetic: statistics in double, each float
+ * product and sum rounded on its own.
+ */
+typedef struct jc_timestral_window {
+  jc_timestral_block layout;
+  const float* window;         /* [rows · encoder · P] BlockLayout.window */
+  const uint8_t* observed;     /* [rows · encoder · P] BlockLayout.observed, 0/1 */
+  float minimum_scale;         /* TimestralConfig.minimumScale */
+  int use_asinh;               /* TimestralConfig.useAsinh */
+  int median;                  /* Quantiles.median() */
+  const float* quantile_scale; /* [Q] Quantiles.scale(); a HOST array in both calls below, Q <= 64 */
+} jc_timestral_window;
+
+/*
+ * BlockForward.predictBlock after the layout, on HOST buffers: quantiles_out [rows · horizon · P · Q]
+ * receives BlockPrep.finish's raw-space quantiles ([rows][H·P][Q]). Sharded, graphed and
+ * validated as jc_forward_timestral; the window crosses to the GPU instead of the tokens
+ * (5 bytes per step instead of 8) and nothing is left for the host to finish.
+ */
+jc_status jc_forecast_timestral(jc_engine* engine, const jc_timestral_window* block, float* quantiles_out);
+
+/* The same on device buffers of the engine's GPU number `slot` (every pointer of `block` except
+ * quantile_scale, and quantiles_out), enqueued on `stream` as jc_forward_timestral_device. */
+jc_status jc_forecast_timestral_device(jc_engine* engine, int slot, const jc_timestral_window* block,
+                                       float* quantiles_out, void* stream);
 
 /* The Chronos2Config fields the forward pass uses (chronos2/Chronos2Config.java:45-60). */
 typedef struct jc_chronos2_desc {

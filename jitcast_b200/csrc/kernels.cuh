@@ -28,4 +28,31 @@ void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int row
 // out[i] = in[i] + add for i < n (integer index rebasing on the device).
 void launch_add_i32(const int* in, int* out, long long n, int add, cudaStream_t s);
 
+// ---- the Timestral host ends on the device (timestral_ends.cu) ----
+
+constexpr int kMaxQuantiles = 64;
+
+// What the scaler, the token assembly and the quantile finish need of one shard: rows of `enc`
+// patches of P steps (window W = enc·P), the context's `ll` patches, Q levels with the median at
+// `median` and Quantiles.scale() in `qscale`.
+struct TsEnds {
+  int rows = 0, enc = 0, P = 0, ll = 0, Q = 0, median = 0, use_asinh = 0;
+  float min_scale = 0.0f;
+  float qscale[kMaxQuantiles] = {};
+};
+
+// Scaler.causalPatchLocScale (Scaler.instanceNorm on known rows) of every row of win/obs
+// [rows · W]: frame [rows · enc] (loc, scale) per patch, row_asinh [rows] whether the row's
+// affine transform takes the asinh.
+void launch_ts_scaler(const float* win, const uint8_t* obs, const int* known, const TsEnds& ep, float2* frame,
+                      uint8_t* row_asinh, cudaStream_t s);
+
+// BlockPrep.tokens [rows · enc · 2P]: each patch's scaled values, then its missing flags.
+void launch_ts_tokens(const float* win, const uint8_t* obs, const float2* frame, const uint8_t* row_asinh,
+                      const TsEnds& ep, float* tok, cudaStream_t s);
+
+// BlockPrep.finish in place on raw [rows · steps · Q] (steps = horizon · P): monotone levels,
+// denormalised with each row's last context frame, infinities clamped.
+void launch_ts_finish(float* raw, const float2* frame, const TsEnds& ep, int steps, cudaStream_t s);
+
 }  // namespace jc

@@ -60,6 +60,13 @@ struct TsPlan {
   float* table = nullptr;
   GraphRunner graph;
   std::vector<int> h_pos, h_gs, h_ge;  // host staging of the transformed integer inputs
+  // the host ends on the device (jc_forecast_timestral), allocated on first use: per-patch frames and
+  // asinh flags, and for host calls the window and its flags staged in HBM
+  DeviceMem ends_mem, stage_mem;
+  float2* frame = nullptr;
+  uint8_t* row_asinh = nullptr;
+  float* win = nullptr;
+  uint8_t* obs = nullptr;
 };
 
 struct TsDevice : DeviceSlot {
@@ -462,14 +469,15 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
 }
 
 // Validates one block's host or device-independent fields.
-jc_status check_block(const TimestralEngine& e, const jc_timestral_block* b, bool host) {
+jc_status check_block(const TimestralEngine& e, const jc_timestral_block* b, bool host, bool tokens = true) {
   if (!b) return fail(JC_ERR_INVALID_ARG, "null block");
   if (b->rows < 1) return fail(JC_ERR_INVALID_ARG, "rows must be >= 1");
   if (b->encoder < 1) return fail(JC_ERR_INVALID_ARG, "encoder tokens must be >= 1");
   if (b->horizon < 1) return fail(JC_ERR_INVALID_ARG, "horizon patches must be >= 1, got " + std::to_string(b->horizon));
   if (b->context_patches < 1 || b->context_patches > b->encoder)
     return fail(JC_ERR_INVALID_ARG, "context patches must be in [1, encoder]");
-  if (!b->tokens || !b->positions || !b->key_valid || !b->known || !b->role || !b->group_start || !b->group_end)
+  if ((tokens && !b->tokens) || !b->positions || !b->key_valid || !b->known || !b->role || !b->group_start ||
+      !b->group_end)
     return fail(JC_ERR_INVALID_ARG, "null block field");
   if (host) {
     for (int i = 0; i < b->rows; ++i) {
@@ -486,12 +494,14 @@ jc_status check_block(const TimestralEngine& e, const jc_timestral_block* b, boo
 // rows (position + encoder) and series ranges become shard-relative. `kind` is HostToDevice for
 // host blocks and DeviceToDevice for device blocks (then the integer transforms run on the GPU).
 cudaError_t upload_shard(const jc_timestral_block* b, int r0, int r1, TsPlan& p, int two_p, cudaStream_t s,
-                         bool host) {
+                         bool host, bool tokens) {
   const int rows = r1 - r0, E = b->encoder, n = E + b->horizon;
   const long long T = static_cast<long long>(rows) * n;
   const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
-  cudaError_t e = cudaMemcpyAsync(p.tok_f32, b->tokens + static_cast<long long>(r0) * E * two_p,
-                                  sizeof(float) * rows * E * two_p, kind, s);
+  cudaError_t e = cudaSuccess;
+  if (tokens)
+    e = cudaMemcpyAsync(p.tok_f32, b->tokens + static_cast<long long>(r0) * E * two_p,
+                        sizeof(float) * rows * E * two_p, kind, s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(p.key_valid, b->key_valid + static_cast<long long>(r0) * E, sizeof(int) * rows * E, kind, s);
   if (e == cudaSuccess) e = cudaMemcpyAsync(p.known, b->known + r0, sizeof(int) * rows, kind, s);
@@ -514,9 +524,52 @@ cudaError_t upload_shard(const jc_timestral_block* b, int r0, int r1, TsPlan& p,
   return cudaGetLastError();
 }
 
-// Runs rows [r0, r1) of `b` on one GPU; raw_out points at the block's first row's outputs.
+// The host ends' buffers of a plan, sized for its rows: frames and asinh flags always, the
+// staged window and flags only for host calls. False when device memory runs out.
+bool ensure_ends(TsPlan& p, int P, bool host) {
+  if (!p.frame) {
+    if (!(p.frame = static_cast<float2*>(p.ends_mem.alloc(sizeof(float2) * p.rows * p.enc))) ||
+        !(p.row_asinh = static_cast<uint8_t*>(p.ends_mem.alloc(p.rows)))) {
+      cudaGetLastError();
+      p.ends_mem.release();
+      p.frame = nullptr;
+      p.row_asinh = nullptr;
+      return false;
+    }
+  }
+  if (host && !p.win) {
+    const long long n = static_cast<long long>(p.rows) * p.enc * P;
+    if (!(p.win = static_cast<float*>(p.stage_mem.alloc(sizeof(float) * n))) ||
+        !(p.obs = static_cast<uint8_t*>(p.stage_mem.alloc(n)))) {
+      cudaGetLastError();
+      p.stage_mem.release();
+      p.win = nullptr;
+      p.obs = nullptr;
+      return false;
+    }
+  }
+  return true;
+}
+
+TsEnds ends_params(const TimestralEngine& e, const jc_timestral_window* w, int rows) {
+  TsEnds ep;
+  ep.rows = rows;
+  ep.enc = w->layout.encoder;
+  ep.P = e.P;
+  ep.ll = w->layout.context_patches;
+  ep.Q = e.Q;
+  ep.median = w->median;
+  ep.use_asinh = w->use_asinh ? 1 : 0;
+  ep.min_scale = w->minimum_scale;
+  for (int i = 0; i < e.Q; ++i) ep.qscale[i] = w->quantile_scale[i];
+  return ep;
+}
+
+// Runs rows [r0, r1) of `b` on one GPU; raw_out points at the block's first row's outputs. With
+// `ends` (whose layout is `b`) the window replaces the tokens and raw_out receives the finished
+// quantiles.
 jc_status run_shard(TimestralEngine& e, TsDevice& dv, const jc_timestral_block* b, int r0, int r1, float* raw_out,
-                    bool host, cudaStream_t stream, std::string* err) {
+                    bool host, cudaStream_t stream, std::string* err, const jc_timestral_window* ends = nullptr) {
   if (cudaSetDevice(dv.device) != cudaSuccess) {
     *err = "cannot select device " + std::to_string(dv.device);
     return JC_ERR_CUDA;
@@ -533,18 +586,62 @@ jc_status run_shard(TimestralEngine& e, TsDevice& dv, const jc_timestral_block* 
   const int prows = e.buckets ? bucket_rows(r1 - r0) : r1 - r0;  // the plan's rows ≥ this shard's
   TsPlan* p = get_plan(e, dv, prows, b->encoder, b->horizon, b->context_patches, b->covariates, err);
   if (!p) return JC_ERR_OOM;
-  cudaError_t ce = upload_shard(b, r0, r1, *p, 2 * e.P, s, host);
+  cudaError_t ce = upload_shard(b, r0, r1, *p, 2 * e.P, s, host, ends == nullptr);
   if (ce != cudaSuccess) {
     *err = std::string("upload: ") + cudaGetErrorString(ce);
     return JC_ERR_CUDA;
   }
   dv.prof.on = e.profile;
+  TsEnds ep;
+  if (ends) {
+    // BlockPrep.of on the GPU: the scaler's frames, then the tokens, into the plan's token rows
+    if (!ensure_ends(*p, e.P, host)) {
+      *err = "out of device memory for the host ends of a plan of " + std::to_string(p->rows) + " rows";
+      return JC_ERR_OOM;
+    }
+    const long long W = static_cast<long long>(b->encoder) * e.P, n = static_cast<long long>(r1 - r0) * W;
+    const float* win = ends->window + r0 * W;
+    const uint8_t* obs = ends->observed + r0 * W;
+    if (host) {
+      ce = cudaMemcpyAsync(p->win, win, sizeof(float) * n, cudaMemcpyHostToDevice, s);
+      if (ce == cudaSuccess) ce = cudaMemcpyAsync(p->obs, obs, n, cudaMemcpyHostToDevice, s);
+      if (ce != cudaSuccess) {
+        *err = std::string("upload: ") + cudaGetErrorString(ce);
+        return JC_ERR_CUDA;
+      }
+      win = p->win;
+      obs = p->obs;
+    }
+    ep = ends_params(e, ends, r1 - r0);
+    dv.prof.begin(s, "prep.scaler", 0);
+    launch_ts_scaler(win, obs, p->known, ep, p->frame, p->row_asinh, s);
+    dv.prof.end(s);
+    dv.prof.begin(s, "prep.tokens", 0);
+    launch_ts_tokens(win, obs, p->frame, p->row_asinh, ep, p->tok_f32, s);
+    dv.prof.end(s);
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+      *err = std::string("prep: ") + cudaGetErrorString(ce);
+      return JC_ERR_CUDA;
+    }
+  }
   TimestralEngine& ec = e;
   TsDevice& dvc = dv;
   ce = p->graph.run(s, [&](cudaStream_t st) { return enqueue_forward(ec, dvc, *p, st); }, e.use_graph && !e.profile);
   if (ce != cudaSuccess) {
     *err = std::string("forward: ") + cudaGetErrorString(ce);
     return JC_ERR_CUDA;
+  }
+  if (ends) {
+    // BlockPrep.finish on the GPU, in place on the shard's raw outputs
+    dv.prof.begin(s, "finish", 0);
+    launch_ts_finish(p->raw, p->frame, ep, b->horizon * e.P, s);
+    dv.prof.end(s);
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+      *err = std::string("finish: ") + cudaGetErrorString(ce);
+      return JC_ERR_CUDA;
+    }
   }
   const size_t nraw = static_cast<size_t>(r1 - r0) * b->horizon * e.P * e.Q;
   ce = cudaMemcpyAsync(raw_out + static_cast<size_t>(r0) * b->horizon * e.P * e.Q, p->raw, sizeof(float) * nraw,
@@ -574,6 +671,16 @@ jc_status run_shard(TimestralEngine& e, TsDevice& dv, const jc_timestral_block* 
     return JC_ERR_TIMEOUT;
   }
   return JC_OK;
+}
+
+jc_status check_window(const TimestralEngine& e, const jc_timestral_window* w, bool host) {
+  if (!w) return fail(JC_ERR_INVALID_ARG, "null block");
+  if (!w->window || !w->observed || !w->quantile_scale) return fail(JC_ERR_INVALID_ARG, "null window field");
+  if (e.Q > kMaxQuantiles)
+    return fail(JC_ERR_UNSUPPORTED_SHAPE, "the host ends on the device support at most " +
+                                              std::to_string(kMaxQuantiles) + " quantiles");
+  if (w->median < 0 || w->median >= e.Q) return fail(JC_ERR_INVALID_ARG, "median index out of range");
+  return check_block(e, &w->layout, host, false);
 }
 
 }  // namespace
@@ -693,6 +800,52 @@ jc_status jc_forward_timestral_device(jc_engine* engine, int slot, const jc_time
   std::lock_guard<std::mutex> lk(e->mu);
   std::string err;
   st = run_shard(*e, *e->devs[slot], block, 0, block->rows, raw_out, false, static_cast<cudaStream_t>(stream), &err);
+  return st == JC_OK ? JC_OK : fail(st, err);
+}
+
+jc_status jc_forecast_timestral(jc_engine* engine, const jc_timestral_window* block, float* quantiles_out) {
+  clear_error();
+  if (!engine || engine->family != 1) return fail(JC_ERR_INVALID_ARG, "not a Timestral engine");
+  auto* e = static_cast<TimestralEngine*>(engine);
+  if (!quantiles_out) return fail(JC_ERR_INVALID_ARG, "null output");
+  jc_status st = check_window(*e, block, true);
+  if (st != JC_OK) return st;
+  const jc_timestral_block* lay = &block->layout;
+  std::lock_guard<std::mutex> lk(e->mu);
+  const int parts = std::min<int>(static_cast<int>(e->devs.size()), lay->rows);
+  std::vector<int> cuts = shard_rows(lay->rows, lay->group_start, lay->group_end, parts);
+  std::vector<jc_status> status(parts, JC_OK);
+  std::vector<std::string> errs(parts);
+  auto work = [&](int i) {
+    if (cuts[i + 1] > cuts[i])
+      status[i] = run_shard(*e, *e->devs[i], lay, cuts[i], cuts[i + 1], quantiles_out, true, nullptr, &errs[i], block);
+  };
+  if (parts == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < parts; ++i) th.emplace_back(work, i);
+    for (auto& t : th) t.join();
+  }
+  for (int i = 0; i < parts; ++i)
+    if (status[i] != JC_OK)
+      return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+  return JC_OK;
+}
+
+jc_status jc_forecast_timestral_device(jc_engine* engine, int slot, const jc_timestral_window* block,
+                                       float* quantiles_out, void* stream) {
+  clear_error();
+  if (!engine || engine->family != 1) return fail(JC_ERR_INVALID_ARG, "not a Timestral engine");
+  auto* e = static_cast<TimestralEngine*>(engine);
+  if (slot < 0 || slot >= static_cast<int>(e->devs.size())) return fail(JC_ERR_INVALID_ARG, "slot out of range");
+  if (!quantiles_out) return fail(JC_ERR_INVALID_ARG, "null output");
+  jc_status st = check_window(*e, block, false);
+  if (st != JC_OK) return st;
+  std::lock_guard<std::mutex> lk(e->mu);
+  std::string err;
+  st = run_shard(*e, *e->devs[slot], &block->layout, 0, block->layout.rows, quantiles_out, false,
+                 static_cast<cudaStream_t>(stream), &err, block);
   return st == JC_OK ? JC_OK : fail(st, err);
 }
 

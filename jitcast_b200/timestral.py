@@ -505,6 +505,8 @@ _lib.declare("jc_engine_create_timestral", c_int, [ctypes.POINTER(_Desc), ctypes
                                                      ctypes.POINTER(c_int), c_int, c_int, ctypes.POINTER(c_vp)])
 _lib.declare("jc_forward_timestral", c_int, [c_vp, ctypes.POINTER(Block), c_vp])
 _lib.declare("jc_forward_timestral_device", c_int, [c_vp, c_int, ctypes.POINTER(Block), c_vp, c_vp])
+_lib.declare("jc_forecast_timestral", c_int, [c_vp, c_vp, c_vp])
+_lib.declare("jc_forecast_timestral_device", c_int, [c_vp, c_int, c_vp, c_vp, c_vp])
 _lib.declare("jc_engine_sync", c_int, [c_vp])
 _lib.declare("jc_engine_set_option", c_int, [c_vp, ctypes.c_char_p, ctypes.c_longlong])
 _lib.declare("jc_engine_profile", c_int, [c_vp, c_int, ctypes.POINTER(ctypes.c_char_p),
@@ -522,7 +524,7 @@ class DeviceInputs:
     horizon: int
     context_patches: int
     covariates: int
-    tokens: np.ndarray
+    tokens: np.ndarray | None  # None for WindowInputs, whose tokens the GPU assembles
     positions: np.ndarray
     key_valid: np.ndarray
     known: np.ndarray
@@ -541,9 +543,44 @@ class DeviceInputs:
 
     def struct(self) -> Block:
         return Block(self.rows, self.encoder, self.horizon, self.context_patches, self.covariates,
-                     self.tokens.ctypes.data, self.positions.ctypes.data, self.key_valid.ctypes.data,
+                     None if self.tokens is None else self.tokens.ctypes.data, self.positions.ctypes.data, self.key_valid.ctypes.data,
                      self.known.ctypes.data, self.role.ctypes.data, self.group_start.ctypes.data,
                      self.group_end.ctypes.data)
+
+
+class Window(ctypes.Structure):
+    """jc_timestral_window."""
+
+    _fields_ = [("layout", Block), ("window", c_vp), ("observed", c_vp), ("minimum_scale", ctypes.c_float),
+                ("use_asinh", c_int), ("median", c_int), ("quantile_scale", c_vp)]
+
+
+@dataclass
+class WindowInputs:
+    """A block's inputs for the forward with BlockPrep's host ends on the GPU (what jc_timestral_window points
+    at): the layout without tokens, and the raw window with its observed flags."""
+
+    layout: DeviceInputs
+    window: np.ndarray    # [rows, encoder · P] float32, BlockLayout.window
+    observed: np.ndarray  # [rows, encoder · P] uint8, BlockLayout.observed
+    minimum_scale: float
+    use_asinh: int
+    median: int
+    quantile_scale: np.ndarray  # [Q] float32, Quantiles.scale()
+
+    @staticmethod
+    def of(c: TimestralConfig, lay: BlockLayout) -> "WindowInputs":
+        gs, ge = lay.group_ranges()
+        i32 = lambda a: np.ascontiguousarray(a, np.int32)  # noqa: E731
+        layout = DeviceInputs(lay.rows, lay.encoder, lay.horizon, lay.context_patches, int(lay.covariates), None,
+                              i32(lay.positions()), i32(lay.key_valid), i32(lay.known), i32(lay.role), gs, ge)
+        return WindowInputs(layout, np.ascontiguousarray(lay.window, np.float32),
+                            np.ascontiguousarray(lay.observed, np.uint8), float(np.float32(c.minimum_scale)),
+                            int(c.use_asinh), c.median_index, np.ascontiguousarray(quantile_scale(c), np.float32))
+
+    def struct(self) -> Window:
+        return Window(self.layout.struct(), self.window.ctypes.data, self.observed.ctypes.data, self.minimum_scale,
+                      self.use_asinh, self.median, self.quantile_scale.ctypes.data)
 
 
 class TimestralEngine:
@@ -590,6 +627,19 @@ class TimestralEngine:
         check(_lib.lib().jc_forward_timestral(self.handle, ctypes.byref(blk), out.ctypes.data))
         return out
 
+    def forecast(self, inp: WindowInputs, out: np.ndarray | None = None) -> np.ndarray:
+        """BlockPrep.finish's quantiles [rows, h · P, Q] with the scaler, the tokens and the finish on the GPU
+        (``jc_forecast_timestral``), written into ``out`` when given (C-contiguous float32 of that shape)."""
+        c = self.config
+        shape = (inp.layout.rows, inp.layout.horizon * c.patch_size, c.num_quantiles)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
+        blk = inp.struct()
+        check(_lib.lib().jc_forecast_timestral(self.handle, ctypes.byref(blk), out.ctypes.data))
+        return out
+
     def set_option(self, key: str, value: int) -> None:
         check(_lib.lib().jc_engine_set_option(self.handle, key.encode(), int(value)))
 
@@ -625,15 +675,22 @@ class TimestralEngine:
 
 
 class B200TimestralForward:
-    """``BlockForward`` on the B200 engine: layout and prep on the host, the transformer on the GPUs,
-    finish on the host (TimestralForward.predictExact, TimestralForward.java:234-252)."""
+    """``BlockForward`` on the B200 engine: the layout on the host, the transformer on the GPUs, and
+    BlockPrep's scaler and finish on the host as the reference runs them (TimestralForward.predictExact,
+    TimestralForward.java:234-252), or with ``ends="device"`` on the GPU around the forward
+    (``jc_forecast_timestral``: the window crosses instead of the tokens, the quantiles come back finished)."""
 
-    def __init__(self, engine: TimestralEngine):
+    def __init__(self, engine: TimestralEngine, ends: str = "host"):
+        if ends not in ("host", "device"):
+            raise ValueError(f"ends must be 'host' or 'device', got {ends!r}")
         self.engine = engine
         self.config = engine.config
+        self.ends = ends
 
     def predict_block(self, block: BlockInput) -> np.ndarray:
         lay = BlockLayout.of(self.config, block)
+        if self.ends == "device":
+            return self.engine.forecast(WindowInputs.of(self.config, lay))
         prep = BlockPrep.of(self.config, lay)
         raw = self.engine.forward(DeviceInputs.of(lay, prep))
         return prep.finish(self.config, lay, raw)

@@ -10,6 +10,7 @@ import pytest
 
 import jitcast_b200
 from jitcast_b200 import _lib
+from jitcast_b200 import chronos2, timestral, tirex2  # noqa: F401  (their entry points' ctypes prototypes)
 
 HEADERS = sorted((Path(__file__).resolve().parent.parent / "include").glob("*.h"))
 

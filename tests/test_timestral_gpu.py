@@ -6,10 +6,13 @@ mixed batches of random walks plus a daily sinusoid, NaN gaps, late starts, mult
 the error measure max|a − e| / max|e| taken on EVERY quantile level.
 """
 
+import dataclasses
+
 import numpy as np
 import pytest
 
 from jitcast_b200 import timestral as ts
+from jitcast_b200._lib import JcError
 from jitcast_b200 import workloads
 from oracle import timestral as ots
 
@@ -127,6 +130,117 @@ def test_sign_flip_in_one_forward_matches_two(jc, tiny):
     two = ((a + -bneg[..., comp]) / np.float32(2)).astype(np.float32)
     assert one.shape == a.shape
     np.testing.assert_array_equal(one, two)
+
+
+def indicator_block(c, seed=21):
+    """A covariate block whose first known-future row is a 0/1 indicator: Scaler.instanceNorm gives it loc 0,
+    scale 1 and no asinh (Scaler.java:100-124)."""
+    b = mixed_block(c, series=7, covariate_groups=2, seed=seed)
+    i = int(np.nonzero(np.asarray(b.role) == ts.KNOWN)[0][0])
+    rng = np.random.default_rng(seed)
+    x, kf = b.inputs.copy(), b.known_future.copy()
+    x[i] = np.where(b.observed[i], rng.random(x.shape[1]) < 0.3, False).astype(np.float32)
+    kf[i] = (rng.random(kf.shape[1]) < 0.3).astype(np.float32)
+    return dataclasses.replace(b, inputs=x, known_future=kf)
+
+
+def ends_block(c, case):
+    if case == "indicator":
+        return indicator_block(c)
+    return mixed_block(c, covariate_groups=2 if case == "covariates" else 0)
+
+
+@pytest.mark.parametrize("case", ["plain", "covariates", "indicator"])
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_host_ends_on_device_match_host_ends(jc, tiny, case, precision):
+    # BlockPrep.of and BlockPrep.finish on the GPU (jc_forecast_timestral) against the same engine with both ends
+    # on the host. The statistics, the tokens and the quantile arithmetic are the reference's operation for
+    # operation, so the outputs are equal bit for bit except where a double transcendental (CUDA's log, exp,
+    # log1p or sinh against NumPy's) lands within an ulp of a float rounding boundary; both meet the oracle's bar
+    c, w, model = tiny
+    b = ends_block(c, case)
+    exp, _ = model.predict_block(b)
+    with ts.TimestralEngine(c, w, precision=precision) as eng:
+        host = ts.B200TimestralForward(eng).predict_block(b)
+        dev_fwd = ts.B200TimestralForward(eng, ends="device")
+        dev = dev_fwd.predict_block(b)
+        dev2 = dev_fwd.predict_block(b)  # graph replay, staged buffers reused
+    assert dev.shape == host.shape == exp.shape
+    np.testing.assert_array_equal(dev, dev2)
+    same = float(np.mean(dev == host))
+    assert same >= 0.999, f"only {same:.4%} of the quantiles equal the host ends' bit for bit"
+    err = per_quantile_err(dev, exp)
+    assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+
+
+def test_host_ends_on_device_clamp_infinities(jc, tiny):
+    # a head scaled so the raw outputs reach the hundreds: sinh overflows on about half the levels, so
+    # Scaler.clampNonFinite maps infinities to the largest / smallest finite level of their step, or to 0 when a
+    # step has none; the GPU's finish does the same as the host's
+    c, w, _ = tiny
+    w2 = dict(w)
+    for k in ("head.projection.output_layer.weight", "head.projection.residual_layer.weight"):
+        w2[k] = w[k] * np.float32(100)
+    b = mixed_block(c, covariate_groups=0)
+    with ts.TimestralEngine(c, w2, precision="fp32") as eng:
+        lay = ts.BlockLayout.of(c, b)
+        prep = ts.BlockPrep.of(c, lay)
+        raw = eng.forward(ts.DeviceInputs.of(lay, prep))
+        host = prep.finish(c, lay, raw)
+        dev = ts.B200TimestralForward(eng, ends="device").predict_block(b)
+    v = ts.monotone_quantiles(c, raw.reshape(lay.rows, lay.horizon * c.patch_size, c.num_quantiles))
+    over = np.abs(v) > 89.5  # sinh overflows float32 above ~89.4
+    assert over.any(axis=-1).mean() > 0.3 and over.all(axis=-1).any()
+    assert np.isfinite(dev).all()
+    same = float(np.mean(dev == host))
+    assert same >= 0.999, f"only {same:.4%} of the quantiles equal the host finish bit for bit"
+
+
+def test_host_ends_device_entry_point_matches_host(jc, tiny):
+    # jc_forecast_timestral_device reads the window and the layout from HBM and leaves the quantiles there; the
+    # same kernels on the same inputs as the host call, so the same bits
+    torch = pytest.importorskip("torch")
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    c, w, _ = tiny
+    b = mixed_block(c, covariate_groups=2)
+    lay = ts.BlockLayout.of(c, b)
+    with ts.TimestralEngine(c, w, precision="fp16") as eng:
+        wi = ts.WindowInputs.of(c, lay)
+        host = eng.forecast(wi)
+        dev = torch.device("cuda", 0)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+        L = wi.layout
+        keep = {k: t(getattr(L, k)) for k in ("positions", "key_valid", "known", "role", "group_start", "group_end")}
+        keep["window"], keep["observed"] = t(wi.window), t(wi.observed)
+        blk = ts.Block(L.rows, L.encoder, L.horizon, L.context_patches, L.covariates, None,
+                       *(keep[k].data_ptr() for k in ("positions", "key_valid", "known", "role", "group_start",
+                                                      "group_end")))
+        win = ts.Window(blk, keep["window"].data_ptr(), keep["observed"].data_ptr(), wi.minimum_scale, wi.use_asinh,
+                        wi.median, wi.quantile_scale.ctypes.data)
+        out = torch.empty(host.shape, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(_lib.lib().jc_forecast_timestral_device(eng.handle, 0, ctypes.byref(win), out.data_ptr(),
+                                                           ctypes.c_void_p(stream.cuda_stream)))
+        eng.sync()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), host)
+
+
+def test_host_ends_on_device_reject_bad_windows(jc, tiny):
+    c, w, _ = tiny
+    b = mixed_block(c, covariate_groups=0)
+    lay = ts.BlockLayout.of(c, b)
+    with ts.TimestralEngine(c, w, precision="bf16") as eng:
+        bad = ts.WindowInputs.of(c, lay)
+        bad.median = c.num_quantiles
+        with pytest.raises(JcError):
+            eng.forecast(bad)
+        good = ts.WindowInputs.of(c, lay)
+        with pytest.raises(ValueError):
+            eng.forecast(good, out=np.empty((1, 1), np.float32))
 
 
 def test_sharding_across_two_slots_matches_one(jc, tiny):
