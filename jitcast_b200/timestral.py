@@ -674,20 +674,53 @@ class TimestralEngine:
             pass
 
 
+def bucket(x: int) -> int:
+    """TimestralForward.bucket (TimestralForward.java:93-99): x itself up to 8, then the next multiple of a quarter
+    of its power of two, so padding adds at most 25 % and the number of shapes grows with log(x)."""
+    if x <= 8:
+        return x
+    step = (1 << ((x - 1).bit_length() - 1)) // 4
+    return (x + step - 1) // step * step
+
+
+def bucketed_context(block: BlockInput, patch: int) -> BlockInput:
+    """The context half of TimestralForward.bucketed (TimestralForward.java:197-231): the window padded in front
+    with empty (unobserved, zero) patches up to ``bucket(patches)``. An empty patch is never a valid key and time
+    positions count from each series' first observation, so the forecasts do not change; the rows half of the
+    bucketing happens inside the engine (its plans are built for bucketed row counts)."""
+    r, t = block.inputs.shape
+    if t % patch:
+        return block  # BlockLayout.of rejects it
+    patches = t // patch
+    padded = bucket(patches)
+    if padded == patches:
+        return block
+    lead = (padded - patches) * patch
+    inputs = np.zeros((r, padded * patch), np.float32)
+    observed = np.zeros((r, padded * patch), bool)
+    inputs[:, lead:] = block.inputs
+    observed[:, lead:] = block.observed
+    return BlockInput(inputs, observed, block.group, block.horizon_patches, block.role, block.known_future,
+                      block.known_future_mask)
+
+
 class B200TimestralForward:
     """``BlockForward`` on the B200 engine: the layout on the host, the transformer on the GPUs, and
     BlockPrep's scaler and finish on the host as the reference runs them (TimestralForward.predictExact,
     TimestralForward.java:234-252), or with ``ends="device"`` on the GPU around the forward
     (``jc_forecast_timestral``: the window crosses instead of the tokens, the quantiles come back finished)."""
 
-    def __init__(self, engine: TimestralEngine, ends: str = "host"):
+    def __init__(self, engine: TimestralEngine, ends: str = "host", buckets: bool = True):
         if ends not in ("host", "device"):
             raise ValueError(f"ends must be 'host' or 'device', got {ends!r}")
         self.engine = engine
         self.config = engine.config
         self.ends = ends
+        self.buckets = buckets  # timestral.tornado.buckets: the context padded to a bucketed patch count
 
     def predict_block(self, block: BlockInput) -> np.ndarray:
+        if self.buckets:
+            block = bucketed_context(block, self.config.patch_size)
         lay = BlockLayout.of(self.config, block)
         if self.ends == "device":
             return self.engine.forecast(WindowInputs.of(self.config, lay))

@@ -110,6 +110,23 @@ def test_bucketed_plans_match_exact_plans(jc, tiny):
             np.testing.assert_array_equal(got, ref)
 
 
+def test_context_buckets_match_exact_context(jc, tiny):
+    # a 17-patch context runs on the 20-patch plan, padded in front with empty patches (TimestralForward.bucketed):
+    # no padded patch is a valid key and positions count from the first observation, so the forecasts equal the
+    # exact context's up to the attention's summation order
+    c, w, model = tiny
+    b = mixed_block(c, length=17 * c.patch_size, covariate_groups=2)
+    exp, _ = model.predict_block(b)
+    with ts.TimestralEngine(c, w, precision="fp32") as eng:
+        padded = ts.B200TimestralForward(eng).predict_block(b)
+        exact = ts.B200TimestralForward(eng, buckets=False).predict_block(b)
+        padded_dev = ts.B200TimestralForward(eng, ends="device").predict_block(b)
+    assert padded.shape == exact.shape == exp.shape
+    assert per_quantile_err(padded, exact) < 1e-5
+    assert per_quantile_err(padded, exp) < TOL["fp32"]
+    assert float(np.mean(padded_dev == padded)) >= 0.999
+
+
 def test_sign_flip_in_one_forward_matches_two(jc, tiny):
     # sign-flip TTA: the block and its negation as one concatenated forward equal the reference's two passes
     # (the block, then its negation) averaged with the complement levels, bit for bit

@@ -81,6 +81,32 @@ def test_host_finish_matches_oracle():
     np.testing.assert_allclose(mine, out, rtol=1e-5, atol=1e-5)
 
 
+def test_bucket_sizes():
+    # TimestralForward.bucket: x up to 8, then the next multiple of a quarter of its power of two
+    assert [ts.bucket(x) for x in (1, 8, 9, 10, 11, 16, 17, 21, 33, 128, 129)] == [1, 8, 10, 10, 12, 16, 20, 24, 40,
+                                                                                  128, 160]
+
+
+def test_context_bucket_pads_in_front_with_empty_patches():
+    # TimestralForward.bucketed: a 17-patch context becomes 20 patches, the 3 in front empty. No padded patch is a
+    # valid key, the real patches keep their positions and tokens (the scaler's state does not move over unobserved
+    # steps), and the oracle's forecasts agree
+    c = tiny_config()
+    b = block(c, length=17 * c.patch_size)
+    p = ts.bucketed_context(b, c.patch_size)
+    assert p.inputs.shape[1] == 20 * c.patch_size
+    assert ts.bucketed_context(p, c.patch_size) is p
+    lay, lp = ts.BlockLayout.of(c, b), ts.BlockLayout.of(c, p)
+    assert lp.context_patches == 20 and not lp.key_valid[:, :3].any()
+    np.testing.assert_array_equal(lp.key_valid[:, 3:], lay.key_valid)
+    np.testing.assert_array_equal(lp.positions()[:, 3:], lay.positions())
+    np.testing.assert_array_equal(ts.BlockPrep.of(c, lp).tokens[:, 3:], ts.BlockPrep.of(c, lay).tokens)
+    model = ots.Model(c, ts.random_checkpoint(c))
+    exact, _ = model.predict_block(b, nthreads=4)
+    padded, _ = model.predict_block(p, nthreads=4)
+    np.testing.assert_allclose(padded, exact, rtol=1e-5, atol=1e-5)
+
+
 def test_non_contiguous_series_rejected():
     c = tiny_config()
     b = block(c, covariate_groups=0)
