@@ -18,6 +18,8 @@
  *   - chronos2/ModelForward.java and chronos2/tornado/Chronos2Forward.java:148-494
  *       ModelForward.forward's device forward (Chronos2Forward)         → jc_engine_create_chronos2,
  *                                                                          jc_forward_chronos2
+ *   - chronos2/ModelPrep.java:29-137 ModelPrep.of / ModelPrep.finish    → jc_forecast_chronos2 (the
+ *       host ends on the GPU around the same forward)
  *   - tirex2/ForwardPass.java and tirex2/tornado/TornadoForward.java:353-827
  *       ForwardPass.forward's device forward (TornadoForward)           → jc_engine_create_tirex2,
  *                                                                          jc_forward_tirex2
@@ -325,6 +327,28 @@ jc_status jc_forward_chronos2(jc_engine* engine, const jc_chronos2_block* block,
 /* The same on inputs already in HBM of the engine's GPU number `slot`, enqueued on `stream`. */
 jc_status jc_forward_chronos2_device(jc_engine* engine, int slot, const jc_chronos2_block* block, float* raw_out,
                                      void* stream);
+
+/*
+ * One forward with ModelPrep's host ends moved onto the GPU (chronos2/ModelPrep.java:29-137): the
+ * layout fields of `layout` as for jc_forward_chronos2 (its `tokens` is not read and may be NULL), and
+ * the window and future covariates the tokens are made from. The GPU runs InstanceNorm (statistics in
+ * double, in the reference's order), assembles the tokens, runs the encoder, then ModelPrep.finish.
+ */
+typedef struct jc_chronos2_window {
+  jc_chronos2_block layout;
+  const float* window;       /* [rows · nc · P] ModelLayout.window, NaN = missing */
+  const float* future;       /* [rows · h · P] ModelLayout.future, NaN = missing */
+  float time_encoding_scale; /* Chronos2Config.timeEncodingScale */
+  int use_arcsinh;           /* Chronos2Config.useArcsinh */
+} jc_chronos2_window;
+
+/* ModelForward.forward after the layout, on HOST buffers: quantiles_out [rows · Q · h·P] receives
+ * ModelPrep.finish's quantiles in each row's own scale. Sharded and validated as jc_forward_chronos2. */
+jc_status jc_forecast_chronos2(jc_engine* engine, const jc_chronos2_window* block, float* quantiles_out);
+
+/* The same on device buffers of the engine's GPU number `slot`, enqueued on `stream`. */
+jc_status jc_forecast_chronos2_device(jc_engine* engine, int slot, const jc_chronos2_window* block,
+                                      float* quantiles_out, void* stream);
 
 /* TiRex-2 time-mixer kinds (the stack recipe's "bi-mlstm" / "bi-slstm", tirex2/TiRex2Config.java:161-175). */
 #define JC_TIREX_MLSTM 0

@@ -323,6 +323,17 @@ _lib.declare("jc_forward_chronos2", c_int, [c_vp, ctypes.POINTER(Block), c_vp])
 _lib.declare("jc_forward_chronos2_device", c_int, [c_vp, c_int, ctypes.POINTER(Block), c_vp, c_vp])
 
 
+class Window(ctypes.Structure):
+    """jc_chronos2_window."""
+
+    _fields_ = [("layout", Block), ("window", c_vp), ("future", c_vp), ("time_encoding_scale", ctypes.c_float),
+                ("use_arcsinh", c_int)]
+
+
+_lib.declare("jc_forecast_chronos2", c_int, [c_vp, ctypes.POINTER(Window), c_vp])
+_lib.declare("jc_forecast_chronos2_device", c_int, [c_vp, c_int, ctypes.POINTER(Window), c_vp, c_vp])
+
+
 def group_ranges(group: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     r = len(group)
     start = np.empty(r, np.int32)
@@ -384,6 +395,28 @@ class Chronos2Engine:
         check(_lib.lib().jc_forward_chronos2(self.handle, ctypes.byref(blk), raw.ctypes.data))
         return raw
 
+    def forecast(self, lay: ModelLayout, group_start, group_end, out: np.ndarray | None = None) -> np.ndarray:
+        """ModelPrep.finish's quantiles [rows, Q, h · P] with ModelPrep.of and finish on the GPU
+        (``jc_forecast_chronos2``): the window and future covariates cross instead of the tokens. Written into
+        ``out`` when given (C-contiguous float32 of that shape); inputs already C-contiguous are used in place."""
+        c = self.config
+        win = np.ascontiguousarray(lay.window, np.float32)
+        fut = np.ascontiguousarray(lay.future, np.float32)
+        live = np.ascontiguousarray(lay.live, np.int32)
+        gs = np.ascontiguousarray(group_start, np.int32)
+        ge = np.ascontiguousarray(group_end, np.int32)
+        shape = (lay.rows, c.num_quantiles, lay.output_patches * c.patch_size)
+        if out is None:
+            out = np.empty(shape, np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
+        blk = Block(lay.rows, lay.context_patches, lay.output_patches, None, live.ctypes.data, gs.ctypes.data,
+                    ge.ctypes.data)
+        w = Window(blk, win.ctypes.data, fut.ctypes.data, float(np.float32(c.time_encoding_scale)),
+                   int(c.use_arcsinh))
+        check(_lib.lib().jc_forecast_chronos2(self.handle, ctypes.byref(w), out.ctypes.data))
+        return out
+
     def set_option(self, key: str, value: int) -> None:
         check(_lib.lib().jc_engine_set_option(self.handle, key.encode(), int(value)))
 
@@ -409,11 +442,16 @@ class Chronos2Engine:
 
 
 class B200Chronos2Forward:
-    """``ModelForward`` on the B200 engine (Chronos2Forward.forward, Chronos2Forward.java:148-176)."""
+    """``ModelForward`` on the B200 engine (Chronos2Forward.forward, Chronos2Forward.java:148-176): ModelPrep's
+    host ends on the host as the reference runs them, or with ``ends="device"`` on the GPU around the encoder
+    (``jc_forecast_chronos2``)."""
 
-    def __init__(self, engine: Chronos2Engine):
+    def __init__(self, engine: Chronos2Engine, ends: str = "host"):
+        if ends not in ("host", "device"):
+            raise ValueError(f"ends must be 'host' or 'device', got {ends!r}")
         self.engine = engine
         self.config = engine.config
+        self.ends = ends
 
     def forward(self, inp: ModelInput) -> np.ndarray:
         """[rows, Q, outputPatches · P] in each row's own scale."""
@@ -424,7 +462,9 @@ class B200Chronos2Forward:
         fut = None if inp.future_covariates is None else np.asarray(inp.future_covariates)[order]
         sorted_inp = ModelInput(np.asarray(inp.context)[order], np.asarray(inp.group)[order], inp.output_patches, fut)
         lay = ModelLayout.of(self.config, sorted_inp)
-        prep = ModelPrep.of(self.config, lay)
         gs, ge = group_ranges(lay.group)
+        if self.ends == "device":
+            return self.engine.forecast(lay, gs, ge)[inv]
+        prep = ModelPrep.of(self.config, lay)
         raw = self.engine.forward_raw(lay, prep, gs, ge)
         return prep.finish(self.config, lay, raw)[inv]

@@ -57,6 +57,11 @@ struct C2Plan {
   float* table = nullptr;
   GraphRunner graph;
   std::vector<int> h_gs, h_ge;
+  // the host ends on the device (jc_forecast_chronos2), allocated on first use: per-row (loc, scale), and for
+  // host calls the window, the future covariates and the finished quantiles staged in HBM
+  DeviceMem ends_mem, stage_mem;
+  float2* norm = nullptr;
+  float *win = nullptr, *fut = nullptr, *qout = nullptr;
 };
 
 struct C2Device : DeviceSlot {
@@ -398,13 +403,14 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   return cudaGetLastError();
 }
 
-jc_status check_block(const jc_chronos2_block* b, bool host) {
+jc_status check_block(const jc_chronos2_block* b, bool host, bool tokens = true) {
   if (!b) return fail(JC_ERR_INVALID_ARG, "null block");
   if (b->rows < 1) return fail(JC_ERR_INVALID_ARG, "rows must be >= 1");
   if (b->context_patches < 1) return fail(JC_ERR_INVALID_ARG, "context patches must be >= 1");
   if (b->output_patches < 1)
     return fail(JC_ERR_INVALID_ARG, "output patches must be >= 1, got " + std::to_string(b->output_patches));
-  if (!b->tokens || !b->live || !b->group_start || !b->group_end) return fail(JC_ERR_INVALID_ARG, "null block field");
+  if ((tokens && !b->tokens) || !b->live || !b->group_start || !b->group_end)
+    return fail(JC_ERR_INVALID_ARG, "null block field");
   if (host)
     for (int i = 0; i < b->rows; ++i) {
       const int s = b->group_start[i], t = b->group_end[i];
@@ -414,8 +420,34 @@ jc_status check_block(const jc_chronos2_block* b, bool host) {
   return JC_OK;
 }
 
+// The host ends' buffers of a plan, sized for its rows: the row statistics always, the staged window,
+// future covariates and quantiles only for host calls. False when device memory runs out.
+bool ensure_ends(C2Plan& p, int P, int Q, bool host) {
+  if (!p.norm) {
+    if (!(p.norm = static_cast<float2*>(p.ends_mem.alloc(sizeof(float2) * p.rows)))) {
+      cudaGetLastError();
+      return false;
+    }
+  }
+  if (host && !p.win) {
+    const long long r = p.rows;
+    if (!(p.win = static_cast<float*>(p.stage_mem.alloc(sizeof(float) * r * p.nc * P))) ||
+        !(p.fut = static_cast<float*>(p.stage_mem.alloc(sizeof(float) * r * p.h * P))) ||
+        !(p.qout = static_cast<float*>(p.stage_mem.alloc(sizeof(float) * r * Q * p.h * P)))) {
+      cudaGetLastError();
+      p.stage_mem.release();
+      p.win = p.fut = p.qout = nullptr;
+      return false;
+    }
+  }
+  return true;
+}
+
+// Runs rows [r0, r1) of `b` on one GPU; raw_out points at the block's first row's outputs. With `ends`
+// (whose layout is `b`) the window and future covariates replace the tokens and raw_out receives
+// ModelPrep.finish's quantiles [rows · Q · h·P].
 jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b, int r0, int r1, float* raw_out,
-                    bool host, cudaStream_t stream, std::string* err) {
+                    bool host, cudaStream_t stream, std::string* err, const jc_chronos2_window* ends = nullptr) {
   if (cudaSetDevice(dv.device) != cudaSuccess) {
     *err = "cannot select device " + std::to_string(dv.device);
     return JC_ERR_CUDA;
@@ -430,8 +462,10 @@ jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b,
   C2Plan* p = get_plan(e, dv, prows, nc, h, err);
   if (!p) return JC_ERR_OOM;
   const cudaMemcpyKind kind = host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
-  cudaError_t ce = cudaMemcpyAsync(p->tok_f32, b->tokens + static_cast<long long>(r0) * ne * 3 * e.P,
-                                   sizeof(float) * rows * ne * 3 * e.P, kind, s);
+  cudaError_t ce = cudaSuccess;
+  if (!ends)
+    ce = cudaMemcpyAsync(p->tok_f32, b->tokens + static_cast<long long>(r0) * ne * 3 * e.P,
+                         sizeof(float) * rows * ne * 3 * e.P, kind, s);
   if (ce == cudaSuccess)
     ce = cudaMemcpyAsync(p->live, b->live + static_cast<long long>(r0) * n, sizeof(int) * rows * n, kind, s);
   if (ce == cudaSuccess) {
@@ -453,6 +487,44 @@ jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b,
     return JC_ERR_CUDA;
   }
   dv.prof.on = e.profile;
+  C2Ends ep;
+  if (ends) {
+    // ModelPrep.of on the GPU: the rows' instance norm, then the tokens, into the plan's token rows
+    if (!ensure_ends(*p, e.P, e.Q, host)) {
+      *err = "out of device memory for the host ends of a plan of " + std::to_string(p->rows) + " rows";
+      return JC_ERR_OOM;
+    }
+    const float* win = ends->window + static_cast<long long>(r0) * nc * e.P;
+    const float* fut = ends->future + static_cast<long long>(r0) * h * e.P;
+    if (host) {
+      ce = cudaMemcpyAsync(p->win, win, sizeof(float) * rows * nc * e.P, cudaMemcpyHostToDevice, s);
+      if (ce == cudaSuccess) ce = cudaMemcpyAsync(p->fut, fut, sizeof(float) * rows * h * e.P, cudaMemcpyHostToDevice, s);
+      if (ce != cudaSuccess) {
+        *err = std::string("upload: ") + cudaGetErrorString(ce);
+        return JC_ERR_CUDA;
+      }
+      win = p->win;
+      fut = p->fut;
+    }
+    ep.rows = rows;
+    ep.nc = nc;
+    ep.h = h;
+    ep.P = e.P;
+    ep.Q = e.Q;
+    ep.use_arcsinh = ends->use_arcsinh ? 1 : 0;
+    ep.time_scale = ends->time_encoding_scale;
+    dv.prof.begin(s, "prep.norm", 0);
+    launch_c2_norm(win, ep, p->norm, s);
+    dv.prof.end(s);
+    dv.prof.begin(s, "prep.tokens", 0);
+    launch_c2_tokens(win, fut, p->norm, ep, p->tok_f32, s);
+    dv.prof.end(s);
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+      *err = std::string("prep: ") + cudaGetErrorString(ce);
+      return JC_ERR_CUDA;
+    }
+  }
   Chronos2Engine& ec = e;
   C2Device& dvc = dv;
   ce = p->graph.run(s, [&](cudaStream_t st) { return enqueue_forward(ec, dvc, *p, st); }, e.use_graph && !e.profile);
@@ -461,8 +533,23 @@ jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b,
     return JC_ERR_CUDA;
   }
   const size_t per_row = static_cast<size_t>(h) * e.Q * e.P;
-  ce = cudaMemcpyAsync(raw_out + static_cast<size_t>(r0) * per_row, p->raw, sizeof(float) * rows * per_row,
-                       host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s);
+  const float* result = p->raw;
+  if (ends) {
+    // ModelPrep.finish on the GPU: straight into a device caller's output, else into the staged quantiles
+    float* q = host ? p->qout : raw_out + static_cast<size_t>(r0) * per_row;
+    dv.prof.begin(s, "finish", 0);
+    launch_c2_finish(p->raw, p->norm, ep, q, s);
+    dv.prof.end(s);
+    ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+      *err = std::string("finish: ") + cudaGetErrorString(ce);
+      return JC_ERR_CUDA;
+    }
+    result = q;
+  }
+  if (result != raw_out + static_cast<size_t>(r0) * per_row)
+    ce = cudaMemcpyAsync(raw_out + static_cast<size_t>(r0) * per_row, result, sizeof(float) * rows * per_row,
+                         host ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, s);
   if (ce != cudaSuccess) {
     *err = std::string("download: ") + cudaGetErrorString(ce);
     return JC_ERR_CUDA;
@@ -488,6 +575,13 @@ jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b,
     return JC_ERR_TIMEOUT;
   }
   return JC_OK;
+}
+
+jc_status check_window(const jc_chronos2_window* w, bool host) {
+  if (!w) return fail(JC_ERR_INVALID_ARG, "null block");
+  if (!w->window || !w->future) return fail(JC_ERR_INVALID_ARG, "null window field");
+  if (!(w->time_encoding_scale > 0.0f)) return fail(JC_ERR_INVALID_ARG, "time encoding scale must be > 0");
+  return check_block(&w->layout, host, false);
 }
 
 }  // namespace
@@ -596,6 +690,51 @@ jc_status jc_forward_chronos2_device(jc_engine* engine, int slot, const jc_chron
   std::lock_guard<std::mutex> lk(e->mu);
   std::string err;
   st = run_shard(*e, *e->devs[slot], block, 0, block->rows, raw_out, false, static_cast<cudaStream_t>(stream), &err);
+  return st == JC_OK ? JC_OK : fail(st, err);
+}
+
+jc_status jc_forecast_chronos2(jc_engine* engine, const jc_chronos2_window* block, float* quantiles_out) {
+  clear_error();
+  if (!engine || engine->family != 2) return fail(JC_ERR_INVALID_ARG, "not a Chronos-2 engine");
+  auto* e = static_cast<Chronos2Engine*>(engine);
+  if (!quantiles_out) return fail(JC_ERR_INVALID_ARG, "null output");
+  jc_status st = check_window(block, true);
+  if (st != JC_OK) return st;
+  const jc_chronos2_block* lay = &block->layout;
+  std::lock_guard<std::mutex> lk(e->mu);
+  const int parts = std::min<int>(static_cast<int>(e->devs.size()), lay->rows);
+  std::vector<int> cuts = shard_rows(lay->rows, lay->group_start, lay->group_end, parts);
+  std::vector<jc_status> status(parts, JC_OK);
+  std::vector<std::string> errs(parts);
+  auto work = [&](int i) {
+    if (cuts[i + 1] > cuts[i])
+      status[i] = run_shard(*e, *e->devs[i], lay, cuts[i], cuts[i + 1], quantiles_out, true, nullptr, &errs[i], block);
+  };
+  if (parts == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < parts; ++i) th.emplace_back(work, i);
+    for (auto& t : th) t.join();
+  }
+  for (int i = 0; i < parts; ++i)
+    if (status[i] != JC_OK) return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+  return JC_OK;
+}
+
+jc_status jc_forecast_chronos2_device(jc_engine* engine, int slot, const jc_chronos2_window* block,
+                                      float* quantiles_out, void* stream) {
+  clear_error();
+  if (!engine || engine->family != 2) return fail(JC_ERR_INVALID_ARG, "not a Chronos-2 engine");
+  auto* e = static_cast<Chronos2Engine*>(engine);
+  if (slot < 0 || slot >= static_cast<int>(e->devs.size())) return fail(JC_ERR_INVALID_ARG, "slot out of range");
+  if (!quantiles_out) return fail(JC_ERR_INVALID_ARG, "null output");
+  jc_status st = check_window(block, false);
+  if (st != JC_OK) return st;
+  std::lock_guard<std::mutex> lk(e->mu);
+  std::string err;
+  st = run_shard(*e, *e->devs[slot], &block->layout, 0, block->layout.rows, quantiles_out, false,
+                 static_cast<cudaStream_t>(stream), &err, block);
   return st == JC_OK ? JC_OK : fail(st, err);
 }
 

@@ -55,4 +55,22 @@ void launch_ts_tokens(const float* win, const uint8_t* obs, const float2* frame,
 // denormalised with each row's last context frame, infinities clamped.
 void launch_ts_finish(float* raw, const float2* frame, const TsEnds& ep, int steps, cudaStream_t s);
 
+// ---- the Chronos-2 host ends on the device (chronos2_ends.cu) ----
+
+// One shard's ModelPrep / finish shape: rows of nc context and h output patches of P steps, Q levels.
+struct C2Ends {
+  int rows = 0, nc = 0, h = 0, P = 0, Q = 0, use_arcsinh = 0;
+  float time_scale = 1.0f;
+};
+
+// InstanceNorm of every row of window [rows · nc·P] (NaN = missing): norm [rows] (loc, scale).
+void launch_c2_norm(const float* window, const C2Ends& ep, float2* norm, cudaStream_t s);
+
+// ModelPrep.tokens [rows · (nc + h) · 3P] from the window and future [rows · h·P].
+void launch_c2_tokens(const float* window, const float* future, const float2* norm, const C2Ends& ep, float* tok,
+                      cudaStream_t s);
+
+// ModelPrep.finish: out [rows · Q · h·P] = sinh(raw)·scale + loc, raw [rows · h · Q · P].
+void launch_c2_finish(const float* raw, const float2* norm, const C2Ends& ep, float* out, cudaStream_t s);
+
 }  // namespace jc

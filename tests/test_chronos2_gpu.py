@@ -77,6 +77,68 @@ def test_tiny_model_matches_oracle(jc, tiny, precision, covariate_groups, shuffl
     np.testing.assert_array_equal(got, got2)
 
 
+def ends_input(c, case):
+    inp = mixed_input(c, covariate_groups=0 if case == "plain" else 2, shuffle=case == "covariates")
+    if case == "degenerate":
+        ctx = inp.context.copy()
+        ctx[0] = np.where(np.isnan(ctx[0]), np.nan, np.float32(3.0))  # constant: InstanceNorm's scale floor 1e-5
+        ctx[1] = np.nan  # nothing observed: (loc, scale) = (0, 1)
+        inp = c2.ModelInput(ctx, inp.group, inp.output_patches, inp.future_covariates)
+    return inp
+
+
+@pytest.mark.parametrize("case", ["plain", "covariates", "degenerate"])
+@pytest.mark.parametrize("precision", ["fp32", "bf16"])
+def test_host_ends_on_device_match_host_ends(jc, tiny, case, precision):
+    # ModelPrep.of and ModelPrep.finish on the GPU (jc_forecast_chronos2) against the same engine with both ends
+    # on the host: the reference's arithmetic operation for operation, so equal bit for bit except where a double
+    # log or sinh (CUDA's against NumPy's) lands within an ulp of a float rounding boundary; both meet the bar
+    c, w, model = tiny
+    inp = ends_input(c, case)
+    exp, _ = model.forward(inp)
+    with c2.Chronos2Engine(c, w, precision=precision) as eng:
+        host = c2.B200Chronos2Forward(eng).forward(inp)
+        fwd = c2.B200Chronos2Forward(eng, ends="device")
+        dev = fwd.forward(inp)
+        dev2 = fwd.forward(inp)  # graph replay, staged buffers reused
+    assert dev.shape == host.shape == exp.shape
+    np.testing.assert_array_equal(dev, dev2)
+    same = float(np.mean(dev == host))
+    assert same >= 0.999, f"only {same:.4%} of the quantiles equal the host ends' bit for bit"
+    err = per_quantile_err(dev, exp)
+    assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+
+
+def test_host_ends_device_entry_point_matches_host(jc, tiny):
+    # jc_forecast_chronos2_device: window, future covariates and layout in HBM, quantiles written there
+    torch = pytest.importorskip("torch")
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    c, w, _ = tiny
+    inp = mixed_input(c, covariate_groups=2)
+    lay = c2.ModelLayout.of(c, inp)
+    gs, ge = c2.group_ranges(lay.group)
+    with c2.Chronos2Engine(c, w, precision="fp16") as eng:
+        host = eng.forecast(lay, gs, ge)
+        dev = torch.device("cuda", 0)
+        t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dt)).to(dev)  # noqa: E731
+        keep = dict(win=t(lay.window, np.float32), fut=t(lay.future, np.float32), live=t(lay.live, np.int32),
+                    gs=t(gs, np.int32), ge=t(ge, np.int32))
+        blk = c2.Block(lay.rows, lay.context_patches, lay.output_patches, None, keep["live"].data_ptr(),
+                       keep["gs"].data_ptr(), keep["ge"].data_ptr())
+        win = c2.Window(blk, keep["win"].data_ptr(), keep["fut"].data_ptr(), float(c.time_encoding_scale),
+                        int(c.use_arcsinh))
+        out = torch.empty(host.shape, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        _lib.check(_lib.lib().jc_forecast_chronos2_device(eng.handle, 0, ctypes.byref(win), out.data_ptr(),
+                                                          ctypes.c_void_p(stream.cuda_stream)))
+        eng.sync()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), host)
+
+
 def test_without_reg_token(jc):
     c = tiny_config(use_reg_token=False)
     w = c2.random_checkpoint(c, seed=6)
