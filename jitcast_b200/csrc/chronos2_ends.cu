@@ -29,20 +29,40 @@ __device__ __forceinline__ float asinh_ref(float v) {
 // InstanceNorm's floor for a constant row (ModelPrep.EPS).
 constexpr float kNormEps = 1e-5f;
 
-__global__ void c2_norm_kernel(const float* __restrict__ window, C2Ends ep, float2* __restrict__ norm) {
+__device__ __forceinline__ float f4_get(const float4& v, int k) {
+  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
+// Calls f(v) on x[0 .. W) in order. With vec (W a multiple of 32, x 16-byte aligned) 32 values are
+// loaded together per round, one memory latency instead of 32, then visited in order.
+template <typename F>
+__device__ __forceinline__ void for_each_in_order(const float* x, long long W, bool vec, F&& f) {
+  long long i = 0;
+  if (vec) {
+    for (; i + 32 <= W; i += 32) {
+      float4 v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = __ldg(reinterpret_cast<const float4*>(x + i) + k);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) f(f4_get(v[k >> 2], k & 3));
+    }
+  }
+  for (; i < W; ++i) f(x[i]);
+}
+
+__global__ void c2_norm_kernel(const float* __restrict__ window, C2Ends ep, float2* __restrict__ norm, bool vec) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= ep.rows) return;
   const long long W = static_cast<long long>(ep.nc) * ep.P;
   const float* x = window + row * W;
   double sum = 0.0;
   long long n = 0;
-  for (long long i = 0; i < W; ++i) {
-    const float v = x[i];
+  for_each_in_order(x, W, vec, [&](float v) {
     if (!isnan(v)) {
       sum = __dadd_rn(sum, static_cast<double>(v));
       ++n;
     }
-  }
+  });
   if (n == 0) {
     norm[row] = make_float2(0.0f, 1.0f);
     return;
@@ -50,13 +70,12 @@ __global__ void c2_norm_kernel(const float* __restrict__ window, C2Ends ep, floa
   const double dn = static_cast<double>(n);
   const float loc = __double2float_rn(__ddiv_rn(sum, dn));
   double ss = 0.0;
-  for (long long i = 0; i < W; ++i) {
-    const float v = x[i];
+  for_each_in_order(x, W, vec, [&](float v) {
     if (!isnan(v)) {
       const float d = __fsub_rn(v, loc);
       ss = __dadd_rn(ss, __dmul_rn(static_cast<double>(d), static_cast<double>(d)));
     }
-  }
+  });
   const float scale = __double2float_rn(sqrt(__ddiv_rn(ss, dn)));
   norm[row] = make_float2(loc, scale == 0.0f ? kNormEps : scale);
 }
@@ -128,7 +147,9 @@ int grid_cap(long long work, int threads) {
 
 void launch_c2_norm(const float* window, const C2Ends& ep, float2* norm, cudaStream_t s) {
   if (ep.rows <= 0) return;
-  c2_norm_kernel<<<(ep.rows + 31) / 32, 32, 0, s>>>(window, ep, norm);
+  const long long W = static_cast<long long>(ep.nc) * ep.P;
+  const bool vec = W % 32 == 0 && reinterpret_cast<uintptr_t>(window) % 16 == 0;
+  c2_norm_kernel<<<(ep.rows + 31) / 32, 32, 0, s>>>(window, ep, norm, vec);
 }
 
 void launch_c2_tokens(const float* window, const float* future, const float2* norm, const C2Ends& ep, float* tok,

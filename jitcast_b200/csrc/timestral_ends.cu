@@ -67,9 +67,41 @@ __device__ __forceinline__ float softplus_ref(float x) {
 // torch.finfo(torch.float32).eps, the floor of the affine transform's divisor (Scaler.FLOAT32_EPS).
 constexpr float kFloat32Eps = 1.1920928955078125e-7f;
 
+// The running state of Scaler.causalPatchLocScale: one step per value, in the reference's operation order.
+struct Welford {
+  double cum_w = 0.0, cum_x = 0.0, m2 = 0.0, prev = 0.0, mean = 0.0;
+
+  __device__ __forceinline__ void step(float x, bool observed) {
+    const double w = observed ? 1.0 : 0.0;
+    const double xi = static_cast<double>(x);
+    cum_w = __dadd_rn(cum_w, w);
+    cum_x = __dadd_rn(cum_x, __dmul_rn(w, xi));
+    mean = __ddiv_rn(cum_x, jmax(cum_w, 1.0));
+    m2 = __dadd_rn(m2, __dmul_rn(__dmul_rn(__dsub_rn(xi, prev), __dsub_rn(xi, mean)), w));
+    prev = mean;
+  }
+
+  // (loc, scale) at a patch's end: the Bessel-corrected std floored at min_scale, both rounded to float
+  __device__ __forceinline__ float2 frame(double min_scale) const {
+    const double var = __ddiv_rn(m2, jmax(__dsub_rn(jmax(cum_w, 1.0), 1.0), 1.0));
+    return make_float2(__double2float_rn(mean), __double2float_rn(jmax(sqrt(var), min_scale)));
+  }
+};
+
+__device__ __forceinline__ float f4_get(const float4& v, int k) {
+  return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
+__device__ __forceinline__ uint32_t u4_byte(const uint4& v, int k) {
+  const int w = k >> 2;
+  const uint32_t word = w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+  return (word >> ((k & 3) * 8)) & 0xffu;
+}
+
+// vec: rows of a multiple of 32 steps, window and flags 16-byte aligned
 __global__ void ts_scaler_kernel(const float* __restrict__ win, const uint8_t* __restrict__ obs,
                                  const int* __restrict__ known, TsEnds ep, float2* __restrict__ frame,
-                                 uint8_t* __restrict__ row_asinh) {
+                                 uint8_t* __restrict__ row_asinh, bool vec) {
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= ep.rows) return;
   const int P = ep.P, enc = ep.enc;
@@ -107,22 +139,36 @@ __global__ void ts_scaler_kernel(const float* __restrict__ win, const uint8_t* _
     return;
   }
   // Scaler.causalPatchLocScale: Welford over every observed value up to each patch's end
-  double cum_w = 0.0, cum_x = 0.0, m2 = 0.0, prev = 0.0, mean = 0.0;
+  Welford s;
   const double min_scale = static_cast<double>(ep.min_scale);
-  for (int p = 0; p < enc; ++p) {
-    const float* xp = x + static_cast<long long>(p) * P;
-    const uint8_t* op = o + static_cast<long long>(p) * P;
-    for (int st = 0; st < P; ++st) {
-      const double w = op[st] ? 1.0 : 0.0;
-      const double xi = static_cast<double>(xp[st]);
-      cum_w = __dadd_rn(cum_w, w);
-      cum_x = __dadd_rn(cum_x, __dmul_rn(w, xi));
-      mean = __ddiv_rn(cum_x, jmax(cum_w, 1.0));
-      m2 = __dadd_rn(m2, __dmul_rn(__dmul_rn(__dsub_rn(xi, prev), __dsub_rn(xi, mean)), w));
-      prev = mean;
+  int st = 0, p = 0;
+  long long i = 0;
+  if (vec) {
+    // 32 steps per round: their values and flags loaded together (one memory latency instead of 32), then
+    // walked in order
+    for (; i + 32 <= W; i += 32) {
+      float4 xv[8];
+      uint4 ov[2];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) xv[k] = __ldg(reinterpret_cast<const float4*>(x + i) + k);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) ov[k] = __ldg(reinterpret_cast<const uint4*>(o + i) + k);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        s.step(f4_get(xv[k >> 2], k & 3), u4_byte(ov[k >> 4], k & 15) != 0);
+        if (++st == P) {
+          fr[p++] = s.frame(min_scale);
+          st = 0;
+        }
+      }
     }
-    const double var = __ddiv_rn(m2, jmax(__dsub_rn(jmax(cum_w, 1.0), 1.0), 1.0));
-    fr[p] = make_float2(__double2float_rn(mean), __double2float_rn(jmax(sqrt(var), min_scale)));
+  }
+  for (; i < W; ++i) {
+    s.step(x[i], o[i] != 0);
+    if (++st == P) {
+      fr[p++] = s.frame(min_scale);
+      st = 0;
+    }
   }
   row_asinh[row] = ep.use_asinh != 0;
 }
@@ -223,7 +269,10 @@ void launch_ts_scaler(const float* win, const uint8_t* obs, const int* known, co
                       uint8_t* row_asinh, cudaStream_t s) {
   if (ep.rows <= 0) return;
   // one warp per CTA spreads the rows' sequential walks over as many SMs as possible
-  ts_scaler_kernel<<<(ep.rows + 31) / 32, 32, 0, s>>>(win, obs, known, ep, frame, row_asinh);
+  const long long W = static_cast<long long>(ep.enc) * ep.P;
+  const bool vec = W % 32 == 0 && reinterpret_cast<uintptr_t>(win) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(obs) % 16 == 0;
+  ts_scaler_kernel<<<(ep.rows + 31) / 32, 32, 0, s>>>(win, obs, known, ep, frame, row_asinh, vec);
 }
 
 void launch_ts_tokens(const float* win, const uint8_t* obs, const float2* frame, const uint8_t* row_asinh,
