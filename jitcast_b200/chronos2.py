@@ -331,6 +331,9 @@ class Window(ctypes.Structure):
 
 
 _lib.declare("jc_forecast_chronos2", c_int, [c_vp, ctypes.POINTER(Window), c_vp])
+_lib.declare("jc_engine_profile", c_int, [c_vp, c_int, ctypes.POINTER(ctypes.c_char_p),
+                                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong),
+                                          ctypes.POINTER(ctypes.c_double), c_int, ctypes.POINTER(c_int)])
 _lib.declare("jc_forecast_chronos2_device", c_int, [c_vp, c_int, ctypes.POINTER(Window), c_vp, c_vp])
 
 
@@ -419,6 +422,17 @@ class Chronos2Engine:
 
     def set_option(self, key: str, value: int) -> None:
         check(_lib.lib().jc_engine_set_option(self.handle, key.encode(), int(value)))
+
+    def profile(self, slot: int = 0) -> dict[str, dict[str, float]]:
+        """Per-stage totals since the last read (engine option ``profile``): ms, launches, flops."""
+        cap = 32
+        names = (ctypes.c_char_p * cap)()
+        ms = (ctypes.c_double * cap)()
+        launches = (ctypes.c_longlong * cap)()
+        flops = (ctypes.c_double * cap)()
+        n = c_int()
+        check(_lib.lib().jc_engine_profile(self.handle, slot, names, ms, launches, flops, cap, ctypes.byref(n)))
+        return {names[i].decode(): {"ms": ms[i], "launches": launches[i], "flops": flops[i]} for i in range(n.value)}
 
     def sync(self) -> None:
         check(_lib.lib().jc_engine_sync(self.handle))
