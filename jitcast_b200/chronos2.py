@@ -457,10 +457,10 @@ class Chronos2Engine:
 
 class B200Chronos2Forward:
     """``ModelForward`` on the B200 engine (Chronos2Forward.forward, Chronos2Forward.java:148-176): ModelPrep's
-    host ends on the host as the reference runs them, or with ``ends="device"`` on the GPU around the encoder
-    (``jc_forecast_chronos2``)."""
+    host ends on the GPU around the encoder (``jc_forecast_chronos2``), or with ``ends="host"`` on the host as
+    the reference runs them (``jc_forward_chronos2``)."""
 
-    def __init__(self, engine: Chronos2Engine, ends: str = "host"):
+    def __init__(self, engine: Chronos2Engine, ends: str = "device"):
         if ends not in ("host", "device"):
             raise ValueError(f"ends must be 'host' or 'device', got {ends!r}")
         self.engine = engine

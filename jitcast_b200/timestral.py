@@ -706,11 +706,12 @@ def bucketed_context(block: BlockInput, patch: int) -> BlockInput:
 
 class B200TimestralForward:
     """``BlockForward`` on the B200 engine: the layout on the host, the transformer on the GPUs, and
-    BlockPrep's scaler and finish on the host as the reference runs them (TimestralForward.predictExact,
-    TimestralForward.java:234-252), or with ``ends="device"`` on the GPU around the forward
-    (``jc_forecast_timestral``: the window crosses instead of the tokens, the quantiles come back finished)."""
+    BlockPrep's scaler and finish on the GPU around the forward (``jc_forecast_timestral``: the window crosses
+    instead of the tokens, the quantiles come back finished; the NumPy host prep of a 8,192-series config-5
+    chunk alone takes seconds), or with ``ends="host"`` on the host as the reference runs them
+    (TimestralForward.predictExact, TimestralForward.java:234-252; ``jc_forward_timestral``)."""
 
-    def __init__(self, engine: TimestralEngine, ends: str = "host", buckets: bool = True):
+    def __init__(self, engine: TimestralEngine, ends: str = "device", buckets: bool = True):
         if ends not in ("host", "device"):
             raise ValueError(f"ends must be 'host' or 'device', got {ends!r}")
         self.engine = engine

@@ -68,12 +68,15 @@ def test_tiny_model_matches_oracle(jc, tiny, precision, covariate_groups, shuffl
     inp = mixed_input(c, covariate_groups=covariate_groups, shuffle=shuffle)
     exp, _ = model.forward(inp)
     with c2.Chronos2Engine(c, w, precision=precision) as eng:
-        fwd = c2.B200Chronos2Forward(eng)
+        fwd = c2.B200Chronos2Forward(eng)  # the host ends on the GPU (the default)
         got = fwd.forward(inp)
         got2 = fwd.forward(inp)  # graph replay
+        got_host = c2.B200Chronos2Forward(eng, ends="host").forward(inp)  # jc_forward_chronos2
     assert got.shape == exp.shape
     err = per_quantile_err(got, exp)
     assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+    err_host = per_quantile_err(got_host, exp)
+    assert err_host < TOL[precision], f"{precision}, host ends: per-quantile rel max err {err_host:.3e}"
     np.testing.assert_array_equal(got, got2)
 
 
@@ -97,7 +100,7 @@ def test_host_ends_on_device_match_host_ends(jc, tiny, case, precision):
     inp = ends_input(c, case)
     exp, _ = model.forward(inp)
     with c2.Chronos2Engine(c, w, precision=precision) as eng:
-        host = c2.B200Chronos2Forward(eng).forward(inp)
+        host = c2.B200Chronos2Forward(eng, ends="host").forward(inp)
         fwd = c2.B200Chronos2Forward(eng, ends="device")
         dev = fwd.forward(inp)
         dev2 = fwd.forward(inp)  # graph replay, staged buffers reused

@@ -73,12 +73,15 @@ def test_tiny_model_matches_oracle(jc, tiny, precision, covariate_groups):
     b = mixed_block(c, covariate_groups=covariate_groups)
     exp, exp_raw = model.predict_block(b)
     with ts.TimestralEngine(c, w, precision=precision) as eng:
-        fwd = ts.B200TimestralForward(eng)
+        fwd = ts.B200TimestralForward(eng)  # the host ends on the GPU (the default)
         got = fwd.predict_block(b)
         got2 = fwd.predict_block(b)  # second call replays the captured CUDA graph
+        got_host = ts.B200TimestralForward(eng, ends="host").predict_block(b)  # jc_forward_timestral
     assert got.shape == exp.shape
     err = per_quantile_err(got, exp)
     assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
+    err_host = per_quantile_err(got_host, exp)
+    assert err_host < TOL[precision], f"{precision}, host ends: per-quantile rel max err {err_host:.3e}"
     np.testing.assert_array_equal(got, got2)
 
 
@@ -118,8 +121,8 @@ def test_context_buckets_match_exact_context(jc, tiny):
     b = mixed_block(c, length=17 * c.patch_size, covariate_groups=2)
     exp, _ = model.predict_block(b)
     with ts.TimestralEngine(c, w, precision="fp32") as eng:
-        padded = ts.B200TimestralForward(eng).predict_block(b)
-        exact = ts.B200TimestralForward(eng, buckets=False).predict_block(b)
+        padded = ts.B200TimestralForward(eng, ends="host").predict_block(b)
+        exact = ts.B200TimestralForward(eng, ends="host", buckets=False).predict_block(b)
         padded_dev = ts.B200TimestralForward(eng, ends="device").predict_block(b)
     assert padded.shape == exact.shape == exp.shape
     assert per_quantile_err(padded, exact) < 1e-5
@@ -178,7 +181,7 @@ def test_host_ends_on_device_match_host_ends(jc, tiny, case, precision):
     b = ends_block(c, case)
     exp, _ = model.predict_block(b)
     with ts.TimestralEngine(c, w, precision=precision) as eng:
-        host = ts.B200TimestralForward(eng).predict_block(b)
+        host = ts.B200TimestralForward(eng, ends="host").predict_block(b)
         dev_fwd = ts.B200TimestralForward(eng, ends="device")
         dev = dev_fwd.predict_block(b)
         dev2 = dev_fwd.predict_block(b)  # graph replay, staged buffers reused
