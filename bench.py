@@ -72,6 +72,9 @@ def workload_config(args, world):
             "series_per_step": args.series, "series_per_gpu": args.series // world, "chunk_series": args.chunk,
             "context": 4096, "horizon_patches": 2, "tokens_per_series": 130, "precision": args.precision,
             "parallelism": f"series-sharded x{world}, no collective",
+            "path": "value: jc_forecast_timestral_device on each chunk's window, observed flags and layout resident "
+                    "in HBM (BlockPrep.of, the forward and BlockPrep.finish on the GPU); e2e: jc_forecast_timestral "
+                    "from pinned host buffers, copies timed; BlockLayout.of before the timed region",
             "l2": "no flush: every forward's working set (GBs) is far larger than the 126 MB L2"}
 
 
@@ -367,30 +370,33 @@ def main():
     per_rank = args.series // world
     first = rank * per_rank
     chunks = []
-    win_in = []  # each chunk's window and layout, for the end-to-end forecast
+    win_in = []  # each chunk's window and layout (host arrays), for the end-to-end forecast
+    lay_fields = ("positions", "key_valid", "known", "role", "group_start", "group_end")
     for c0 in range(first, first + per_rank, args.chunk):
         n = min(args.chunk, first + per_rank - c0)
         x = workloads.sinusoid_noise(n, 4096, seed=c0)  # chunk-seeded: the same series for every N
         b = ts.BlockInput(x, np.ones_like(x, bool), np.arange(n, dtype=np.int32), 2)
-        lay = ts.BlockLayout.of(cfg, b)
-        prep = ts.BlockPrep.of(cfg, lay)
-        hin = ts.DeviceInputs.of(lay, prep)
-        win_in.append(ts.WindowInputs.of(cfg, lay))
-        d = {k: torch.from_numpy(np.ascontiguousarray(getattr(hin, k))).to(dev)
-             for k in ("tokens", "positions", "key_valid", "known", "role", "group_start", "group_end")}
-        raw = torch.empty(n * 2, cfg.patch_size * cfg.num_quantiles, device=dev)
-        blk = ts.Block(hin.rows, hin.encoder, hin.horizon, hin.context_patches, hin.covariates,
-                       *(d[k].data_ptr() for k in ("tokens", "positions", "key_valid", "known", "role",
-                                                   "group_start", "group_end")))
-        chunks.append((hin, d, raw, blk, n))
+        wi = ts.WindowInputs.of(cfg, ts.BlockLayout.of(cfg, b))
+        win_in.append(wi)
+        # resident in HBM: the window, its observed flags and the layout; the GPU runs BlockPrep.of, the forward
+        # and BlockPrep.finish (jc_forecast_timestral_device)
+        d = {k: torch.from_numpy(np.ascontiguousarray(getattr(wi.layout, k))).to(dev) for k in lay_fields}
+        d["window"], d["observed"] = torch.from_numpy(wi.window).to(dev), torch.from_numpy(wi.observed).to(dev)
+        out = torch.empty(n, 2 * cfg.patch_size, cfg.num_quantiles, device=dev)
+        L0 = wi.layout
+        blk = ts.Block(L0.rows, L0.encoder, L0.horizon, L0.context_patches, L0.covariates, None,
+                       *(d[k].data_ptr() for k in lay_fields))
+        win = ts.Window(blk, d["window"].data_ptr(), d["observed"].data_ptr(), wi.minimum_scale, wi.use_asinh,
+                        wi.median, wi.quantile_scale.ctypes.data)
+        chunks.append((wi, d, out, win, n))
     L = _lib.lib()
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
 
     def device_step():
-        for _, _, raw, blk, _ in chunks:
-            _lib.check(L.jc_forward_timestral_device(engine.handle, 0, ctypes.byref(blk), raw.data_ptr(),
-                                                     stream.cuda_stream))
+        for _, _, out, win, _ in chunks:
+            _lib.check(L.jc_forecast_timestral_device(engine.handle, 0, ctypes.byref(win), out.data_ptr(),
+                                                      stream.cuda_stream))
 
     def barrier():
         if world > 1:
@@ -425,7 +431,7 @@ def main():
     # end to end through the host C ABI (jc_forecast_timestral): each chunk's window, observed flags and layout
     # from pinned host buffers, BlockPrep's scaler and tokens, the forward and BlockPrep.finish on the GPU, the
     # finished quantiles back into pinned host buffers, copies timed (the layout itself is built before)
-    fields = ("positions", "key_valid", "known", "role", "group_start", "group_end")
+    fields = lay_fields
     host_chunks = []
     for wi, (_, _, _, _, n) in zip(win_in, chunks):
         lp = dataclasses.replace(wi.layout, **{k: pinned(getattr(wi.layout, k)) for k in fields})
@@ -446,17 +452,15 @@ def main():
     e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
     barrier()
 
-    # kernel-class timings of one profiled forward (eager, CUDA events around every launch)
+    # kernel-class timings of one profiled forecast (eager, CUDA events around every launch)
     engine.set_option("profile", 1)
-    hin0, _, raw0, blk0, n0 = chunks[0]
-    _lib.check(L.jc_forward_timestral_device(engine.handle, 0, ctypes.byref(blk0), raw0.data_ptr(),
-                                             stream.cuda_stream))
+    _, _, out0, win0, _ = chunks[0]
+    _lib.check(L.jc_forecast_timestral_device(engine.handle, 0, ctypes.byref(win0), out0.data_ptr(),
+                                              stream.cuda_stream))
     torch.cuda.synchronize()
     prof = engine.profile()
-    # the host ends on the GPU (scaler, tokens, finish) of one chunk's forecast, timed the same way
-    engine.forecast(host_chunks[0][0], out=host_chunks[0][1])
-    ends_prof = {k: v for k, v in engine.profile().items() if k.startswith(("prep", "finish"))}
     engine.set_option("profile", 0)
+    ends_prof = {k: v for k, v in prof.items() if k.startswith(("prep", "finish"))}
     launches_per_forward = sum(v["launches"] for v in prof.values()) + 3  # + the 3 index-rebasing kernels
     gemms = {k: v for k, v in prof.items() if k.startswith("gemm")}
     g = {f: sum(v[f] for v in gemms.values()) for f in ("ms", "launches", "flops")}
