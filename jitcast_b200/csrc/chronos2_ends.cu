@@ -136,13 +136,6 @@ __global__ void c2_finish_kernel(const float* __restrict__ raw, const float2* __
   }
 }
 
-int grid_cap(long long work, int threads) {
-  long long b = (work + threads - 1) / threads;
-  const long long cap = 148LL * 16;
-  if (b > cap) b = cap;
-  return b < 1 ? 1 : static_cast<int>(b);
-}
-
 }  // namespace
 
 void launch_c2_norm(const float* window, const C2Ends& ep, float2* norm, cudaStream_t s) {
@@ -156,13 +149,13 @@ void launch_c2_tokens(const float* window, const float* future, const float2* no
                       cudaStream_t s) {
   const long long n = static_cast<long long>(ep.rows) * (ep.nc + ep.h) * ep.P;
   if (n <= 0) return;
-  c2_tokens_kernel<<<grid_cap(n, 256), 256, 0, s>>>(window, future, norm, ep, tok);
+  c2_tokens_kernel<<<grid_for(n, 256), 256, 0, s>>>(window, future, norm, ep, tok);
 }
 
 void launch_c2_finish(const float* raw, const float2* norm, const C2Ends& ep, float* out, cudaStream_t s) {
   const long long n = static_cast<long long>(ep.rows) * ep.Q * ep.h * ep.P;
   if (n <= 0) return;
-  c2_finish_kernel<<<grid_cap(n, 256), 256, 0, s>>>(raw, norm, ep, out);
+  c2_finish_kernel<<<grid_for(n, 256), 256, 0, s>>>(raw, norm, ep, out);
 }
 
 }  // namespace jc

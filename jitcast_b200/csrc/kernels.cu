@@ -125,14 +125,14 @@ __global__ void add_i32_kernel(const int* __restrict__ in, int* __restrict__ out
     out[i] = in[i] + add;
 }
 
+}  // namespace
+
 int grid_for(long long work, int threads) {
   long long b = (work + threads - 1) / threads;
-  const long long cap = 148LL * 16;
+  const long long cap = 148LL * 16;  // 16 CTAs on each of the 148 SMs, grid-stride beyond
   if (b > cap) b = cap;
   return b < 1 ? 1 : static_cast<int>(b);
 }
-
-}  // namespace
 
 void launch_convert(int op, const float* src, long long lds, void* dst_hi, void* dst_lo, long long ldd,
                     long long rows, int cols, cudaStream_t s) {

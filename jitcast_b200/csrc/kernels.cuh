@@ -25,6 +25,9 @@ void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, flo
 void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int t0, int t1, int n,
                       cudaStream_t s);
 
+// Blocks of `threads` for `work` grid-stride items: enough to cover it, at most 16 per SM of the 148.
+int grid_for(long long work, int threads);
+
 // out[i] = in[i] + add for i < n (integer index rebasing on the device).
 void launch_add_i32(const int* in, int* out, long long n, int add, cudaStream_t s);
 

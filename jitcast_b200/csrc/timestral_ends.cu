@@ -256,13 +256,6 @@ __global__ void ts_finish_kernel(float* __restrict__ q, const float2* __restrict
   }
 }
 
-int grid_cap(long long work, int threads) {
-  long long b = (work + threads - 1) / threads;
-  const long long cap = 148LL * 16;
-  if (b > cap) b = cap;
-  return b < 1 ? 1 : static_cast<int>(b);
-}
-
 }  // namespace
 
 void launch_ts_scaler(const float* win, const uint8_t* obs, const int* known, const TsEnds& ep, float2* frame,
@@ -282,16 +275,16 @@ void launch_ts_tokens(const float* win, const uint8_t* obs, const float2* frame,
   const bool vec = ep.P % 4 == 0 && reinterpret_cast<uintptr_t>(win) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(obs) % 4 == 0 && reinterpret_cast<uintptr_t>(tok) % 16 == 0;
   if (vec) {
-    ts_tokens_kernel<4><<<grid_cap(n / 4, 256), 256, 0, s>>>(win, obs, frame, row_asinh, ep, tok);
+    ts_tokens_kernel<4><<<grid_for(n / 4, 256), 256, 0, s>>>(win, obs, frame, row_asinh, ep, tok);
   } else {
-    ts_tokens_kernel<1><<<grid_cap(n, 256), 256, 0, s>>>(win, obs, frame, row_asinh, ep, tok);
+    ts_tokens_kernel<1><<<grid_for(n, 256), 256, 0, s>>>(win, obs, frame, row_asinh, ep, tok);
   }
 }
 
 void launch_ts_finish(float* raw, const float2* frame, const TsEnds& ep, int steps, cudaStream_t s) {
   const long long n = static_cast<long long>(ep.rows) * steps;
   if (n <= 0) return;
-  ts_finish_kernel<<<grid_cap(n, 128), 128, 0, s>>>(raw, frame, ep, steps);
+  ts_finish_kernel<<<grid_for(n, 128), 128, 0, s>>>(raw, frame, ep, steps);
 }
 
 }  // namespace jc

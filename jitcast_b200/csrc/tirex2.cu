@@ -1139,13 +1139,6 @@ __global__ void unpatch_kernel(const float* __restrict__ y, const float* __restr
   }
 }
 
-int grid_for(long long work, int threads) {
-  long long b = (work + threads - 1) / threads;
-  const long long cap = 148LL * 16;
-  if (b > cap) b = cap;
-  return b < 1 ? 1 : static_cast<int>(b);
-}
-
 // ---- engine -------------------------------------------------------------------------------------
 
 struct TxBlock {
