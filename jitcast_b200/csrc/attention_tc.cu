@@ -124,12 +124,18 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   const bool known = a.mask_mode == 0 && a.known[row] != 0;
   const T* qkv = static_cast<const T*>(a.qkv);
 
+  const long long row0 = static_cast<long long>(row) * n;
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
     mbar_init(&bars[2], 1);
     *abort_flag = 0;
     fence_mbar_init();
+    // the head's Q, K and V in flight from the start, under the TMEM allocation and the key-flag loads
+    mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(kTcQ * 128 + 2 * sh.nkl * 128));
+    tma_load_2d(qs, &tmQ, &bars[0], hh * 64, static_cast<int>(row0));
+    tma_load_2d(ks, &tmKV, &bars[0], a.d + hh * 64, static_cast<int>(row0));
+    tma_load_2d(vs, &tmKV, &bars[0], 2 * a.d + hh * 64, static_cast<int>(row0));
   }
   __syncwarp();
   if (warp == 0) {
@@ -152,14 +158,6 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const long long row0 = static_cast<long long>(row) * n;
-
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bars[0], static_cast<uint32_t>(kTcQ * 128 + 2 * sh.nkl * 128));
-    tma_load_2d(qs, &tmQ, &bars[0], hh * 64, static_cast<int>(row0));
-    tma_load_2d(ks, &tmKV, &bars[0], a.d + hh * 64, static_cast<int>(row0));
-    tma_load_2d(vs, &tmKV, &bars[0], 2 * a.d + hh * 64, static_cast<int>(row0));
-  }
   // the first tail round's q and gate rows (queries past the MMA tile), one 16-byte chunk per thread,
   // in flight during the TMA wait
   uint4 pq = make_uint4(0u, 0u, 0u, 0u), pg = make_uint4(0u, 0u, 0u, 0u);
