@@ -80,3 +80,17 @@ def test_no_device_is_reported():
     st = _call_linear()
     assert st == _lib.ERR_NO_DEVICE
     assert "device" in _lib.last_error().lower()
+
+
+@pytest.mark.parametrize("name", ["jc_forecast_timestral", "jc_forecast_chronos2", "jc_forward_timestral",
+                                  "jc_forward_chronos2", "jc_forward_tirex2"])
+def test_model_forwards_reject_a_null_engine(name):
+    # the reference's fail-fast contract: a bad handle is an argument error, reported before any device work
+    assert getattr(_lib.lib(), name)(None, None, None) == _lib.ERR_INVALID_ARG
+    assert "engine" in _lib.last_error()
+
+
+@pytest.mark.parametrize("name", ["jc_forecast_timestral_device", "jc_forecast_chronos2_device"])
+def test_device_forecasts_reject_a_null_engine(name):
+    assert getattr(_lib.lib(), name)(None, 0, None, None, None) == _lib.ERR_INVALID_ARG
+    assert "engine" in _lib.last_error()
