@@ -380,16 +380,30 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
           add_bias(p, n0 + ca, 32, a);
           add_bias(p, n0 + cb, 32, b);
         }
-        if (n0 + ca < p.rope_cols) {
+        // the pairs of this chunk that rotate (a partial rotary factor leaves the rest as they are)
+        const int nr = min(32, (p.rope_pairs > 0 ? p.rope_pairs : hh) - s);
+        if (n0 + ca < p.rope_cols && nr > 0) {
           float cs[32], sn[32];
           const float* tc = p.rope_table + (long long)pos * hd + s;
-          load_ro(tc, 32, p.vec_ok, cs);
-          load_ro(tc + hh, 32, p.vec_ok, sn);
+          if (nr == 16 && p.vec_ok >= 1) {  // a half-rotary head: 16 cos and 16 sin in 16-byte vectors
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 c4 = __ldg(reinterpret_cast<const float4*>(tc) + q);
+              const float4 s4 = __ldg(reinterpret_cast<const float4*>(tc + hh) + q);
+              cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+              sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+            }
+          } else {
+            load_ro(tc, nr, p.vec_ok, cs);
+            load_ro(tc + hh, nr, p.vec_ok, sn);
+          }
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float x = a[j], y = b[j];
-            a[j] = x * cs[j] + -y * sn[j];
-            b[j] = y * cs[j] + x * sn[j];
+            if (j < nr) {
+              const float x = a[j], y = b[j];
+              a[j] = x * cs[j] + -y * sn[j];
+              b[j] = y * cs[j] + x * sn[j];
+            }
           }
         }
         store_operand(p, (long long)orow * p.ldo + n0 + ca, 32, a);

@@ -67,6 +67,9 @@ struct EpiParams {
   int rg, rg_stride, rg_off, rg_split, rg_shift;
   // kEpiQKV
   int rope_cols, head_dim;
+  // pairs (e, e + head_dim/2) with a nonzero frequency, e < rope_pairs; 0 = all. A partial rotary factor
+  // leaves the other pairs at cos 1, sin 0 — the identity — so the epilogue neither loads nor applies them.
+  int rope_pairs;
   const int* pos;           // [M] index into rope_table rows
   const float* rope_table;  // [positions, head_dim]: cos at e, sin at head_dim/2 + e
   int n_split;

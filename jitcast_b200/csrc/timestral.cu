@@ -385,6 +385,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       g.ep.ldo = 3LL * d;
       g.ep.rope_cols = A.time ? 2 * d : 0;
       g.ep.head_dim = e.dh;
+      g.ep.rope_pairs = e.rope_dim / 2;  // partial rotary: the pairs past rope_dim/2 keep cos 1, sin 0
       g.ep.pos = p.pos;
       g.ep.rope_table = p.table;
       g.ep.n_split = 3 * d;
