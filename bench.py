@@ -42,6 +42,26 @@ GEMM_BYTES_PER_LAUNCH_1024 = 1.674e9
 UNIT = "series/s"
 
 
+def rank_chunks(series: int, chunk: int, world: int, rank: int) -> list[tuple[int, int]]:
+    """The (first series, count) of every forward call of one rank: the batch split evenly over the ranks, each
+    share in chunks. Chunks are seeded by their first series, so every N runs the same series."""
+    per_rank = series // world
+    first = rank * per_rank
+    return [(c0, min(chunk, first + per_rank - c0)) for c0 in range(first, first + per_rank, chunk)]
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    """The largest of every rank's v (the whole job's time is its slowest rank's)."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def peaks() -> tuple[dict, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -368,12 +388,10 @@ def main():
     engine = ts.TimestralEngine(cfg, weights, devices=(local,), precision=args.precision)
 
     per_rank = args.series // world
-    first = rank * per_rank
     chunks = []
     win_in = []  # each chunk's window and layout (host arrays), for the end-to-end forecast
     lay_fields = ("positions", "key_valid", "known", "role", "group_start", "group_end")
-    for c0 in range(first, first + per_rank, args.chunk):
-        n = min(args.chunk, first + per_rank - c0)
+    for c0, n in rank_chunks(args.series, args.chunk, world, rank):
         x = workloads.sinusoid_noise(n, 4096, seed=c0)  # chunk-seeded: the same series for every N
         b = ts.BlockInput(x, np.ones_like(x, bool), np.arange(n, dtype=np.int32), 2)
         wi = ts.WindowInputs.of(cfg, ts.BlockLayout.of(cfg, b))
@@ -402,12 +420,8 @@ def main():
         if world > 1:
             dist.barrier()
 
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    def over_ranks(v: float) -> float:
+        return max_over_ranks(v, world, dev)
 
     for _ in range(max(args.warmup, 3)):
         device_step()
@@ -425,7 +439,7 @@ def main():
         torch.cuda.synchronize()
     engine.sync()
     barrier()
-    ms = max_over_ranks(start.elapsed_time(stop) / args.steps)
+    ms = over_ranks(start.elapsed_time(stop) / args.steps)
     value = args.series / (ms / 1000.0)
 
     # end to end through the host C ABI (jc_forecast_timestral): each chunk's window, observed flags and layout
@@ -449,7 +463,7 @@ def main():
             engine.forecast(hp, out=qp)
             h2d += hp.window.nbytes + hp.observed.nbytes + sum(getattr(hp.layout, k).nbytes for k in fields)
             d2h += qp.nbytes
-    e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+    e2e_s = over_ranks((time.perf_counter() - t0) / args.steps)
     barrier()
 
     # kernel-class timings of one profiled forecast (eager, CUDA events around every launch)

@@ -416,6 +416,15 @@ jc_status jc_forward_tirex2_device(jc_engine* engine, int slot, const jc_tirex2_
 jc_status jc_engine_sync(jc_engine* engine);
 
 /*
+ * The rule every multi-GPU forward shards rows by (host arithmetic only, no device): cuts_out[0 .. parts]
+ * receives the first row of each of `parts` contiguous ranges and cuts_out[parts] = rows. Each cut starts
+ * at rows·p/parts and moves forward to the next series boundary, so no series (group_start/group_end,
+ * as the blocks carry them) spans two GPUs; a range may be empty. JC_ERR_INVALID_ARG for rows < 0,
+ * parts < 1, null arrays or series ranges that are not contiguous.
+ */
+jc_status jc_shard_rows(int rows, const int32_t* group_start, const int32_t* group_end, int parts, int32_t* cuts_out);
+
+/*
  * Engine options (the reference's -D properties, e.g. timestral.tornado.cudaGraph and
  * timestral.tornado.plans in TimestralForward.java:146-160):
  *   "cuda_graph"  1 (default) replay each shape as a captured CUDA graph, 0 run eagerly

@@ -13,3 +13,17 @@ __version__ = "0.1.0"
 
 def version() -> str:
     return lib().jc_version().decode()
+
+
+def shard_rows(group_start, group_end, parts: int):
+    """``jc_shard_rows``: the first row of each of ``parts`` contiguous row ranges (and the row count last) that
+    a multi-GPU forward gives its GPUs, no series split across two."""
+    import numpy as np
+
+    from ._lib import check
+
+    gs = np.ascontiguousarray(group_start, np.int32)
+    ge = np.ascontiguousarray(group_end, np.int32)
+    cuts = np.empty(parts + 1, np.int32)
+    check(lib().jc_shard_rows(len(gs), gs.ctypes.data, ge.ctypes.data, parts, cuts.ctypes.data))
+    return cuts

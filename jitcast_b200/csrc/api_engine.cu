@@ -9,6 +9,20 @@ using namespace jc;
 
 extern "C" {
 
+jc_status jc_shard_rows(int rows, const int32_t* group_start, const int32_t* group_end, int parts, int32_t* cuts_out) {
+  clear_error();
+  if (rows < 0 || parts < 1) return fail(JC_ERR_INVALID_ARG, "rows must be >= 0 and parts >= 1");
+  if (!cuts_out || (rows > 0 && (!group_start || !group_end))) return fail(JC_ERR_INVALID_ARG, "null array");
+  for (int i = 0; i < rows; ++i) {
+    const int s = group_start[i], t = group_end[i];
+    if (s < 0 || s > i || t <= i || t > rows || group_start[s] != s || group_end[s] != t)
+      return fail(JC_ERR_INVALID_ARG, "rows of a series are not contiguous (row " + std::to_string(i) + ")");
+  }
+  const std::vector<int> cuts = jc::shard_rows(rows, group_start, group_end, parts);
+  for (int p = 0; p <= parts; ++p) cuts_out[p] = cuts[p];
+  return JC_OK;
+}
+
 jc_status jc_engine_sync(jc_engine* engine) {
   clear_error();
   if (!engine) return fail(JC_ERR_INVALID_ARG, "null engine");
