@@ -504,8 +504,9 @@ def main():
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
             "config": workload_config(args, world),
-            "e2e": {"value": args.series / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d // args.steps,
-                    "d2h_bytes_per_step": d2h // args.steps},
+            # whole-job bytes: every rank moves the same share
+            "e2e": {"value": args.series / e2e_s, "unit": UNIT, "h2d_bytes_per_step": world * h2d // args.steps,
+                    "d2h_bytes_per_step": world * d2h // args.steps},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic,
                          "kernel": "gemm_pair_kernel / gemm_tc_kernel (tcgen05, all linear layers)",
