@@ -191,8 +191,8 @@ def reference_arm(args, rank, world):
     return 0
 
 
-# GEMM FLOPs per series of one forward (2·M·K·N over the model's linear layers; SURVEY-style accounting of the
-# configs: Chronos-2 config 2 with 128 context + [REG] + 4 future tokens, TiRex-2 config 4 with headwise gates)
+# GEMM FLOPs per series of one forward (2·M·K·N summed over the model's linear layers at the configs' shapes:
+# Chronos-2 config 2 with 128 context + [REG] + 4 future tokens, TiRex-2 config 4 with headwise gates)
 WORKLOAD_GEMM_FLOPS = {"config2": 30.82e9, "config4": 5.02e9}
 
 
