@@ -265,10 +265,11 @@ class ModelPrep:
         x = lay.window
         obs = ~np.isnan(x)
         n = obs.sum(axis=1)
-        s = np.where(obs, x.astype(np.float64), 0.0).sum(axis=1)
+        # sums in double in the reference's loop order (np.add.accumulate runs in order; np.sum pairs terms)
+        s = np.add.accumulate(np.where(obs, x.astype(np.float64), 0.0), axis=1)[:, -1]
         loc = np.where(n > 0, (s / np.maximum(n, 1)).astype(np.float32), np.float32(0))
         d = np.where(obs, (x - loc[:, None]).astype(np.float32), np.float32(0)).astype(np.float64)
-        sc = np.sqrt((d * d).sum(axis=1) / np.maximum(n, 1)).astype(np.float32)
+        sc = np.sqrt(np.add.accumulate(d * d, axis=1)[:, -1] / np.maximum(n, 1)).astype(np.float32)
         sc = np.where(sc == 0, np.float32(1e-5), sc)
         scale = np.where(n > 0, sc, np.float32(1)).astype(np.float32)
         loc = loc.astype(np.float32)

@@ -387,11 +387,13 @@ def causal_patch_loc_scale(x: np.ndarray, obs: np.ndarray, patch: int, min_scale
 def instance_norm(x: np.ndarray, obs: np.ndarray, min_scale: float) -> tuple[float, float, bool]:
     """Scaler.instanceNorm for one known-covariate row: (loc, scale, binary)."""
     n = max(float(obs.sum()), 1.0)
-    s = float(np.sum(x[obs].astype(np.float64)))
+    xo = x[obs].astype(np.float64)
+    s = float(np.add.accumulate(xo)[-1]) if xo.size else 0.0  # in the reference's loop order
     loc = np.float32(s / n)
-    d = np.where(obs, x - loc, np.float32(0)).astype(np.float32)
-    ss = float(np.sum(d.astype(np.float64) ** 2))
-    scale = max(np.float32(math.sqrt(np.float32(ss / n))), np.float32(min_scale))
+    d = np.where(obs, x - loc, np.float32(0)).astype(np.float64)
+    ss = float(np.add.accumulate(d * d)[-1]) if d.size else 0.0
+    with np.errstate(over="ignore"):  # a float overflow gives inf, as the reference's (float) cast does
+        scale = max(np.float32(math.sqrt(np.float32(ss / n))), np.float32(min_scale))
     zero_one = bool(np.all((x == 0) | (x == 1) | ~obs))
     if zero_one and obs.any():
         return np.float32(0), np.float32(1), True

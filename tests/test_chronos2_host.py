@@ -57,3 +57,16 @@ def test_finish_matches_oracle():
     lay = c2.ModelLayout.of(c, inp)
     prep = c2.ModelPrep.of(c, lay)
     np.testing.assert_allclose(prep.finish(c, lay, raw), out, rtol=1e-5, atol=1e-5)
+
+
+def test_instance_norm_sums_in_the_reference_order():
+    # ModelPrep.instanceNorm sums in double in its loop order: 1e20 absorbs every 1 that follows it (the
+    # reference's loc is 0), where a pairwise sum would keep some of them
+    c = tiny_config(context_length=16)
+    x = np.array([[1e20] + [1.0] * 14 + [-1e20]], np.float32)
+    lay = c2.ModelLayout.of(c, c2.ModelInput(x, np.zeros(1, np.int32), 1))
+    prep = c2.ModelPrep.of(c, lay)
+    s = 0.0
+    for v in x[0]:
+        s += float(v)
+    assert prep.loc[0] == np.float32(s / 16) == 0.0

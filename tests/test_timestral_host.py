@@ -125,3 +125,14 @@ def test_layout_errors():
     b = block(c, covariate_groups=0, length=250)
     with pytest.raises(ValueError, match="multiple of the patch size"):
         ts.BlockLayout.of(c, b)
+
+
+def test_instance_norm_sums_in_the_reference_order():
+    # Scaler.instanceNorm sums in double in its loop order: 1e20 absorbs every 1 that follows it, so the
+    # reference's loc is 0 here, where a pairwise sum would keep some of the ones
+    x = np.array([1e20] + [1.0] * 15 + [-1e20], np.float32)
+    s = 0.0
+    for v in x:
+        s += float(v)
+    loc, _, binary = ts.instance_norm(x, np.ones_like(x, bool), 1e-6)
+    assert not binary and loc == np.float32(s / len(x)) == 0.0
