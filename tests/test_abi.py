@@ -3,6 +3,7 @@ and rejects bad arguments with the reference's fail-fast statuses before touchin
 
 import ctypes
 import re
+import subprocess
 from pathlib import Path
 
 import numpy as np
@@ -94,3 +95,40 @@ def test_model_forwards_reject_a_null_engine(name):
 def test_device_forecasts_reject_a_null_engine(name):
     assert getattr(_lib.lib(), name)(None, 0, None, None, None) == _lib.ERR_INVALID_ARG
     assert "engine" in _lib.last_error()
+
+
+# every ctypes mirror of a header struct: (C struct, Python class) — sizes and field offsets must agree
+_STRUCTS = [("jc_tensor_view", "timestral._TensorView"), ("jc_timestral_desc", "timestral._Desc"),
+            ("jc_timestral_block", "timestral.Block"), ("jc_timestral_window", "timestral.Window"),
+            ("jc_chronos2_desc", "chronos2._Desc"), ("jc_chronos2_block", "chronos2.Block"),
+            ("jc_chronos2_window", "chronos2.Window"), ("jc_tirex2_desc", "tirex2._Desc"),
+            ("jc_tirex2_batch", "tirex2.Batch")]
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    # the C compiler's sizeof/offsetof for each struct of include/jitcast_b200.h against the Python mirrors
+    import importlib
+    import shutil
+
+    if not shutil.which("gcc"):
+        pytest.skip("no C compiler")
+    classes = {c: getattr(importlib.import_module(f"jitcast_b200.{p.split('.')[0]}"), p.split(".")[1])
+               for c, p in _STRUCTS}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "jitcast_b200.h"', "int main(void) {"]
+    for c, cls in classes.items():
+        lines.append(f'  printf("{c} size %zu\\n", sizeof({c}));')
+        for name, _ in cls._fields_:
+            lines.append(f'  printf("{c} {name} %zu\\n", offsetof({c}, {name}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layouts.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layouts"
+    inc = Path(__file__).resolve().parent.parent / "include"
+    r = subprocess.run(["gcc", "-std=c11", "-I", str(inc), str(src), "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = {tuple(l.split()[:2]): int(l.split()[2]) for l in out if l}
+    for c, cls in classes.items():
+        assert got[(c, "size")] == ctypes.sizeof(cls), c
+        for name, _ in cls._fields_:
+            assert got[(c, name)] == getattr(cls, name).offset, f"{c}.{name}"
