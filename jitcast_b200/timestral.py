@@ -321,11 +321,12 @@ class BlockLayout:
         valid = np.logical_or.accumulate(patch_obs, axis=1) if c.attend_missing_patches else patch_obs
         first_row = np.where(patch_obs.any(axis=1), patch_obs.argmax(axis=1), enc)
         group = np.asarray(b.group)
-        first = np.empty(r, np.int64)
-        for g in np.unique(group):
-            sel = group == g
-            f = first_row[sel].min()
-            first[sel] = 0 if f == enc else f
+        # each series' first observed patch over all its rows (0 for a series with none), in one pass
+        _, inv = np.unique(group, return_inverse=True)
+        gmin = np.full(int(inv.max()) + 1 if r else 0, enc, np.int64)
+        np.minimum.at(gmin, inv, first_row)
+        first = gmin[inv]
+        first[first == enc] = 0
         return BlockLayout(r, ps, ll, enc, h, cov, group, role, valid, first, window, obs)
 
     def group_ranges(self) -> tuple[np.ndarray, np.ndarray]:
