@@ -412,6 +412,18 @@ jc_status jc_forward_tirex2(jc_engine* engine, const jc_tirex2_batch* batch, flo
 jc_status jc_forward_tirex2_device(jc_engine* engine, int slot, const jc_tirex2_batch* batch, float* out,
                                    void* stream);
 
+/*
+ * BlockPrep.of's GPU half alone (timestral/BlockPrep.java:40-73, the kernels jc_forecast_timestral runs
+ * before its forward): on DEVICE buffers of `device`, window [rows · encoder · patch] FP32 and observed
+ * (0/1 bytes) as BlockLayout.window / observed, known [rows] as BlockLayout.known, write
+ * tokens_out [rows · encoder · 2·patch] as BlockPrep.tokens (each patch's scaled values, then its missing
+ * flags). For callers that build their own device inputs for jc_forward_timestral_device. Enqueued on
+ * `stream`; the call's scratch is stream-ordered memory freed on the same stream.
+ */
+jc_status jc_timestral_prep_device(int device, int rows, int encoder, int patch, const float* window,
+                                   const uint8_t* observed, const int32_t* known, float minimum_scale, int use_asinh,
+                                   float* tokens_out, void* stream);
+
 /* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
 jc_status jc_engine_sync(jc_engine* engine);
 

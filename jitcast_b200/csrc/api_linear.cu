@@ -201,6 +201,40 @@ jc_status jc_gemm_device(int device, jc_precision precision, const void* a_hi, c
   return JC_OK;
 }
 
+jc_status jc_timestral_prep_device(int device, int rows, int encoder, int patch, const float* window,
+                                   const uint8_t* observed, const int32_t* known, float minimum_scale, int use_asinh,
+                                   float* tokens_out, void* stream) {
+  clear_error();
+  if (rows < 1 || encoder < 1 || patch < 1) return fail(JC_ERR_INVALID_ARG, "rows, encoder and patch must be >= 1");
+  if (!window || !observed || !known || !tokens_out) return fail(JC_ERR_INVALID_ARG, "null pointer");
+  std::string why;
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TsEnds ep;
+  ep.rows = rows;
+  ep.enc = encoder;
+  ep.P = patch;
+  ep.ll = encoder;
+  ep.min_scale = minimum_scale;
+  ep.use_asinh = use_asinh ? 1 : 0;
+  // the per-patch frames and asinh flags live only for this call, in stream-ordered memory
+  void* scratch = nullptr;
+  const size_t frame_bytes = sizeof(float2) * static_cast<size_t>(rows) * encoder;
+  cudaError_t e = cudaMallocAsync(&scratch, frame_bytes + rows, s);
+  if (e != cudaSuccess) return fail(JC_ERR_OOM, std::string("scratch: ") + cudaGetErrorString(e));
+  float2* frame = static_cast<float2*>(scratch);
+  uint8_t* row_asinh = static_cast<uint8_t*>(scratch) + frame_bytes;
+  launch_ts_scaler(window, observed, known, ep, frame, row_asinh, s);
+  launch_ts_tokens(window, observed, frame, row_asinh, ep, tokens_out, s);
+  e = cudaGetLastError();
+  cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return fail_cuda(e, "prep launch");
+  return JC_OK;
+}
+
 jc_status jc_device_sync(int device) {
   clear_error();
   std::string why;

@@ -193,6 +193,36 @@ def test_host_ends_on_device_match_host_ends(jc, tiny, case, precision):
     assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
 
 
+@pytest.mark.parametrize("covariate_groups", [0, 2])
+def test_device_prep_tokens_match_the_oracle(jc, tiny, covariate_groups):
+    # jc_timestral_prep_device (the scaler and token kernels of jc_forecast_timestral) against the C restatement
+    # of BlockPrep.of (the reference's loop order, double statistics, -ffp-contract=off): equal bit for bit but
+    # where a double log (CUDA's against glibc's) lands within an ulp of a float rounding boundary
+    torch = pytest.importorskip("torch")
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    c, _, model = tiny
+    b = mixed_block(c, covariate_groups=covariate_groups)
+    ref = np.asarray(model.prepare(b)["tokens"], np.float32)
+    lay = ts.BlockLayout.of(c, b)
+    dev = torch.device("cuda", 0)
+    t = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a, dt)).to(dev)  # noqa: E731
+    win, obs, known = t(lay.window, np.float32), t(lay.observed, np.uint8), t(lay.known, np.int32)
+    tok = torch.empty(lay.rows * lay.encoder * 2 * c.patch_size, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    _lib.check(_lib.lib().jc_timestral_prep_device(0, lay.rows, lay.encoder, c.patch_size, win.data_ptr(),
+                                                   obs.data_ptr(), known.data_ptr(), float(np.float32(c.minimum_scale)),
+                                                   int(c.use_asinh), tok.data_ptr(),
+                                                   ctypes.c_void_p(stream.cuda_stream)))
+    torch.cuda.synchronize()
+    got = tok.cpu().numpy().reshape(ref.shape)
+    same = float(np.mean(got == ref))
+    assert same >= 0.9999, f"only {same:.4%} of the tokens equal the oracle's bit for bit"
+    np.testing.assert_allclose(got, ref, rtol=2.0 ** -22, atol=0)
+
+
 def test_host_ends_on_device_clamp_infinities(jc, tiny):
     # a head scaled so the raw outputs reach the hundreds: sinh overflows on about half the levels, so
     # Scaler.clampNonFinite maps infinities to the largest / smallest finite level of their step, or to 0 when a
