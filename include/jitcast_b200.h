@@ -424,6 +424,16 @@ jc_status jc_timestral_prep_device(int device, int rows, int encoder, int patch,
                                    const uint8_t* observed, const int32_t* known, float minimum_scale, int use_asinh,
                                    float* tokens_out, void* stream);
 
+/*
+ * ModelPrep.of's GPU half alone (chronos2/ModelPrep.java:29-70, the kernels jc_forecast_chronos2 runs before
+ * its encoder): on DEVICE buffers of `device`, window [rows · context_patches · patch] and future
+ * [rows · output_patches · patch] FP32 (NaN = missing) as ModelLayout.window / future, write
+ * tokens_out [rows · (context_patches + output_patches) · 3·patch] as ModelPrep.tokens. Enqueued on `stream`.
+ */
+jc_status jc_chronos2_prep_device(int device, int rows, int context_patches, int output_patches, int patch,
+                                  const float* window, const float* future, float time_encoding_scale,
+                                  int use_arcsinh, float* tokens_out, void* stream);
+
 /* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
 jc_status jc_engine_sync(jc_engine* engine);
 

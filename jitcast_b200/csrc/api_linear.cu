@@ -235,6 +235,39 @@ jc_status jc_timestral_prep_device(int device, int rows, int encoder, int patch,
   return JC_OK;
 }
 
+jc_status jc_chronos2_prep_device(int device, int rows, int context_patches, int output_patches, int patch,
+                                  const float* window, const float* future, float time_encoding_scale,
+                                  int use_arcsinh, float* tokens_out, void* stream) {
+  clear_error();
+  if (rows < 1 || context_patches < 1 || output_patches < 1 || patch < 1)
+    return fail(JC_ERR_INVALID_ARG, "rows, patch counts and patch must be >= 1");
+  if (!(time_encoding_scale > 0.0f)) return fail(JC_ERR_INVALID_ARG, "time encoding scale must be > 0");
+  if (!window || !future || !tokens_out) return fail(JC_ERR_INVALID_ARG, "null pointer");
+  std::string why;
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  C2Ends ep;
+  ep.rows = rows;
+  ep.nc = context_patches;
+  ep.h = output_patches;
+  ep.P = patch;
+  ep.use_arcsinh = use_arcsinh ? 1 : 0;
+  ep.time_scale = time_encoding_scale;
+  void* scratch = nullptr;  // the rows' (loc, scale), stream-ordered
+  cudaError_t e = cudaMallocAsync(&scratch, sizeof(float2) * static_cast<size_t>(rows), s);
+  if (e != cudaSuccess) return fail(JC_ERR_OOM, std::string("scratch: ") + cudaGetErrorString(e));
+  float2* norm = static_cast<float2*>(scratch);
+  launch_c2_norm(window, ep, norm, s);
+  launch_c2_tokens(window, future, norm, ep, tokens_out, s);
+  e = cudaGetLastError();
+  cudaFreeAsync(scratch, s);
+  if (e != cudaSuccess) return fail_cuda(e, "prep launch");
+  return JC_OK;
+}
+
 jc_status jc_device_sync(int device) {
   clear_error();
   std::string why;

@@ -112,6 +112,36 @@ def test_host_ends_on_device_match_host_ends(jc, tiny, case, precision):
     assert err < TOL[precision], f"{precision}: per-quantile rel max err {err:.3e}"
 
 
+@pytest.mark.parametrize("case", ["covariates", "degenerate"])
+def test_device_prep_tokens_match_the_oracle(jc, tiny, case):
+    # jc_chronos2_prep_device (the norm and token kernels of jc_forecast_chronos2) against the C restatement of
+    # ModelPrep.of (the reference's loop order, double sums): equal bit for bit but where a double log (CUDA's
+    # against glibc's) lands within an ulp of a float rounding boundary
+    torch = pytest.importorskip("torch")
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    c, _, model = tiny
+    inp = ends_input(c, case)
+    ref = np.asarray(model.prepare(inp)["tokens"], np.float32)
+    lay = c2.ModelLayout.of(c, inp)
+    dev = torch.device("cuda", 0)
+    win = torch.from_numpy(np.ascontiguousarray(lay.window, np.float32)).to(dev)
+    fut = torch.from_numpy(np.ascontiguousarray(lay.future, np.float32)).to(dev)
+    tok = torch.empty(ref.size, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    _lib.check(_lib.lib().jc_chronos2_prep_device(0, lay.rows, lay.context_patches, lay.output_patches, c.patch_size,
+                                                  win.data_ptr(), fut.data_ptr(),
+                                                  float(np.float32(c.time_encoding_scale)), int(c.use_arcsinh),
+                                                  tok.data_ptr(), ctypes.c_void_p(stream.cuda_stream)))
+    torch.cuda.synchronize()
+    got = tok.cpu().numpy().reshape(ref.shape)
+    same = float(np.mean(got == ref))
+    assert same >= 0.9999, f"only {same:.4%} of the tokens equal the oracle's bit for bit"
+    np.testing.assert_allclose(got, ref, rtol=2.0 ** -22, atol=0)
+
+
 def test_host_ends_device_entry_point_matches_host(jc, tiny):
     # jc_forecast_chronos2_device: window, future covariates and layout in HBM, quantiles written there
     torch = pytest.importorskip("torch")
