@@ -434,6 +434,25 @@ jc_status jc_chronos2_prep_device(int device, int rows, int context_patches, int
                                   const float* window, const float* future, float time_encoding_scale,
                                   int use_arcsinh, float* tokens_out, void* stream);
 
+/*
+ * BlockPrep.finish on the GPU alone (timestral/BlockPrep.java:81-101): in place on raw [rows · steps · Q]
+ * (steps = horizon · P, the head's raw outputs), Quantiles.apply with `quantile_scale` [Q] (Quantiles.scale(),
+ * a HOST array, Q <= 64) and `median`, then Scaler.invert with each row's (loc, scale) of its last context
+ * patch (loc_scale [rows · 2], device, 8-byte aligned) and Scaler.clampNonFinite. Enqueued on `stream`.
+ */
+jc_status jc_timestral_finish_device(int device, int rows, int steps, int quantiles, int median,
+                                     const float* quantile_scale, int use_asinh, const float* loc_scale, float* raw,
+                                     void* stream);
+
+/*
+ * ModelPrep.finish on the GPU alone (chronos2/ModelPrep.java:116-137): out [rows · Q · h·P] =
+ * sinh(raw)·scale + loc from raw [rows · h · Q · P] (each output token's quantiles level-major) and each
+ * row's (loc, scale) (loc_scale [rows · 2], device, 8-byte aligned). Enqueued on `stream`.
+ */
+jc_status jc_chronos2_finish_device(int device, int rows, int output_patches, int patch, int quantiles,
+                                    int use_arcsinh, const float* loc_scale, const float* raw, float* out,
+                                    void* stream);
+
 /* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
 jc_status jc_engine_sync(jc_engine* engine);
 

@@ -69,6 +69,8 @@ PROTOTYPES: dict[str, tuple] = {
                                          c_vp]),
     "jc_chronos2_prep_device": (c_int, [c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, ctypes.c_float, c_int, c_vp,
                                         c_vp]),
+    "jc_timestral_finish_device": (c_int, [c_int, c_int, c_int, c_int, c_int, c_vp, c_int, c_vp, c_vp, c_vp]),
+    "jc_chronos2_finish_device": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_vp]),
     "jc_time_attention_device": (c_int, [c_int, c_int, c_vp, c_ll, c_vp, c_ll, c_vp, c_ll, c_int, c_int, c_int, c_int,
                                          c_int, ctypes.c_float, c_int, c_int, c_int, c_vp, c_vp, c_vp, c_int, c_vp]),
 }

@@ -268,6 +268,59 @@ jc_status jc_chronos2_prep_device(int device, int rows, int context_patches, int
   return JC_OK;
 }
 
+jc_status jc_timestral_finish_device(int device, int rows, int steps, int quantiles, int median,
+                                     const float* quantile_scale, int use_asinh, const float* loc_scale, float* raw,
+                                     void* stream) {
+  clear_error();
+  if (rows < 1 || steps < 1 || quantiles < 1) return fail(JC_ERR_INVALID_ARG, "rows, steps and quantiles must be >= 1");
+  if (quantiles > kMaxQuantiles)
+    return fail(JC_ERR_UNSUPPORTED_SHAPE, "at most " + std::to_string(kMaxQuantiles) + " quantiles");
+  if (median < 0 || median >= quantiles) return fail(JC_ERR_INVALID_ARG, "median index out of range");
+  if (!quantile_scale || !loc_scale || !raw) return fail(JC_ERR_INVALID_ARG, "null pointer");
+  if (reinterpret_cast<uintptr_t>(loc_scale) % 8 != 0) return fail(JC_ERR_INVALID_ARG, "loc_scale not 8-byte aligned");
+  std::string why;
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  TsEnds ep;
+  ep.rows = rows;
+  ep.enc = 1;  // one frame per row: the last context patch's
+  ep.ll = 1;
+  ep.Q = quantiles;
+  ep.median = median;
+  ep.use_asinh = use_asinh ? 1 : 0;
+  for (int i = 0; i < quantiles; ++i) ep.qscale[i] = quantile_scale[i];
+  launch_ts_finish(raw, reinterpret_cast<const float2*>(loc_scale), ep, steps, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? JC_OK : fail_cuda(e, "finish launch");
+}
+
+jc_status jc_chronos2_finish_device(int device, int rows, int output_patches, int patch, int quantiles,
+                                    int use_arcsinh, const float* loc_scale, const float* raw, float* out,
+                                    void* stream) {
+  clear_error();
+  if (rows < 1 || output_patches < 1 || patch < 1 || quantiles < 1)
+    return fail(JC_ERR_INVALID_ARG, "rows, output patches, patch and quantiles must be >= 1");
+  if (!loc_scale || !raw || !out) return fail(JC_ERR_INVALID_ARG, "null pointer");
+  if (reinterpret_cast<uintptr_t>(loc_scale) % 8 != 0) return fail(JC_ERR_INVALID_ARG, "loc_scale not 8-byte aligned");
+  std::string why;
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  C2Ends ep;
+  ep.rows = rows;
+  ep.nc = 1;
+  ep.h = output_patches;
+  ep.P = patch;
+  ep.Q = quantiles;
+  ep.use_arcsinh = use_arcsinh ? 1 : 0;
+  launch_c2_finish(raw, reinterpret_cast<const float2*>(loc_scale), ep, out, static_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? JC_OK : fail_cuda(e, "finish launch");
+}
+
 jc_status jc_device_sync(int device) {
   clear_error();
   std::string why;

@@ -142,6 +142,34 @@ def test_device_prep_tokens_match_the_oracle(jc, tiny, case):
     np.testing.assert_allclose(got, ref, rtol=2.0 ** -22, atol=0)
 
 
+@pytest.mark.parametrize("case", ["covariates", "degenerate"])
+def test_device_finish_matches_the_oracle(jc, tiny, case):
+    # jc_chronos2_finish_device on the oracle's raw output patch embedding against its ModelPrep.finish
+    torch = pytest.importorskip("torch")
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    c, _, model = tiny
+    inp = ends_input(c, case)
+    out, raw = model.forward(inp)
+    prep = model.prepare(inp)
+    ls = np.stack([prep["loc"], prep["scale"]], axis=1).astype(np.float32)
+    dev = torch.device("cuda", 0)
+    r = torch.from_numpy(np.ascontiguousarray(raw, np.float32)).to(dev)
+    lsd = torch.from_numpy(np.ascontiguousarray(ls)).to(dev)
+    got_t = torch.empty(out.size, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    _lib.check(_lib.lib().jc_chronos2_finish_device(0, out.shape[0], inp.output_patches, c.patch_size,
+                                                    c.num_quantiles, int(c.use_arcsinh), lsd.data_ptr(), r.data_ptr(),
+                                                    got_t.data_ptr(), ctypes.c_void_p(stream.cuda_stream)))
+    torch.cuda.synchronize()
+    got = got_t.cpu().numpy().reshape(out.shape)
+    same = float(np.mean(got == out))
+    assert same >= 0.9999, f"only {same:.4%} of the quantiles equal the oracle's bit for bit"
+    np.testing.assert_allclose(got, out, rtol=1e-6, atol=1e-6 * float(np.abs(out).max()))
+
+
 def test_host_ends_device_entry_point_matches_host(jc, tiny):
     # jc_forecast_chronos2_device: window, future covariates and layout in HBM, quantiles written there
     torch = pytest.importorskip("torch")

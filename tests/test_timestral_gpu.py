@@ -223,6 +223,36 @@ def test_device_prep_tokens_match_the_oracle(jc, tiny, covariate_groups):
     np.testing.assert_allclose(got, ref, rtol=2.0 ** -22, atol=0)
 
 
+@pytest.mark.parametrize("covariate_groups", [0, 2])
+def test_device_finish_matches_the_oracle(jc, tiny, covariate_groups):
+    # jc_timestral_finish_device on the oracle's own raw head outputs against its BlockPrep.finish (the C
+    # restatement: Quantiles.apply, Scaler.invert, Scaler.clampNonFinite in the reference's operation order)
+    torch = pytest.importorskip("torch")
+    import ctypes
+
+    from jitcast_b200 import _lib
+
+    c, _, model = tiny
+    b = mixed_block(c, covariate_groups=covariate_groups)
+    out, raw = model.predict_block(b)
+    prep = model.prepare(b)
+    anchor = (prep["ll"] - 1) * c.patch_size
+    ls = np.stack([prep["loc"][:, anchor], prep["scale"][:, anchor]], axis=1).astype(np.float32)
+    dev = torch.device("cuda", 0)
+    r = torch.from_numpy(np.ascontiguousarray(raw, np.float32)).to(dev)
+    lsd = torch.from_numpy(np.ascontiguousarray(ls)).to(dev)
+    qs = np.ascontiguousarray(ts.quantile_scale(c), np.float32)
+    stream = torch.cuda.current_stream(dev)
+    _lib.check(_lib.lib().jc_timestral_finish_device(0, out.shape[0], out.shape[1], c.num_quantiles, c.median_index,
+                                                     qs.ctypes.data, int(c.use_asinh), lsd.data_ptr(), r.data_ptr(),
+                                                     ctypes.c_void_p(stream.cuda_stream)))
+    torch.cuda.synchronize()
+    got = r.cpu().numpy().reshape(out.shape)
+    same = float(np.mean(got == out))
+    assert same >= 0.9999, f"only {same:.4%} of the quantiles equal the oracle's bit for bit"
+    np.testing.assert_allclose(got, out, rtol=1e-6, atol=1e-6 * float(np.abs(out).max()))
+
+
 def test_host_ends_on_device_clamp_infinities(jc, tiny):
     # a head scaled so the raw outputs reach the hundreds: sinh overflows on about half the levels, so
     # Scaler.clampNonFinite maps infinities to the largest / smallest finite level of their step, or to 0 when a
