@@ -453,6 +453,14 @@ jc_status jc_chronos2_finish_device(int device, int rows, int output_patches, in
                                     int use_arcsinh, const float* loc_scale, const float* raw, float* out,
                                     void* stream);
 
+/*
+ * Self-test of the bounded waits every kernel of the library uses (no counterpart in the reference): one
+ * thread waits `limit_us` microseconds (1 .. 1,000,000), with the same mbarrier wait, for a barrier phase
+ * that nothing completes, gives up, records it in the device's error word and returns. The call then reports
+ * it as jc_device_sync would — JC_ERR_TIMEOUT, the error word cleared — and the device stays usable.
+ */
+jc_status jc_device_wait_selftest(int device, int limit_us);
+
 /* Waits for every GPU of the engine; JC_ERR_TIMEOUT if a kernel's bounded wait gave up. */
 jc_status jc_engine_sync(jc_engine* engine);
 

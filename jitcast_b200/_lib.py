@@ -64,6 +64,7 @@ PROTOTYPES: dict[str, tuple] = {
     "jc_gemm_device": (c_int, [c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_int, c_int,
                                c_int, c_int, c_vp]),
     "jc_device_sync": (c_int, [c_int]),
+    "jc_device_wait_selftest": (c_int, [c_int, c_int]),
     "jc_shard_rows": (c_int, [c_int, c_vp, c_vp, c_int, c_vp]),
     "jc_timestral_prep_device": (c_int, [c_int, c_int, c_int, c_int, c_vp, c_vp, c_vp, ctypes.c_float, c_int, c_vp,
                                          c_vp]),

@@ -6,7 +6,22 @@
 
 #include "gemm.h"
 #include "kernels.cuh"
+#include "ptx.cuh"
 #include "runtime.h"
+
+namespace {
+
+// One thread waits, with the library's bounded mbarrier wait, for a phase that nothing completes.
+__global__ void wait_selftest_kernel(uint32_t* err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    jc::mbar_init(&bar, 1);
+    jc::fence_mbar_init();
+    if (!jc::mbar_wait(&bar, 0, limit_ns)) atomicOr(err, jc::kErrTimeoutFlag);
+  }
+}
+
+}  // namespace
 
 using namespace jc;
 
@@ -319,6 +334,21 @@ jc_status jc_chronos2_finish_device(int device, int rows, int output_patches, in
   launch_c2_finish(raw, reinterpret_cast<const float2*>(loc_scale), ep, out, static_cast<cudaStream_t>(stream));
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? JC_OK : fail_cuda(e, "finish launch");
+}
+
+jc_status jc_device_wait_selftest(int device, int limit_us) {
+  clear_error();
+  if (limit_us < 1 || limit_us > 1000000) return fail(JC_ERR_INVALID_ARG, "limit_us must be in [1, 1000000]");
+  std::string why;
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  wait_selftest_kernel<<<1, 32, 0, rt->stream>>>(rt->err, static_cast<uint64_t>(limit_us) * 1000ull);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(rt->stream);
+  if (e != cudaSuccess) return fail_cuda(e, "wait self-test");
+  return take_device_error(rt);
 }
 
 jc_status jc_device_sync(int device) {

@@ -132,3 +132,10 @@ def test_struct_layouts_match_the_header(tmp_path):
         assert got[(c, "size")] == ctypes.sizeof(cls), c
         for name, _ in cls._fields_:
             assert got[(c, name)] == getattr(cls, name).offset, f"{c}.{name}"
+
+
+def test_wait_selftest_arguments():
+    assert _lib.lib().jc_device_wait_selftest(0, 0) == _lib.ERR_INVALID_ARG
+    assert _lib.lib().jc_device_wait_selftest(0, 2_000_000) == _lib.ERR_INVALID_ARG
+    if _lib.lib().jc_device_count() == 0:
+        assert _lib.lib().jc_device_wait_selftest(0, 1000) == _lib.ERR_NO_DEVICE
