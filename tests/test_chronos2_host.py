@@ -48,6 +48,8 @@ def test_host_prep_matches_oracle(reg, covariate_groups, length):
     np.testing.assert_allclose(prep.loc, ref["loc"], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(prep.scale, ref["scale"], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(prep.tokens, ref["tokens"], rtol=1e-5, atol=1e-6)
+    for k in ("tokens", "loc", "scale"):  # bit for bit but at a rounding boundary of a double log
+        assert np.mean(getattr(prep, k) == ref[k]) >= 0.9999, k
 
 
 def test_finish_matches_oracle():

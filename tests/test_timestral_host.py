@@ -68,6 +68,10 @@ def test_host_prep_matches_oracle(covariate_groups):
     np.testing.assert_allclose(prep.loc, ref["loc"], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(prep.scale, ref["scale"], rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(prep.tokens, ref["tokens"], rtol=1e-5, atol=1e-6)
+    # the same operations in the same order: bit for bit but where NumPy's and the C library's double log differ
+    # across a float rounding boundary
+    for k in ("tokens", "loc", "scale"):
+        assert np.mean(getattr(prep, k) == ref[k]) >= 0.9999, k
 
 
 def test_host_finish_matches_oracle():
