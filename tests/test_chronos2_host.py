@@ -58,7 +58,9 @@ def test_finish_matches_oracle():
     out, raw = oc2.Model(c, c2.random_checkpoint(c)).forward(inp, nthreads=4)
     lay = c2.ModelLayout.of(c, inp)
     prep = c2.ModelPrep.of(c, lay)
-    np.testing.assert_allclose(prep.finish(c, lay, raw), out, rtol=1e-5, atol=1e-5)
+    mine = prep.finish(c, lay, raw)
+    np.testing.assert_allclose(mine, out, rtol=1e-5, atol=1e-5)
+    assert np.mean(mine == out) >= 0.9999  # bit for bit but at a rounding boundary of a double sinh
 
 
 def test_instance_norm_sums_in_the_reference_order():

@@ -83,6 +83,7 @@ def test_host_finish_matches_oracle():
     prep = ts.BlockPrep.of(c, lay)
     mine = prep.finish(c, lay, raw.copy())
     np.testing.assert_allclose(mine, out, rtol=1e-5, atol=1e-5)
+    assert np.mean(mine == out) >= 0.9999  # bit for bit but at a rounding boundary of a double transcendental
 
 
 def test_bucket_sizes():
