@@ -367,13 +367,11 @@ def main():
     if args.workload != "config5":
         return workload_bench(args, world)
 
-    import ctypes
     import datetime
 
     import torch
     import torch.distributed as dist
 
-    from jitcast_b200 import _lib
     from jitcast_b200 import timestral as ts
     from jitcast_b200 import workloads
 
@@ -390,7 +388,7 @@ def main():
     per_rank = args.series // world
     chunks = []
     win_in = []  # each chunk's window and layout (host arrays), for the end-to-end forecast
-    lay_fields = ("positions", "key_valid", "known", "role", "group_start", "group_end")
+    lay_fields = ts.DeviceWindow.FIELDS
     for c0, n in rank_chunks(args.series, args.chunk, world, rank):
         x = workloads.sinusoid_noise(n, 4096, seed=c0)  # chunk-seeded: the same series for every N
         b = ts.BlockInput(x, np.ones_like(x, bool), np.arange(n, dtype=np.int32), 2)
@@ -398,23 +396,15 @@ def main():
         win_in.append(wi)
         # resident in HBM: the window, its observed flags and the layout; the GPU runs BlockPrep.of, the forward
         # and BlockPrep.finish (jc_forecast_timestral_device)
-        d = {k: torch.from_numpy(np.ascontiguousarray(getattr(wi.layout, k))).to(dev) for k in lay_fields}
-        d["window"], d["observed"] = torch.from_numpy(wi.window).to(dev), torch.from_numpy(wi.observed).to(dev)
-        out = torch.empty(n, 2 * cfg.patch_size, cfg.num_quantiles, device=dev)
-        L0 = wi.layout
-        blk = ts.Block(L0.rows, L0.encoder, L0.horizon, L0.context_patches, L0.covariates, None,
-                       *(d[k].data_ptr() for k in lay_fields))
-        win = ts.Window(blk, d["window"].data_ptr(), d["observed"].data_ptr(), wi.minimum_scale, wi.use_asinh,
-                        wi.median, wi.quantile_scale.ctypes.data)
-        chunks.append((wi, d, out, win, n))
-    L = _lib.lib()
+        dw = ts.DeviceWindow(wi, dev)
+        out = torch.empty(dw.out_shape(cfg), device=dev)
+        chunks.append((wi, dw, out, n))
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
 
     def device_step():
-        for _, _, out, win, _ in chunks:
-            _lib.check(L.jc_forecast_timestral_device(engine.handle, 0, ctypes.byref(win), out.data_ptr(),
-                                                      stream.cuda_stream))
+        for _, dw, out, _ in chunks:
+            dw.forecast(engine, out, stream)
 
     def barrier():
         if world > 1:
@@ -447,7 +437,7 @@ def main():
     # finished quantiles back into pinned host buffers, copies timed (the layout itself is built before)
     fields = lay_fields
     host_chunks = []
-    for wi, (_, _, _, _, n) in zip(win_in, chunks):
+    for wi, (_, _, _, n) in zip(win_in, chunks):
         lp = dataclasses.replace(wi.layout, **{k: pinned(getattr(wi.layout, k)) for k in fields})
         hp = dataclasses.replace(wi, layout=lp, window=pinned(wi.window), observed=pinned(wi.observed))
         qp = pinned_empty((n, 2 * cfg.patch_size, cfg.num_quantiles))
@@ -468,9 +458,8 @@ def main():
 
     # kernel-class timings of one profiled forecast (eager, CUDA events around every launch)
     engine.set_option("profile", 1)
-    _, _, out0, win0, _ = chunks[0]
-    _lib.check(L.jc_forecast_timestral_device(engine.handle, 0, ctypes.byref(win0), out0.data_ptr(),
-                                              stream.cuda_stream))
+    _, dw0, out0, _ = chunks[0]
+    dw0.forecast(engine, out0, stream)
     torch.cuda.synchronize()
     prof = engine.profile()
     engine.set_option("profile", 0)

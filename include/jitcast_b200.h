@@ -113,10 +113,15 @@ jc_status jc_linear_device(int device, jc_precision precision, const float* a, l
  *   - (m + n) x round_up(k, 64) operands must fit: 2 bytes per element for JC_BF16 and JC_FP16, 4
  *     for JC_TF32, 8 for JC_FP32 (hi and lo). Larger shapes fail with JC_ERR_UNSUPPORTED_SHAPE.
  *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with
- *     that device current; make that first call before any stream capture.
- *   - Every call shares the one array and it keeps the last call's contents; the operands are fully
- *     rewritten by each call. Calls that overlapped on the GPU would race on it, so calls are
- *     serialised and each one waits for its own kernels on `stream` before it returns.
+ *     that device current. Under CUDA's lazy module loading (the default since CUDA 12.2) that first
+ *     use of the library on a device is also what loads its module there and reserves the 16 MiB.
+ *     So make one call on each device at start-up: before any stream capture, and before the caller
+ *     sizes its arena from the free memory.
+ *   - Calls on one device are serialised (they share that device's array); calls on different
+ *     devices run side by side.
+ *   - Every call on a device shares that device's array and it keeps the last call's contents; the
+ *     operands are fully rewritten by each call. Calls that overlapped on the GPU would race on it,
+ *     so each call waits for its own kernels on `stream` before it returns.
  *   - Returns JC_ERR_TIMEOUT if a bounded wait inside the GEMM gave up.
  */
 jc_status jc_linear_device_noalloc(int device, jc_precision precision, const float* a, long long lda, const float* w,

@@ -6,7 +6,9 @@
 // The operand conversions that jc_linear_device writes into grown-on-demand library scratch go
 // instead into one fixed array in the library's own device image (kNoAllocScratchBytes per GPU,
 // present on every GPU that loads the library, until the process exits). Nothing here calls
-// cudaMalloc, cudaFree or a library routine that allocates.
+// cudaMalloc, cudaFree or a library routine that allocates. Under CUDA's lazy module loading (the
+// default since CUDA 12.2) the array is reserved on a device when the library's module is first
+// loaded there, which the first call on that device does (or any earlier call of the library on it).
 #include <mutex>
 #include <string>
 
@@ -25,12 +27,14 @@ static __device__ __align__(16) uint32_t g_noalloc_err[4];
 
 // Device addresses of the two symbols, looked up once per device with that device current. In
 // host code the symbols' names are host-side stand-ins, not device addresses.
+// One lock per device: calls on one device share that device's copy of the array and are serialised;
+// calls on different devices use different copies and run side by side.
 struct Addresses {
+  std::mutex mu;
   bool ready = false;
   unsigned char* scratch = nullptr;
   uint32_t* err = nullptr;
 };
-std::mutex g_mu;
 Addresses g_addr[64];
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -61,6 +65,12 @@ extern "C" jc_status jc_linear_device_noalloc(int device, jc_precision precision
                                         : kOpSplit;
   const long long kp = round_up(k, 64);
   const size_t esz = (op == kOpBF16 || op == kOpF16) ? 2 : 4;
+  // refuse before multiplying: m · kp · esz could wrap size_t when m and k are both near INT_MAX
+  if (static_cast<size_t>(kp) > kNoAllocScratchBytes / esz / static_cast<size_t>(m > n ? m : n))
+    return fail(JC_ERR_UNSUPPORTED_SHAPE,
+                "jc_linear_device_noalloc: the operands of a " + std::to_string(m) + " x " + std::to_string(n) +
+                    " x " + std::to_string(k) + " GEMM do not fit the fixed scratch of " +
+                    std::to_string(kNoAllocScratchBytes) + " bytes");
   const size_t a_part = align256(static_cast<size_t>(m) * kp * esz);
   const size_t w_part = align256(static_cast<size_t>(n) * kp * esz);
   const size_t parts = op == kOpSplit ? 2 : 1;
@@ -77,10 +87,10 @@ extern "C" jc_status jc_linear_device_noalloc(int device, jc_precision precision
   }
   if (device < 0 || device >= count || device >= 64) return fail(JC_ERR_NO_DEVICE, "device out of range");
 
-  std::lock_guard<std::mutex> lk(g_mu);
+  Addresses& ad = g_addr[device];
+  std::lock_guard<std::mutex> lk(ad.mu);
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return fail_cuda(e, "cudaSetDevice");
-  Addresses& ad = g_addr[device];
   if (!ad.ready) {
     // first call on this device: resolve the symbols' device addresses (make this first call
     // before any stream capture that would include the entry point)
@@ -99,12 +109,6 @@ extern "C" jc_status jc_linear_device_noalloc(int device, jc_precision precision
   void* w_hi = base + a_part;
   void* a_lo = op == kOpSplit ? base + a_part + w_part : nullptr;
   void* w_lo = op == kOpSplit ? base + 2 * a_part + w_part : nullptr;
-  // the conversions write every element of the padded operands (zeros past k), so nothing left in
-  // the shared scratch by an earlier call is read
-  launch_convert(op, a, lda, a_hi, a_lo, kp, m, k, s);
-  launch_convert(op, w, ldw, w_hi, w_lo, kp, n, k, s);
-  e = cudaMemsetAsync(ad.err, 0, sizeof(uint32_t), s);
-  if (e != cudaSuccess) return fail_cuda(e, "clearing the error word");
 
   GemmArgs g{};
   g.op = op;
@@ -126,7 +130,17 @@ extern "C" jc_status jc_linear_device_noalloc(int device, jc_precision precision
   g.ep.ldc = ldc;
   g.ep.cin = c;
   g.ep.ldcin = ldc;
+  // every check comes before the first launch, so a refused call leaves the stream untouched
   if (const char* msg = check_gemm(g)) return fail(JC_ERR_UNSUPPORTED_SHAPE, msg);
+
+  // the conversions write every element of the padded operands (zeros past k), so nothing left in
+  // the shared scratch by an earlier call is read
+  launch_convert(op, a, lda, a_hi, a_lo, kp, m, k, s);
+  launch_convert(op, w, ldw, w_hi, w_lo, kp, n, k, s);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail_cuda(e, "operand conversion launch");
+  e = cudaMemsetAsync(ad.err, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return fail_cuda(e, "clearing the error word");
   e = launch_gemm(g, s, ad.err);
   if (e != cudaSuccess) return fail_cuda(e, "GEMM launch");
   // the scratch is reused by the next call, so the call completes before returning; the word

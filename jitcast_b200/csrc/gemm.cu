@@ -37,12 +37,19 @@ struct Cfg {
   static constexpr int STAGE_BYTES = NOP * (A_BYTES + B_BYTES);
   static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int TMEM_COLS = 2 * BN;
+  // The split FP32 mode drains every stage's partial product (K = 32) out of TMEM and sums the partials in
+  // FP32 with round-to-nearest (a "slab" accumulation): NACC rotating partial buffers plus one sum buffer.
+  // The tensor cores' own accumulation truncates, and over a long K that bias grows with the number of
+  // accumulate steps; drained per stage it is bounded by 16 steps.
+  static constexpr bool SLAB = OPK == kOpSplit;
+  static constexpr int NACC = SLAB ? 3 : 2;
+  static constexpr int TMEM_COLS = SLAB ? 4 * BN : 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
   static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : OPK == kOpF16 ? 0u : 2u, BM, BN);
   static_assert(STAGES >= 2, "too few stages");
   static_assert(TMEM_COLS >= 32 && TMEM_COLS <= 512, "TMEM columns");
+  static_assert(!SLAB || BN <= 128, "the split mode's slab buffers need BN <= 128");
 };
 
 constexpr int kEpiWarps = 8;                    // two warps per TMEM lane quarter, splitting the columns
@@ -414,6 +421,40 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
   if (p.rowsq && live) atomicAdd(p.rowsq + orow, sq);
 }
 
+// Which epilogue warp half (0 or 1) of a TMEM lane quarter reads the tile's 32-column chunk `c` in
+// epilogue_tile: 64-column units alternate between the halves, or, for the q|k|v columns of the RoPE mode,
+// whole heads do.
+__device__ __forceinline__ int chunk_owner(const EpiParams& p, int n0, int c) {
+  if (p.mode == kEpiQKV && n0 < p.n_split) return ((32 * c) / p.head_dim) & 1;
+  return (c >> 1) & 1;
+}
+
+// The split mode's drain of one stage's partial product: for every chunk this thread's epilogue will read,
+// sum += partial (FP32, round-to-nearest), or sum = partial for the tile's first stage. The sum buffer stays
+// with this thread from the first stage to the epilogue, so only its own tcgen05.ld/st order it.
+template <int BN>
+__device__ __forceinline__ void drain_partial(const EpiParams& p, int N, int n0, int half, uint32_t part,
+                                              uint32_t sum, bool first) {
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    if (n0 + 32 * c >= N) break;  // warp-uniform
+    if (chunk_owner(p, n0, c) != half) continue;
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(part + 32 * c, r);
+    if (!first) {
+      uint32_t q[32];
+      tmem_ld_32x32b_x32(sum + 32 * c, q);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(q[j])));
+    } else {
+      tmem_ld_wait();
+    }
+    tmem_st_32x32b_x32(sum + 32 * c, r);
+  }
+  tmem_st_wait();
+}
+
 // ---- the kernel -----------------------------------------------------------------------------
 template <int BN, int OPK>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -426,8 +467,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + C::NACC;
+  uint64_t* drain = acc_empty + C::NACC;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -441,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::NACC; ++b) {
       mbar_init(acc_full + b, 1);
       mbar_init(acc_empty + b, 32 * kEpiWarps);
     }
@@ -517,19 +558,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
+      int slab = 0;  // split mode: stages issued so far, each into partial buffer slab % NACC
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
         const int buf = it & 1;
         const uint32_t aph = (it >> 1) & 1;
-        if (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag) {
+        if (!C::SLAB && (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag)) {
           atomicOr(err, kErrTimeoutAccFree);
           *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
+        uint32_t d = tmem + buf * BN;
         for (int kb = 0; kb < kblks; ++kb) {
+          if (C::SLAB) {
+            const int pb = slab % C::NACC;
+            if (!mbar_wait(acc_empty + pb, ((slab / C::NACC) & 1) ^ 1) || *abort_flag) {
+              atomicOr(err, kErrTimeoutAccFree);
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d = tmem + pb * BN;
+          }
           if (!mbar_wait(full + stage, phase) || *abort_flag) {
             atomicOr(err, kErrTimeoutFull);
             *abort_flag = 1;
@@ -543,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < C::NSUB; ++k) {
             const uint64_t ad = sdesc_k_sw128(sa + 32 * k);
             const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t acc = ((kb > 0 && !C::SLAB) || k > 0) ? 1u : 0u;
             if (OPK == kOpBF16 || OPK == kOpF16) {
               umma_bf16(d, ad, bd, C::IDESC, acc);
             } else if (OPK == kOpTF32) {
@@ -559,17 +612,46 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           umma_commit(empty + stage);
+          if (C::SLAB) umma_commit(acc_full + (slab++ % C::NACC));
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(acc_full + buf);
+        if (!C::SLAB) umma_commit(acc_full + buf);
       }
       // every MMA this thread issued has completed once `drain` flips
       umma_commit(drain);
       mbar_wait(drain, 0);
+    }
+  } else if (C::SLAB) {
+    // ---- split-mode epilogue: drain each stage's partial into the sum buffer, then the tile's epilogue ----
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t lanes = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t sum = tmem + lanes + C::NACC * BN;
+    int slab = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
+      for (int kb = 0; kb < kblks; ++kb, ++slab) {
+        const int pb = slab % C::NACC;
+        const bool got = mbar_wait(acc_full + pb, (slab / C::NACC) & 1);
+        if (!(__all_sync(0xffffffffu, got) && !*abort_flag)) {
+          if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        drain_partial<BN>(ep, N, n0, half, tmem + lanes + pb * BN, sum, kb == 0);
+        tc_fence_before();
+        mbar_arrive(acc_empty + pb);
+      }
+      if (!ok) break;
+      epilogue_tile<BN>(ep, M, N, m0, n0, sum, row_in_tile, half);
     }
   } else {
     // ---- epilogue: warps 2..9; TMEM lane quarter = warp % 4, column half = (warp - 2) / 4 ----
@@ -1030,7 +1112,12 @@ cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err)
       }
     }
   }
-  const int bn = choose_bn(g, sms);
+  int bn = choose_bn(g, sms);
+  if (g.op == kOpSplit && bn > 128) {  // the split mode's slab buffers: 4 · BN TMEM columns
+    const int allowed = g.ep.mode == kEpiQKV ? qkv_tile_choices(g.ep) : 7;
+    bn = (allowed & 2) ? 128 : (allowed & 1) ? 64 : 0;
+    if (!bn) return cudaErrorInvalidValue;
+  }
 #define JC_LAUNCH(BN_)                                                  \
   switch (g.op) {                                                       \
     case kOpBF16: return launch_cfg<BN_, kOpBF16>(g, stream, err, sms); \
@@ -1039,7 +1126,11 @@ cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err)
     default: return launch_cfg<BN_, kOpSplit>(g, stream, err, sms);     \
   }
   if (bn == 256) {
-    JC_LAUNCH(256)
+    switch (g.op) {
+      case kOpBF16: return launch_cfg<256, kOpBF16>(g, stream, err, sms);
+      case kOpTF32: return launch_cfg<256, kOpTF32>(g, stream, err, sms);
+      default: return launch_cfg<256, kOpF16>(g, stream, err, sms);
+    }
   } else if (bn == 128) {
     JC_LAUNCH(128)
   } else {

@@ -586,6 +586,36 @@ class WindowInputs:
                       self.use_asinh, self.median, self.quantile_scale.ctypes.data)
 
 
+class DeviceWindow:
+    """A block's window inputs resident in one GPU's memory (torch tensors), with the ``jc_timestral_window`` that
+    points at them: what ``jc_forecast_timestral_device`` reads, for a caller whose inputs are already in HBM."""
+
+    FIELDS = ("positions", "key_valid", "known", "role", "group_start", "group_end")
+
+    def __init__(self, wi: WindowInputs, device):
+        import torch
+
+        up = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
+        lay = wi.layout
+        self.inputs = wi  # keeps quantile_scale (a host array the call reads) alive
+        self.tensors = {k: up(getattr(lay, k)) for k in self.FIELDS}
+        self.tensors["window"], self.tensors["observed"] = up(wi.window), up(wi.observed)
+        blk = Block(lay.rows, lay.encoder, lay.horizon, lay.context_patches, lay.covariates, None,
+                    *(self.tensors[k].data_ptr() for k in self.FIELDS))
+        self.struct = Window(blk, self.tensors["window"].data_ptr(), self.tensors["observed"].data_ptr(),
+                             wi.minimum_scale, wi.use_asinh, wi.median, wi.quantile_scale.ctypes.data)
+
+    def out_shape(self, c: TimestralConfig) -> tuple[int, int, int]:
+        lay = self.inputs.layout
+        return (lay.rows, lay.horizon * c.patch_size, c.num_quantiles)
+
+    def forecast(self, engine: "TimestralEngine", out, stream, slot: int = 0) -> None:
+        """Enqueues ``jc_forecast_timestral_device`` on ``stream`` (a torch stream) into ``out`` (a float32 CUDA
+        tensor of ``out_shape``)."""
+        check(_lib.lib().jc_forecast_timestral_device(engine.handle, slot, ctypes.byref(self.struct), out.data_ptr(),
+                                                      c_vp(stream.cuda_stream)))
+
+
 class TimestralEngine:
     """A Timestral model resident on one or more GPUs (``jc_engine_create_timestral``)."""
 

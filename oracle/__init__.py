@@ -10,6 +10,7 @@ this package, and only as the checker. The product path (``jitcast_b200``) never
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 import os
@@ -36,6 +37,10 @@ def lib() -> ctypes.CDLL:
         _lib.jco_rmsnorm.argtypes = [_F, ctypes.c_int, ctypes.c_int, _F, ctypes.c_float, _F]
         _lib.jco_gemm.argtypes = [_F, _F, _F, _F, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                   ctypes.c_int]
+        _lib.jco_set_operand_format.argtypes = [ctypes.c_int]
+        _lib.jco_operand_format.restype = ctypes.c_int
+        _lib.jco_round_operand.argtypes = [ctypes.c_float, ctypes.c_int]
+        _lib.jco_round_operand.restype = ctypes.c_float
         _lib.jco_silu.argtypes = [ctypes.c_float]
         _lib.jco_silu.restype = ctypes.c_float
         for name, fn in _extra_bindings():
@@ -67,6 +72,23 @@ def fptr(a: np.ndarray | None):
         return None
     assert a.dtype == np.float32 and a.flags.c_contiguous
     return a.ctypes.data_as(_F)
+
+
+# jco_set_operand_format codes: a reduced-precision run of the reference arithmetic
+OPERAND_FORMATS = {"fp32": 0, "tf32": 1, "bf16": 2, "fp16": 3}
+
+
+@contextlib.contextmanager
+def operand_format(name: str):
+    """Within the block every oracle GEMM (``Ops.linear``) rounds its operands to ``name`` ("tf32", "bf16",
+    "fp16"; "fp32" = the reference's arithmetic) before its double accumulation: the reduced-precision run of
+    the reference arithmetic that the reference holds its reduced-precision device paths to
+    (tirex2/tornado/TornadoForwardAccelTest.java:39-44, GoldenData.nxaiGpuError)."""
+    lib().jco_set_operand_format(OPERAND_FORMATS[name])
+    try:
+        yield
+    finally:
+        lib().jco_set_operand_format(0)
 
 
 def threads() -> int:

@@ -17,16 +17,71 @@
  *
  * linear runs row chunks of 16 (Ops.java:31 PARALLEL_ROWS) on a pthread pool; the result does
  * not depend on the thread count.
+ *
+ * jco_set_operand_format selects a reduced-precision run of the same arithmetic: every linear
+ * rounds its x and w elements (to nearest even) to TF32, BF16 or FP16 before the double
+ * accumulation, as tensor-core operands are rounded. This is the reference's yardstick for its
+ * reduced-precision device paths — no further from the FP32 reference than a reduced-precision run
+ * of the reference arithmetic (tirex2/tornado/TornadoForwardAccelTest.java:39-44,
+ * GoldenData.nxaiGpuError) — and the tests use it to measure that distance. The default (0) is the
+ * reference's FP32 arithmetic.
  */
 #include "oracle.h"
 
 #include <math.h>
 #include <pthread.h>
 #include <stdatomic.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 
 #define PARALLEL_ROWS 16
+
+static int g_operand_format = JCO_OPERANDS_FP32;
+
+void jco_set_operand_format(int fmt) { g_operand_format = fmt; }
+
+int jco_operand_format(void) { return g_operand_format; }
+
+/* v rounded to nearest even, keeping `bits` explicit mantissa bits (FP32 exponent range). */
+static float round_mantissa(float v, int bits) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return v; /* inf, nan */
+  const int sh = 23 - bits;
+  const uint64_t w = (uint64_t)u + ((1u << (sh - 1)) - 1) + ((u >> sh) & 1u);
+  u = (uint32_t)((w >> sh) << sh);
+  memcpy(&v, &u, 4);
+  return v;
+}
+
+/* v as IEEE half (nearest even, subnormals kept), saturated to ±65504 as the device's operand stores. */
+static float round_half(float v) {
+  if (v != v) return v;
+  if (v > 65504.0f) return 65504.0f;
+  if (v < -65504.0f) return -65504.0f;
+  const float a = fabsf(v);
+  if (a < 6.103515625e-05f) { /* subnormal half: a multiple of 2^-24 */
+    const double q = nearbyint((double)a * 16777216.0) / 16777216.0;
+    return (float)(v < 0 ? -q : q);
+  }
+  return round_mantissa(v, 10);
+}
+
+float jco_round_operand(float v, int fmt) {
+  switch (fmt) {
+    case JCO_OPERANDS_TF32: return round_mantissa(v, 10);
+    case JCO_OPERANDS_BF16: return round_mantissa(v, 7);
+    case JCO_OPERANDS_FP16: return round_half(v);
+    default: return v;
+  }
+}
+
+static float* rounded_copy(const float* a, size_t n, int fmt) {
+  float* r = (float*)malloc(n * sizeof(float));
+  for (size_t i = 0; i < n; i++) r[i] = jco_round_operand(a[i], fmt);
+  return r;
+}
 
 float jco_silu(float v) { return (float)(v / (1.0 + exp(-(double)v))); }
 
@@ -64,7 +119,24 @@ static void* linear_worker(void* arg) {
   return NULL;
 }
 
+static void linear_exact(const float* x, int rows, const float* w, const float* b, int in, int out, float* y,
+                         int threads);
+
 void jco_linear(const float* x, int rows, const float* w, const float* b, int in, int out, float* y, int threads) {
+  const int fmt = g_operand_format;
+  if (fmt == JCO_OPERANDS_FP32) {
+    linear_exact(x, rows, w, b, in, out, y, threads);
+    return;
+  }
+  float* xr = rounded_copy(x, (size_t)rows * in, fmt);
+  float* wr = rounded_copy(w, (size_t)out * in, fmt);
+  linear_exact(xr, rows, wr, b, in, out, y, threads);
+  free(xr);
+  free(wr);
+}
+
+static void linear_exact(const float* x, int rows, const float* w, const float* b, int in, int out, float* y,
+                         int threads) {
   if (rows <= PARALLEL_ROWS || threads <= 1) {
     linear_rows(x, w, b, in, out, y, 0, rows);
     return;

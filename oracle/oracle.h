@@ -16,6 +16,19 @@ extern "C" {
 #define JCO_RELU 16
 #define JCO_GELU 32
 
+/* Operand formats of jco_set_operand_format (a reduced-precision run of the reference arithmetic). */
+#define JCO_OPERANDS_FP32 0
+#define JCO_OPERANDS_TF32 1
+#define JCO_OPERANDS_BF16 2
+#define JCO_OPERANDS_FP16 3
+
+/* Every later jco_linear rounds its x and w elements to `fmt` before the double accumulation
+ * (JCO_OPERANDS_FP32, the default: the reference's own arithmetic). Process-wide, not thread-safe. */
+void jco_set_operand_format(int fmt);
+int jco_operand_format(void);
+/* v rounded to nearest even in `fmt` (FP16 saturating at ±65504). */
+float jco_round_operand(float v, int fmt);
+
 float jco_silu(float v);
 double jco_sigmoid(double v);
 

@@ -182,9 +182,25 @@ void jco_tirex2_slstm_recurrence(const float* wx, int rows, int seq, int d, int 
   free(raw);
 }
 
-/* Cells.headwiseGates (Cells.java:143-168): wx[rt·4d + g·d + h·dh + o] */
+/* Cells.headwiseGates (Cells.java:143-168): wx[rt·4d + g·d + h·dh + o]. Under a reduced-precision operand
+ * format (jco_set_operand_format) its operands are rounded like every other GEMM's. */
 static void headwise_gates(const float* x, int n, int d, int heads, const float* const gates[4], float* wx) {
   const int dh = d / heads;
+  const int fmt = jco_operand_format();
+  float* xr = NULL;
+  const float* gr[4] = {gates[0], gates[1], gates[2], gates[3]};
+  float* gown[4] = {NULL, NULL, NULL, NULL};
+  if (fmt != JCO_OPERANDS_FP32) {
+    xr = fa((size_t)n * d);
+    for (size_t i = 0; i < (size_t)n * d; i++) xr[i] = jco_round_operand(x[i], fmt);
+    x = xr;
+    for (int g = 0; g < 4; g++) {
+      gown[g] = fa((size_t)d * dh);
+      for (size_t i = 0; i < (size_t)d * dh; i++) gown[g][i] = jco_round_operand(gates[g][i], fmt);
+      gr[g] = gown[g];
+    }
+    gates = gr;
+  }
   for (int rt = 0; rt < n; rt++) {
     size_t xo = (size_t)rt * d;
     for (int g = 0; g < 4; g++)
@@ -196,6 +212,8 @@ static void headwise_gates(const float* x, int n, int d, int heads, const float*
           wx[(size_t)rt * 4 * d + g * d + h * dh + o] = (float)acc;
         }
   }
+  free(xr);
+  for (int g = 0; g < 4; g++) free(gown[g]);
 }
 
 /* Cells.mlstm / Cells.slstm on x [rows·seq·d]; returns [rows·seq·d]. */
