@@ -142,6 +142,33 @@ jc_status jc_gemm_device(int device, jc_precision precision, const void* a_hi, c
                          const void* w_hi, const void* w_lo, long long ldw, const float* bias, float* c,
                          long long ldc, int m, int n, int k, int flags, void* stream);
 
+/* One GEMM of a group (jc_gemm_group_device): the arguments of jc_gemm_device after the precision. */
+typedef struct jc_gemm_problem {
+  const void* a_hi;
+  const void* a_lo;
+  long long lda;
+  const void* w_hi;
+  const void* w_lo;
+  long long ldw;
+  const float* bias;
+  float* c;
+  long long ldc;
+  int m, n, k;
+  int flags;
+} jc_gemm_problem;
+
+/*
+ * 1 to 4 independent GEMMs of one precision as ONE persistent launch on DEVICE operands (each problem as
+ * jc_gemm_device: operands in the precision's storage format, its own shape, bias, flags and C), enqueued
+ * on `stream`. Every problem's tiles run in one walk over the SMs; the results equal one jc_gemm_device call
+ * per problem bit for bit. No problem may write what another reads. Replaces the reference's per-head gate
+ * GEMMs of the sLSTM (tirex2/tornado/TornadoForward.java:730, one launch over the dense block-diagonal
+ * packing of tirex2/tornado/PackedWeights.java:242-254) and runs independent projections of one input
+ * together (timestral/tornado/TimestralForward.java:327, the patch embedding's hidden and residual).
+ */
+jc_status jc_gemm_group_device(int device, jc_precision precision, const jc_gemm_problem* problems, int count,
+                               void* stream);
+
 /*
  * Time attention of one layer on DEVICE buffers, the companion kernel of the Timestral and Chronos-2
  * forwards (timestral/tornado/TimestralKernels.java:114 timeAttention, chronos2/tornado/Chronos2Kernels.java:130

@@ -63,6 +63,7 @@ PROTOTYPES: dict[str, tuple] = {
                                          c_int, c_vp]),
     "jc_gemm_device": (c_int, [c_int, c_int, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_vp, c_vp, c_ll, c_int, c_int,
                                c_int, c_int, c_vp]),
+    "jc_gemm_group_device": (c_int, [c_int, c_int, c_vp, c_int, c_vp]),
     "jc_device_sync": (c_int, [c_int]),
     "jc_device_wait_selftest": (c_int, [c_int, c_int]),
     "jc_shard_rows": (c_int, [c_int, c_vp, c_vp, c_int, c_vp]),

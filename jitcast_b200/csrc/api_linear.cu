@@ -216,6 +216,55 @@ jc_status jc_gemm_device(int device, jc_precision precision, const void* a_hi, c
   return JC_OK;
 }
 
+jc_status jc_gemm_group_device(int device, jc_precision precision, const jc_gemm_problem* problems, int count,
+                               void* stream) {
+  clear_error();
+  if (!valid_precision(precision)) return fail(JC_ERR_INVALID_ARG, "unknown precision");
+  if (!problems || count < 1 || count > kMaxGemmGroup)
+    return fail(JC_ERR_INVALID_ARG, "a group holds 1 to " + std::to_string(kMaxGemmGroup) + " problems");
+  GemmArgs g[kMaxGemmGroup];
+  std::string why;
+  for (int i = 0; i < count; ++i) {
+    const jc_gemm_problem& q = problems[i];
+    const std::string at = "problem " + std::to_string(i) + ": ";
+    if (q.m < 1 || q.n < 1 || q.k < 1) return fail(JC_ERR_INVALID_ARG, at + "m, n and k must be positive");
+    if (!q.a_hi || !q.w_hi || !q.c) return fail(JC_ERR_INVALID_ARG, at + "null buffer");
+    if ((q.flags & JC_BIAS) && !q.bias) return fail(JC_ERR_INVALID_ARG, at + "JC_BIAS without a bias");
+    if (q.ldc < q.n) return fail(JC_ERR_INVALID_ARG, at + "ldc smaller than n");
+    int act = 0;
+    if (!act_of(q.flags, &act, &why)) return fail(JC_ERR_INVALID_ARG, at + why);
+    GemmArgs& x = g[i];
+    x = GemmArgs{};
+    x.op = op_of(precision);
+    x.a_hi = q.a_hi;
+    x.a_lo = q.a_lo;
+    x.lda = q.lda;
+    x.w_hi = q.w_hi;
+    x.w_lo = q.w_lo;
+    x.ldw = q.ldw;
+    x.M = q.m;
+    x.N = q.n;
+    x.K = q.k;
+    x.ep = epi_default();
+    x.ep.act = act;
+    x.ep.bias_on = (q.flags & JC_BIAS) != 0;
+    x.ep.bias = q.bias;
+    x.ep.accumulate = (q.flags & JC_ACCUMULATE) != 0;
+    x.ep.c = q.c;
+    x.ep.ldc = q.ldc;
+    x.ep.cin = q.c;
+    x.ep.ldcin = q.ldc;
+  }
+  if (const char* msg = check_gemm_group(g, count)) return fail(JC_ERR_UNSUPPORTED_SHAPE, msg);
+  DeviceRt* rt = device_rt(device, &why);
+  if (!rt) return fail(JC_ERR_NO_DEVICE, why);
+  std::lock_guard<std::mutex> lk(rt->mu);
+  cudaSetDevice(device);
+  cudaError_t e = launch_gemm_group(g, count, static_cast<cudaStream_t>(stream), rt->err);
+  if (e != cudaSuccess) return fail_cuda(e, "grouped GEMM launch");
+  return JC_OK;
+}
+
 jc_status jc_timestral_prep_device(int device, int rows, int encoder, int patch, const float* window,
                                    const uint8_t* observed, const int32_t* known, float minimum_scale, int use_asinh,
                                    float* tokens_out, void* stream) {

@@ -266,6 +266,16 @@ cudaError_t gemm(C2Device& dv, GemmArgs& g, cudaStream_t s, const char* name) {
   return r;
 }
 
+// Independent GEMMs as one grouped launch (launch_gemm_group), timed as one launch under `name`.
+cudaError_t gemm_group(C2Device& dv, GemmArgs* g, int count, cudaStream_t s, const char* name) {
+  double flops = 0.0;
+  for (int i = 0; i < count; ++i) flops += 2.0 * g[i].M * g[i].N * g[i].K;
+  dv.prof.begin(s, name, flops);
+  cudaError_t r = launch_gemm_group(g, count, s, dv.err);
+  dv.prof.end(s);
+  return r;
+}
+
 void set_out(EpiParams& ep, int op, const OpBuf& o) {
   ep.o_kind = out_of_op(op);
   ep.o_hi = o.hi;
@@ -299,20 +309,20 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   prof.begin(s, "convert", 0);
   launch_convert(op, p.tok_f32, P3, p.tok.hi, p.tok.lo, p.tok.ld, EN, P3, s);
   prof.end(s);
-  // input embedding: output(ReLU(hidden(tok))) + residual(tok), around the [REG] token
-  GemmArgs g = gemm_args(op, p.tok, EN, w.in_h);
-  g.ep.act = kActRelu;
-  set_out(g.ep, op, p.emb_h);
-  JC_TRY(gemm(dv, g, s, "gemm.embed"));
-  g = gemm_args(op, p.emb_h, EN, w.in_o);
-  g.ep.c = p.x;
-  g.ep.ldc = d;
-  g.ep.rg = ne;
-  g.ep.rg_stride = n;
-  g.ep.rg_split = nc;
-  g.ep.rg_shift = reg;
-  JC_TRY(gemm(dv, g, s, "gemm.embed"));
-  g = gemm_args(op, p.tok, EN, w.in_r);
+  // input embedding: output(ReLU(hidden(tok))) + residual(tok), around the [REG] token. The two GEMMs of tok
+  // (hidden, and residual stored into x) run as one grouped launch; output then adds into x, the same float
+  // sum as the reference's output + residual
+  GemmArgs ge[2] = {gemm_args(op, p.tok, EN, w.in_h), gemm_args(op, p.tok, EN, w.in_r)};
+  ge[0].ep.act = kActRelu;
+  set_out(ge[0].ep, op, p.emb_h);
+  ge[1].ep.c = p.x;
+  ge[1].ep.ldc = d;
+  ge[1].ep.rg = ne;
+  ge[1].ep.rg_stride = n;
+  ge[1].ep.rg_split = nc;
+  ge[1].ep.rg_shift = reg;
+  JC_TRY(gemm_group(dv, ge, 2, s, "gemm.embed"));
+  GemmArgs g = gemm_args(op, p.emb_h, EN, w.in_o);
   residual_into(g, p.x, d);
   g.ep.rg = ne;
   g.ep.rg_stride = n;
@@ -383,16 +393,16 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   prof.begin(s, "rmsnorm", 0);
   launch_rmsnorm(p.x, d, w.final_norm, d, e.eps, out_kind, p.dec.hi, p.dec.lo, p.dec.ld, decT, h, n, fs, s);
   prof.end(s);
-  g = gemm_args(op, p.dec, decT, w.out_h);
-  g.ep.act = kActRelu;
-  set_out(g.ep, op, p.head_h);
-  JC_TRY(gemm(dv, g, s, "gemm.head"));
+  // the output embedding: output(ReLU(hidden(dec))) + residual(dec); hidden and residual (stored into raw) as
+  // one grouped launch, then output adds into raw
   const int qp = e.Q * e.P;
+  GemmArgs gh[2] = {gemm_args(op, p.dec, decT, w.out_h), gemm_args(op, p.dec, decT, w.out_r)};
+  gh[0].ep.act = kActRelu;
+  set_out(gh[0].ep, op, p.head_h);
+  gh[1].ep.c = p.raw;
+  gh[1].ep.ldc = qp;
+  JC_TRY(gemm_group(dv, gh, 2, s, "gemm.head"));
   g = gemm_args(op, p.head_h, decT, w.out_o);
-  g.ep.c = p.raw;
-  g.ep.ldc = qp;
-  JC_TRY(gemm(dv, g, s, "gemm.head"));
-  g = gemm_args(op, p.dec, decT, w.out_r);
   g.ep.c = p.raw;
   g.ep.ldc = qp;
   g.ep.cin = p.raw;

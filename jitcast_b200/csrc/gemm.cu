@@ -455,12 +455,37 @@ __device__ __forceinline__ void drain_partial(const EpiParams& p, int N, int n0,
   tmem_st_wait();
 }
 
+// ---- problems and groups ----------------------------------------------------------------------
+// One GEMM of a launch: its operands' tensor maps, shape, epilogue and the first tile it owns in the launch's
+// tile walk. A grouped launch walks the tiles of up to kMaxGemmGroup problems one after another, so GEMMs
+// that are independent of each other (the heads of a headwise projection, two projections of one input) share
+// one persistent grid. G = 1 is the plain single GEMM.
+struct alignas(64) GemmProblem {
+  CUtensorMap a, w;    // A [M, K] and W [N, K]
+  CUtensorMap a2, w2;  // the split mode's lo parts (unused otherwise)
+  EpiParams ep;
+  int M, N, kblks, n_blks, tile0;
+};
+
+template <int G>
+struct GemmGroup {
+  GemmProblem p[G];
+  int count, tiles;
+  // The problem that owns tile t of the walk, and t's index within that problem's tiles.
+  __device__ __forceinline__ const GemmProblem& of(int t, int& local) const {
+    int i = 0;
+    if constexpr (G > 1) {
+      while (i + 1 < count && t >= p[i + 1].tile0) ++i;
+    }
+    local = t - p[i].tile0;
+    return p[i];
+  }
+};
+
 // ---- the kernel -----------------------------------------------------------------------------
-template <int BN, int OPK>
+template <int BN, int OPK, int G>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, int M,
-                   int N, int K, EpiParams ep, uint32_t* err) {
+    gemm_tc_kernel(const __grid_constant__ GemmGroup<G> grp, uint32_t* err) {
   using C = Cfg<BN, OPK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -473,9 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_blks = (M + C::BM - 1) / C::BM, n_blks = (N + BN - 1) / BN;
-  const int tiles = m_blks * n_blks;
-  const int kblks = (K + C::BK - 1) / C::BK;
+  const int tiles = grp.tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -491,11 +514,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
-    if (OPK == kOpSplit) {
-      prefetch_tmap(&tmA2);
-      prefetch_tmap(&tmB2);
+    for (int i = 0; i < grp.count; ++i) {
+      prefetch_tmap(&grp.p[i].a);
+      prefetch_tmap(&grp.p[i].w);
+      if (OPK == kOpSplit) {
+        prefetch_tmap(&grp.p[i].a2);
+        prefetch_tmap(&grp.p[i].w2);
+      }
     }
   }
   if (warp == 1) {
@@ -515,8 +540,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
-        for (int kb = 0; kb < kblks; ++kb) {
+        int lt;
+        const GemmProblem& P = grp.of(t, lt);
+        const int m0 = (lt / P.n_blks) * C::BM, n0 = (lt % P.n_blks) * BN;
+        for (int kb = 0; kb < P.kblks; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1) || *abort_flag) {
             atomicOr(err, kErrTimeoutEmpty);
             *abort_flag = 1;
@@ -526,11 +553,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
           mbar_arrive_expect_tx(full + stage, C::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, full + stage, kb * C::BK, m0);
-          tma_load_2d(sb, &tmB, full + stage, kb * C::BK, n0);
+          tma_load_2d(sa, &P.a, full + stage, kb * C::BK, m0);
+          tma_load_2d(sb, &P.w, full + stage, kb * C::BK, n0);
           if (OPK == kOpSplit) {
-            tma_load_2d(sb + C::B_BYTES, &tmA2, full + stage, kb * C::BK, m0);
-            tma_load_2d(sb + C::B_BYTES + C::A_BYTES, &tmB2, full + stage, kb * C::BK, n0);
+            tma_load_2d(sb + C::B_BYTES, &P.a2, full + stage, kb * C::BK, m0);
+            tma_load_2d(sb + C::B_BYTES + C::A_BYTES, &P.w2, full + stage, kb * C::BK, n0);
           }
           ++issued;
           if (++stage == C::STAGES) {
@@ -561,6 +588,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int slab = 0;  // split mode: stages issued so far, each into partial buffer slab % NACC
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++it) {
+        int lt;
+        const int kblks = grp.of(t, lt).kblks;
         const int buf = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         if (!C::SLAB && (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag)) {
@@ -635,8 +664,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int slab = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-      const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
-      for (int kb = 0; kb < kblks; ++kb, ++slab) {
+      int lt;
+      const GemmProblem& P = grp.of(t, lt);
+      const int m0 = (lt / P.n_blks) * C::BM, n0 = (lt % P.n_blks) * BN;
+      for (int kb = 0; kb < P.kblks; ++kb, ++slab) {
         const int pb = slab % C::NACC;
         const bool got = mbar_wait(acc_full + pb, (slab / C::NACC) & 1);
         if (!(__all_sync(0xffffffffu, got) && !*abort_flag)) {
@@ -646,12 +677,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        drain_partial<BN>(ep, N, n0, half, tmem + lanes + pb * BN, sum, kb == 0);
+        drain_partial<BN>(P.ep, P.N, n0, half, tmem + lanes + pb * BN, sum, kb == 0);
         tc_fence_before();
         mbar_arrive(acc_empty + pb);
       }
       if (!ok) break;
-      epilogue_tile<BN>(ep, M, N, m0, n0, sum, row_in_tile, half);
+      epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, sum, row_in_tile, half);
     }
   } else {
     // ---- epilogue: warps 2..9; TMEM lane quarter = warp % 4, column half = (warp - 2) / 4 ----
@@ -662,7 +693,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      prefetch_residual<BN>(ep, M, N, (t / n_blks) * C::BM, (t % n_blks) * BN, row_in_tile, half);
+      int lt;
+      const GemmProblem& P = grp.of(t, lt);
+      const int m0 = (lt / P.n_blks) * C::BM, n0 = (lt % P.n_blks) * BN;
+      prefetch_residual<BN>(P.ep, P.M, P.N, m0, n0, row_in_tile, half);
       const bool got = mbar_wait(acc_full + buf, aph);
       const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
       if (!all) {
@@ -671,12 +705,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m0 = (t / n_blks) * C::BM, n0 = (t % n_blks) * BN;
       // the next tile's residual / table lines, a whole epilogue ahead of their use
       const int tn = t + gridDim.x;
-      if (tn < tiles) prefetch_residual<BN>(ep, M, N, (tn / n_blks) * C::BM, (tn % n_blks) * BN, row_in_tile, half);
+      if (tn < tiles) {
+        int ln;
+        const GemmProblem& Q = grp.of(tn, ln);
+        prefetch_residual<BN>(Q.ep, Q.M, Q.N, (ln / Q.n_blks) * C::BM, (ln % Q.n_blks) * BN, row_in_tile, half);
+      }
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile, half);
+      epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half);
       tc_fence_before();
       mbar_arrive(acc_empty + buf);
     }
@@ -719,10 +756,9 @@ struct CfgPair {
   static_assert(SMEM <= 200 * 1024, "shared memory");
 };
 
-template <int OPK>
+template <int OPK, int G>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
-                     int K, EpiParams ep, uint32_t* err) {
+    gemm_pair_kernel(const __grid_constant__ GemmGroup<G> grp, uint32_t* err) {
   using C = CfgPair<OPK>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
@@ -738,9 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int m_blks = (M + 2 * C::BM - 1) / (2 * C::BM), n_blks = (N + BN - 1) / BN;
-  const int tiles = m_blks * n_blks;
-  const int kblks = (K + C::BK - 1) / C::BK;
+  const int tiles = grp.tiles;
   const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
 
   if (warp == 0 && lane == 0) {
@@ -755,8 +789,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
+    for (int i = 0; i < grp.count; ++i) {
+      prefetch_tmap(&grp.p[i].a);
+      prefetch_tmap(&grp.p[i].w);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
@@ -777,9 +813,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += pairs) {
-        const int m0 = (t / n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM;
-        const int n0 = (t % n_blks) * BN + static_cast<int>(rank) * (BN / 2);
-        for (int kb = 0; kb < kblks; ++kb) {
+        int lt;
+        const GemmProblem& P = grp.of(t, lt);
+        const int m0 = (lt / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM;
+        const int n0 = (lt % P.n_blks) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < P.kblks; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1) || *abort_flag) {
             atomicOr(err, kErrTimeoutEmpty);
             *abort_flag = 1;
@@ -788,8 +826,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           if (leader) mbar_arrive_expect_tx(full + stage, 2 * C::STAGE_BYTES);
-          tma_load_2d_pair(sa, &tmA, full0 + 8 * stage, kb * C::BK, m0);
-          tma_load_2d_pair(sa + C::A_BYTES, &tmB, full0 + 8 * stage, kb * C::BK, n0);
+          tma_load_2d_pair(sa, &P.a, full0 + 8 * stage, kb * C::BK, m0);
+          tma_load_2d_pair(sa + C::A_BYTES, &P.w, full0 + 8 * stage, kb * C::BK, n0);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -805,6 +843,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += pairs, ++it) {
+        int lt;
+        const int kblks = grp.of(t, lt).kblks;
         const int buf = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         if (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag) {
@@ -858,8 +898,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = pair; t < tiles; t += pairs, ++it) {
       const int buf = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      const int m0 = (t / n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (t % n_blks) * BN;
-      prefetch_residual<BN>(ep, M, N, m0, n0, row_in_tile, half);
+      int lt;
+      const GemmProblem& P = grp.of(t, lt);
+      const int m0 = (lt / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (lt % P.n_blks) * BN;
+      prefetch_residual<BN>(P.ep, P.M, P.N, m0, n0, row_in_tile, half);
       const bool got = mbar_wait(acc_full + buf, aph);
       const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
       if (!all) {
@@ -869,11 +911,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const int tn = t + pairs;
-      if (tn < tiles)
-        prefetch_residual<BN>(ep, M, N, (tn / n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM,
-                              (tn % n_blks) * BN, row_in_tile, half);
+      if (tn < tiles) {
+        int ln;
+        const GemmProblem& Q = grp.of(tn, ln);
+        prefetch_residual<BN>(Q.ep, Q.M, Q.N, (ln / Q.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM,
+                              (ln % Q.n_blks) * BN, row_in_tile, half);
+      }
       const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_tile<BN>(ep, M, N, m0, n0, tbase, row_in_tile, half);
+      epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
@@ -979,49 +1024,71 @@ const char* check_gemm(const GemmArgs& g) {
   return nullptr;
 }
 
-template <int BN, int OPK>
-static cudaError_t launch_cfg(const GemmArgs& g, cudaStream_t stream, uint32_t* err, int num_sms) {
+// Fills grp's problems for tiles of bm rows × bn columns (the W box: w_rows rows); false if a map fails.
+template <int G>
+static bool build_group(GemmGroup<G>& grp, const GemmArgs* g, int count, int bm, int bn, int a_rows, int w_rows) {
+  int tile = 0;
+  for (int i = 0; i < count; ++i) {
+    const GemmArgs& x = g[i];
+    GemmProblem& P = grp.p[i];
+    if (!make_map(&P.a, x.a_hi, x.op, x.M, x.K, x.lda, a_rows) || !make_map(&P.w, x.w_hi, x.op, x.N, x.K, x.ldw, w_rows))
+      return false;
+    if (x.op == kOpSplit) {
+      if (!make_map(&P.a2, x.a_lo, x.op, x.M, x.K, x.lda, a_rows) ||
+          !make_map(&P.w2, x.w_lo, x.op, x.N, x.K, x.ldw, w_rows))
+        return false;
+    } else {
+      P.a2 = P.a;
+      P.w2 = P.w;
+    }
+    const int esz = (x.op == kOpBF16 || x.op == kOpF16) ? 2 : 4;
+    const int bk = 128 / esz;
+    P.ep = x.ep;
+    P.M = x.M;
+    P.N = x.N;
+    P.kblks = (x.K + bk - 1) / bk;
+    P.n_blks = (x.N + bn - 1) / bn;
+    P.tile0 = tile;
+    tile += ((x.M + bm - 1) / bm) * P.n_blks;
+  }
+  grp.count = count;
+  grp.tiles = tile;
+  return true;
+}
+
+template <int BN, int OPK, int G>
+static cudaError_t launch_cfg(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
   using C = Cfg<BN, OPK>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<BN, OPK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, OPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
-  CUtensorMap ma, mb, ma2, mb2;
-  if (!make_map(&ma, g.a_hi, OPK, g.M, g.K, g.lda, C::BM) || !make_map(&mb, g.w_hi, OPK, g.N, g.K, g.ldw, BN))
-    return cudaErrorInvalidValue;
-  if (OPK == kOpSplit) {
-    if (!make_map(&ma2, g.a_lo, OPK, g.M, g.K, g.lda, C::BM) || !make_map(&mb2, g.w_lo, OPK, g.N, g.K, g.ldw, BN))
-      return cudaErrorInvalidValue;
-  } else {
-    ma2 = ma;
-    mb2 = mb;
-  }
-  const int tiles = ((g.M + C::BM - 1) / C::BM) * ((g.N + BN - 1) / BN);
-  const int grid = tiles < num_sms ? tiles : num_sms;
-  gemm_tc_kernel<BN, OPK><<<grid, kThreads, C::SMEM, stream>>>(ma, mb, ma2, mb2, g.M, g.N, g.K, g.ep, err);
+  GemmGroup<G> grp;
+  if (!build_group(grp, g, count, C::BM, BN, C::BM, BN)) return cudaErrorInvalidValue;
+  const int grid = grp.tiles < num_sms ? grp.tiles : num_sms;
+  gemm_tc_kernel<BN, OPK, G><<<grid, kThreads, C::SMEM, stream>>>(grp, err);
   return cudaGetLastError();
 }
 
-template <int OPK>
-static cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, uint32_t* err, int num_sms) {
+template <int OPK, int G>
+static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
   using C = CfgPair<OPK>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, g.a_hi, OPK, g.M, g.K, g.lda, C::BM) || !make_map(&mb, g.w_hi, OPK, g.N, g.K, g.ldw, C::BN / 2))
-    return cudaErrorInvalidValue;
-  const int tiles = ((g.M + 2 * C::BM - 1) / (2 * C::BM)) * ((g.N + C::BN - 1) / C::BN);
-  const int pairs = tiles < num_sms / 2 ? tiles : num_sms / 2;
+  GemmGroup<G> grp;
+  if (!build_group(grp, g, count, 2 * C::BM, C::BN, C::BM, C::BN / 2)) return cudaErrorInvalidValue;
+  const int pairs = grp.tiles < num_sms / 2 ? grp.tiles : num_sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1034,7 +1101,7 @@ static cudaError_t launch_pair(const GemmArgs& g, cudaStream_t stream, uint32_t*
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK>, ma, mb, g.M, g.N, g.K, g.ep, err);
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK, G>, grp, err);
 }
 
 // JC_GEMM_PAIR=0 in the environment keeps every GEMM on the single-CTA kernel (for comparisons).
@@ -1059,20 +1126,31 @@ static int sm_count() {
   return count[dev & 63];
 }
 
-// The widest tile that still gives every SM a tile, else the narrowest.
-static int choose_bn(const GemmArgs& g, int num_sms) {
-  if (g.bn) return g.bn;
-  const int m_blks = (g.M + 127) / 128;
-  const int allowed = g.ep.mode == kEpiQKV ? qkv_tile_choices(g.ep) : 7;
+// Tile widths every problem of a launch allows (bit 0: 64, bit 1: 128, bit 2: 256).
+static int allowed_widths(const GemmArgs* g, int count) {
+  int allowed = 7;
+  for (int i = 0; i < count; ++i)
+    if (g[i].ep.mode == kEpiQKV) allowed &= qkv_tile_choices(g[i].ep);
+  return allowed;
+}
+
+// The widest allowed tile that still gives every SM a tile, else the narrowest (all problems of a launch
+// share the tile width).
+static int choose_bn(const GemmArgs* g, int count, int num_sms) {
+  if (g[0].bn) return g[0].bn;
+  const int allowed = allowed_widths(g, count);
   const int widths[3] = {64, 128, 256};
-  // the widest allowed tile that still gives every SM a tile
   for (int i = 2; i >= 0; --i)
     if ((allowed >> i) & 1) {
-      const long long tiles = (long long)m_blks * ((g.N + widths[i] - 1) / widths[i]);
+      long long tiles = 0;
+      for (int j = 0; j < count; ++j)
+        tiles += (long long)((g[j].M + 127) / 128) * ((g[j].N + widths[i] - 1) / widths[i]);
       if (tiles >= num_sms) return widths[i];
     }
   // too few tiles for the grid: the narrowest allowed tile, unless N fits one 128-wide tile
-  if (g.N <= 128 && g.N > 64 && (allowed & 2)) return 128;
+  int max_n = 0;
+  for (int j = 0; j < count; ++j) max_n = g[j].N > max_n ? g[j].N : max_n;
+  if (max_n <= 128 && max_n > 64 && (allowed & 2)) return 128;
   for (int i = 0; i < 3; ++i)
     if ((allowed >> i) & 1) return widths[i];
   return 256;
@@ -1094,49 +1172,77 @@ static int vector_ok(const EpiParams& e) {
   return 0;
 }
 
-cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err) {
-  if (check_gemm(gin)) return cudaErrorInvalidValue;
-  GemmArgs g = gin;
-  g.ep.vec_ok = vector_ok(g.ep);
+template <int G>
+static cudaError_t launch_group(GemmArgs* g, int count, cudaStream_t stream, uint32_t* err) {
+  const int op = g[0].op;
   const int sms = sm_count();
   // CTA pairs for the 16-bit and TF32 modes when the 256 × 256 tiles still give every SM pair work and the
   // tile width keeps the q|k|v|gate layout whole
-  if (pair_enabled() && g.op != kOpSplit && (g.bn == 0 || g.bn == 256) &&
-      (g.ep.mode != kEpiQKV || ((qkv_tile_choices(g.ep) >> 2) & 1))) {
-    const long long ptiles = (long long)((g.M + 255) / 256) * ((g.N + 255) / 256);
+  const int allowed = allowed_widths(g, count);
+  if (pair_enabled() && op != kOpSplit && (g[0].bn == 0 || g[0].bn == 256) && ((allowed >> 2) & 1)) {
+    long long ptiles = 0;
+    for (int i = 0; i < count; ++i) ptiles += (long long)((g[i].M + 255) / 256) * ((g[i].N + 255) / 256);
     if (ptiles >= sms / 2) {
-      switch (g.op) {
-        case kOpBF16: return launch_pair<kOpBF16>(g, stream, err, sms);
-        case kOpF16: return launch_pair<kOpF16>(g, stream, err, sms);
-        default: return launch_pair<kOpTF32>(g, stream, err, sms);
+      switch (op) {
+        case kOpBF16: return launch_pair<kOpBF16, G>(g, count, stream, err, sms);
+        case kOpF16: return launch_pair<kOpF16, G>(g, count, stream, err, sms);
+        default: return launch_pair<kOpTF32, G>(g, count, stream, err, sms);
       }
     }
   }
-  int bn = choose_bn(g, sms);
-  if (g.op == kOpSplit && bn > 128) {  // the split mode's slab buffers: 4 · BN TMEM columns
-    const int allowed = g.ep.mode == kEpiQKV ? qkv_tile_choices(g.ep) : 7;
+  int bn = choose_bn(g, count, sms);
+  if (op == kOpSplit && bn > 128) {  // the split mode's slab buffers: 4 · BN TMEM columns
     bn = (allowed & 2) ? 128 : (allowed & 1) ? 64 : 0;
     if (!bn) return cudaErrorInvalidValue;
   }
-#define JC_LAUNCH(BN_)                                                  \
-  switch (g.op) {                                                       \
-    case kOpBF16: return launch_cfg<BN_, kOpBF16>(g, stream, err, sms); \
-    case kOpTF32: return launch_cfg<BN_, kOpTF32>(g, stream, err, sms); \
-    case kOpF16: return launch_cfg<BN_, kOpF16>(g, stream, err, sms);   \
-    default: return launch_cfg<BN_, kOpSplit>(g, stream, err, sms);     \
-  }
   if (bn == 256) {
-    switch (g.op) {
-      case kOpBF16: return launch_cfg<256, kOpBF16>(g, stream, err, sms);
-      case kOpTF32: return launch_cfg<256, kOpTF32>(g, stream, err, sms);
-      default: return launch_cfg<256, kOpF16>(g, stream, err, sms);
+    switch (op) {
+      case kOpBF16: return launch_cfg<256, kOpBF16, G>(g, count, stream, err, sms);
+      case kOpTF32: return launch_cfg<256, kOpTF32, G>(g, count, stream, err, sms);
+      default: return launch_cfg<256, kOpF16, G>(g, count, stream, err, sms);
     }
-  } else if (bn == 128) {
+  }
+#define JC_LAUNCH(BN_)                                                              \
+  switch (op) {                                                                     \
+    case kOpBF16: return launch_cfg<BN_, kOpBF16, G>(g, count, stream, err, sms);   \
+    case kOpTF32: return launch_cfg<BN_, kOpTF32, G>(g, count, stream, err, sms);   \
+    case kOpF16: return launch_cfg<BN_, kOpF16, G>(g, count, stream, err, sms);     \
+    default: return launch_cfg<BN_, kOpSplit, G>(g, count, stream, err, sms);       \
+  }
+  if (bn == 128) {
     JC_LAUNCH(128)
   } else {
     JC_LAUNCH(64)
   }
 #undef JC_LAUNCH
+}
+
+cudaError_t launch_gemm(const GemmArgs& gin, cudaStream_t stream, uint32_t* err) {
+  if (check_gemm(gin)) return cudaErrorInvalidValue;
+  GemmArgs g = gin;
+  g.ep.vec_ok = vector_ok(g.ep);
+  return launch_group<1>(&g, 1, stream, err);
+}
+
+const char* check_gemm_group(const GemmArgs* g, int count) {
+  if (count < 1 || count > kMaxGemmGroup) return "a GEMM group holds 1 to kMaxGemmGroup problems";
+  for (int i = 0; i < count; ++i) {
+    if (const char* m = check_gemm(g[i])) return m;
+    if (g[i].op != g[0].op) return "the problems of a GEMM group must share the operand kind";
+    if (g[i].bn != g[0].bn) return "the problems of a GEMM group must share the tile width request";
+  }
+  return nullptr;
+}
+
+cudaError_t launch_gemm_group(const GemmArgs* gin, int count, cudaStream_t stream, uint32_t* err) {
+  if (check_gemm_group(gin, count)) return cudaErrorInvalidValue;
+  GemmArgs g[kMaxGemmGroup];
+  for (int i = 0; i < count; ++i) {
+    g[i] = gin[i];
+    g[i].ep.vec_ok = vector_ok(g[i].ep);
+  }
+  if (count == 1) return launch_group<1>(g, 1, stream, err);
+  return launch_group<kMaxGemmGroup>(g, count, stream, err);
 }
 
 }  // namespace jc

@@ -106,6 +106,14 @@ cudaError_t launch_gemm(const GemmArgs& g, cudaStream_t stream, uint32_t* err);
 // Checks the alignment and shape rules of launch_gemm; returns nullptr or a message.
 const char* check_gemm(const GemmArgs& g);
 
+// Up to kMaxGemmGroup independent GEMMs of one operand kind as ONE persistent launch: the tiles of every
+// problem in one walk over the SMs, each tile with its own problem's operands, shape and epilogue. For GEMMs
+// that could run in any order (a headwise projection's heads; two projections of one input), it saves the
+// launches, the grid tails and the prologues of all but one. Results equal separate launch_gemm calls.
+constexpr int kMaxGemmGroup = 4;
+cudaError_t launch_gemm_group(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err);
+const char* check_gemm_group(const GemmArgs* g, int count);
+
 // A 2-D TMA tensor map over a row-major [rows, k] matrix of operand kind `op` (row pitch `ld`
 // elements): 128-byte swizzle, box = 128 bytes of a row × box_rows rows, zero fill past the edges.
 // The layout the tcgen05 K-major (and, for 64 16-bit columns, MN-major) operand descriptors read.

@@ -324,6 +324,16 @@ cudaError_t gemm(TsDevice& dv, GemmArgs& g, cudaStream_t s, const char* name) {
   return r;
 }
 
+// Independent GEMMs as one grouped launch (launch_gemm_group), timed as one launch under `name`.
+cudaError_t gemm_group(TsDevice& dv, GemmArgs* g, int count, cudaStream_t s, const char* name) {
+  double flops = 0.0;
+  for (int i = 0; i < count; ++i) flops += 2.0 * g[i].M * g[i].N * g[i].K;
+  dv.prof.begin(s, name, flops);
+  cudaError_t r = launch_gemm_group(g, count, s, dv.err);
+  dv.prof.end(s);
+  return r;
+}
+
 void set_op_out(EpiParams& ep, int op, const OpBuf& o) {
   ep.o_kind = out_of_op(op);
   ep.o_hi = o.hi;
@@ -348,18 +358,18 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   prof.begin(s, "convert", 0);
   launch_convert(op, p.tok_f32, P2, p.tok.hi, p.tok.lo, p.tok.ld, encT, P2, s);
   prof.end(s);
-  // patch embedding: output(SiLU(hidden(tok))) + residual(tok), into the encoder rows of x
-  GemmArgs g = gemm_args(op, p.tok, encT, w.emb_h);
-  g.ep.act = kActSilu;
-  set_op_out(g.ep, op, p.emb_h);
-  JC_TRY(gemm(dv, g, s, "gemm.embed"));
-  g = gemm_args(op, p.emb_h, encT, w.emb_o);
-  g.ep.c = p.x;
-  g.ep.ldc = d;
-  g.ep.rg = E;
-  g.ep.rg_stride = n;
-  JC_TRY(gemm(dv, g, s, "gemm.embed"));
-  g = gemm_args(op, p.tok, encT, w.emb_r);
+  // patch embedding: output(SiLU(hidden(tok))) + residual(tok), into the encoder rows of x. The two GEMMs of
+  // tok (hidden, and residual stored into x) run as one grouped launch; output then adds into x, the same
+  // float sum as the reference's output + residual
+  GemmArgs ge[2] = {gemm_args(op, p.tok, encT, w.emb_h), gemm_args(op, p.tok, encT, w.emb_r)};
+  ge[0].ep.act = kActSilu;
+  set_op_out(ge[0].ep, op, p.emb_h);
+  ge[1].ep.c = p.x;
+  ge[1].ep.ldc = d;
+  ge[1].ep.rg = E;
+  ge[1].ep.rg_stride = n;
+  JC_TRY(gemm_group(dv, ge, 2, s, "gemm.embed"));
+  GemmArgs g = gemm_args(op, p.emb_h, encT, w.emb_o);
   g.ep.c = p.x;
   g.ep.ldc = d;
   g.ep.cin = p.x;
@@ -449,16 +459,16 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   prof.begin(s, "rmsnorm", 0);
   launch_rmsnorm(p.x, d, w.out_norm, d, e.eps, out_kind, p.dec.hi, p.dec.lo, p.dec.ld, decT, H, n, E, s);
   prof.end(s);
-  g = gemm_args(op, p.dec, decT, w.head_h);
-  g.ep.act = kActSilu;
-  set_op_out(g.ep, op, p.head_h);
-  JC_TRY(gemm(dv, g, s, "gemm.head"));
+  // the head: output(SiLU(hidden(dec))) + residual(dec); hidden and residual (stored into raw) as one grouped
+  // launch, then output adds into raw
   const int pq = e.P * e.Q;
+  GemmArgs gh[2] = {gemm_args(op, p.dec, decT, w.head_h), gemm_args(op, p.dec, decT, w.head_r)};
+  gh[0].ep.act = kActSilu;
+  set_op_out(gh[0].ep, op, p.head_h);
+  gh[1].ep.c = p.raw;
+  gh[1].ep.ldc = pq;
+  JC_TRY(gemm_group(dv, gh, 2, s, "gemm.head"));
   g = gemm_args(op, p.head_h, decT, w.head_o);
-  g.ep.c = p.raw;
-  g.ep.ldc = pq;
-  JC_TRY(gemm(dv, g, s, "gemm.head"));
-  g = gemm_args(op, p.dec, decT, w.head_r);
   g.ep.c = p.raw;
   g.ep.ldc = pq;
   g.ep.cin = p.raw;

@@ -1431,6 +1431,16 @@ cudaError_t gemm(TxDevice& dv, GemmArgs& g, cudaStream_t s, const char* name) {
   return r;
 }
 
+// Independent GEMMs as one grouped launch (launch_gemm_group), timed as one launch under `name`.
+cudaError_t gemm_group(TxDevice& dv, GemmArgs* g, int count, cudaStream_t s, const char* name) {
+  double flops = 0.0;
+  for (int i = 0; i < count; ++i) flops += 2.0 * g[i].M * g[i].N * g[i].K;
+  dv.prof.begin(s, name, flops);
+  cudaError_t r = launch_gemm_group(g, count, s, dv.err);
+  dv.prof.end(s);
+  return r;
+}
+
 void set_out(EpiParams& ep, int op, const OpBuf& o) {
   ep.o_kind = out_of_op(op);
   ep.o_hi = o.hi;
@@ -1493,11 +1503,18 @@ cudaError_t run_cell(const Tirex2Engine& e, TxDevice& dv, TxPlan& p, const TxBlo
     into_f32(g, dst, d, accumulate);
     JC_TRY(gemm(dv, g, s, "gemm.out_proj"));
   } else {
+    // the headwise gate projections (Cells.headwiseGates): one K = 128 GEMM per head, all heads as one grouped
+    // launch (kMaxGemmGroup heads at a time)
     const long long ldw = 4LL * d;
-    for (int h = 0; h < e.SH; ++h) {
-      GemmArgs g = gemm_args(op, cols_of(in, op, static_cast<long long>(h) * kDh), T, B.gates[h]);
-      into_f32(g, p.proj + h * 4 * kDh, ldw, false);
-      JC_TRY(gemm(dv, g, s, "gemm.gates"));
+    for (int h0 = 0; h0 < e.SH; h0 += kMaxGemmGroup) {
+      GemmArgs gh[kMaxGemmGroup];
+      const int cnt = e.SH - h0 < kMaxGemmGroup ? e.SH - h0 : kMaxGemmGroup;
+      for (int j = 0; j < cnt; ++j) {
+        const int h = h0 + j;
+        gh[j] = gemm_args(op, cols_of(in, op, static_cast<long long>(h) * kDh), T, B.gates[h]);
+        into_f32(gh[j], p.proj + h * 4 * kDh, ldw, false);
+      }
+      JC_TRY(gemm_group(dv, gh, cnt, s, "gemm.gates"));
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kSlCta * ((rows + kSlRows - 1) / kSlRows), e.SH);
@@ -1536,14 +1553,14 @@ cudaError_t enqueue_forward(const Tirex2Engine& e, TxDevice& dv, TxPlan& p, cuda
                                        p.tok.lo, p.tok.ld, p.stats);
   prof.end(s);
   JC_TRY(cudaGetLastError());
-  GemmArgs g = gemm_args(op, p.tok, T, w.in_h);
-  g.ep.act = kActSilu;
-  set_out(g.ep, op, p.emb_h);
-  JC_TRY(gemm(dv, g, s, "gemm.embed"));
-  g = gemm_args(op, p.emb_h, T, w.in_o);
-  into_f32(g, p.h, d, false);
-  JC_TRY(gemm(dv, g, s, "gemm.embed"));
-  g = gemm_args(op, p.tok, T, w.in_r);
+  // input embedding: output(SiLU(hidden(tok))) + residual(tok). The two GEMMs of tok (hidden, and residual
+  // stored into h) run as one grouped launch; output then adds into h, the same float sum as the reference's
+  GemmArgs ge[2] = {gemm_args(op, p.tok, T, w.in_h), gemm_args(op, p.tok, T, w.in_r)};
+  ge[0].ep.act = kActSilu;
+  set_out(ge[0].ep, op, p.emb_h);
+  into_f32(ge[1], p.h, d, false);
+  JC_TRY(gemm_group(dv, ge, 2, s, "gemm.embed"));
+  GemmArgs g = gemm_args(op, p.emb_h, T, w.in_o);
   into_f32(g, p.h, d, true);
   JC_TRY(gemm(dv, g, s, "gemm.embed"));
   for (const TxBlock& B : w.blocks) {
@@ -1636,15 +1653,15 @@ cudaError_t enqueue_forward(const Tirex2Engine& e, TxDevice& dv, TxPlan& p, cuda
   prof.begin(s, "rmsnorm", 0);
   launch_rmsnorm(p.h, d, w.out_norm, d, e.out_eps, ok_kind, p.xn.hi, p.xn.lo, p.xn.ld, T, 0, 0, 0, s);
   prof.end(s);
-  g = gemm_args(op, p.xn, T, w.out_h);
-  g.ep.act = kActSilu;
-  set_out(g.ep, op, p.oh);
-  JC_TRY(gemm(dv, g, s, "gemm.head"));
+  // the output embedding: output(SiLU(hidden(xn))) + residual(xn); hidden and residual (stored into y) as one
+  // grouped launch, then output adds into y
   const long long qp = static_cast<long long>(e.Q) * P;
+  GemmArgs gh[2] = {gemm_args(op, p.xn, T, w.out_h), gemm_args(op, p.xn, T, w.out_r)};
+  gh[0].ep.act = kActSilu;
+  set_out(gh[0].ep, op, p.oh);
+  into_f32(gh[1], p.y, qp, false);
+  JC_TRY(gemm_group(dv, gh, 2, s, "gemm.head"));
   g = gemm_args(op, p.oh, T, w.out_o);
-  into_f32(g, p.y, qp, false);
-  JC_TRY(gemm(dv, g, s, "gemm.head"));
-  g = gemm_args(op, p.xn, T, w.out_r);
   into_f32(g, p.y, qp, true);
   JC_TRY(gemm(dv, g, s, "gemm.head"));
   prof.begin(s, "unpatch", 0);

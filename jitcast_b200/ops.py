@@ -8,13 +8,15 @@ already live in HBM (torch CUDA tensors), enqueued on the current torch stream.
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 
 from . import _lib
 from ._lib import ACCUMULATE, BIAS, GELU, RELU, SILU, TWIN_ONLY, check, precision_code
 
-__all__ = ["gemm", "linear", "linear_device", "device_sync", "BIAS", "ACCUMULATE", "SILU", "RELU", "GELU",
-           "TWIN_ONLY"]
+__all__ = ["gemm", "linear", "linear_device", "gemm_device", "gemm_group_device", "GemmProblem", "device_sync", "BIAS",
+           "ACCUMULATE", "SILU", "RELU", "GELU", "TWIN_ONLY"]
 
 
 def _f32(a) -> np.ndarray:
@@ -64,6 +66,44 @@ def linear_device(a, w, bias, c, flags: int, precision="bf16", stream=None) -> N
                                      w.data_ptr(), w.stride(0), None if bias is None else bias.data_ptr(),
                                      c.data_ptr(), c.stride(0), m, n, k, flags, s.cuda_stream)
     check(st)
+
+
+class GemmProblem(ctypes.Structure):
+    """jc_gemm_problem: one GEMM of a group, on device operands in the precision's storage format."""
+
+    _fields_ = [("a_hi", ctypes.c_void_p), ("a_lo", ctypes.c_void_p), ("lda", ctypes.c_longlong),
+                ("w_hi", ctypes.c_void_p), ("w_lo", ctypes.c_void_p), ("ldw", ctypes.c_longlong),
+                ("bias", ctypes.c_void_p), ("c", ctypes.c_void_p), ("ldc", ctypes.c_longlong), ("m", ctypes.c_int),
+                ("n", ctypes.c_int), ("k", ctypes.c_int), ("flags", ctypes.c_int)]
+
+
+def problem(a_hi, w_hi, c, flags: int = 0, bias=None, a_lo=None, w_lo=None) -> GemmProblem:
+    """A GemmProblem over torch CUDA tensors: ``a_hi`` [m, k] and ``w_hi`` [n, k] (row views, unit column stride)
+    in the storage format (bf16 / fp16 / fp32 holding TF32; JC_FP32 adds the fp32 remainders ``a_lo``, ``w_lo``),
+    ``c`` [m, n] fp32, ``bias`` [n] fp32 or None."""
+    m, k = a_hi.shape
+    n = w_hi.shape[0]
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    return GemmProblem(ptr(a_hi), ptr(a_lo), a_hi.stride(0), ptr(w_hi), ptr(w_lo), w_hi.stride(0), ptr(bias),
+                       c.data_ptr(), c.stride(0), m, n, k, flags)
+
+
+def gemm_device(p: GemmProblem, precision="bf16", device: int = 0, stream=None) -> None:
+    """``jc_gemm_device`` for one problem, enqueued on ``stream`` (default: torch's current stream)."""
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    check(_lib.lib().jc_gemm_device(device, precision_code(precision), p.a_hi, p.a_lo, p.lda, p.w_hi, p.w_lo, p.ldw,
+                                    p.bias, p.c, p.ldc, p.m, p.n, p.k, p.flags, s.cuda_stream))
+
+
+def gemm_group_device(problems, precision="bf16", device: int = 0, stream=None) -> None:
+    """``jc_gemm_group_device``: 1 to 4 independent problems as one launch, enqueued on ``stream``."""
+    import torch
+
+    arr = (GemmProblem * len(problems))(*problems)
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    check(_lib.lib().jc_gemm_group_device(device, precision_code(precision), arr, len(problems), s.cuda_stream))
 
 
 def device_sync(device: int = 0) -> None:

@@ -102,7 +102,7 @@ _STRUCTS = [("jc_tensor_view", "timestral._TensorView"), ("jc_timestral_desc", "
             ("jc_timestral_block", "timestral.Block"), ("jc_timestral_window", "timestral.Window"),
             ("jc_chronos2_desc", "chronos2._Desc"), ("jc_chronos2_block", "chronos2.Block"),
             ("jc_chronos2_window", "chronos2.Window"), ("jc_tirex2_desc", "tirex2._Desc"),
-            ("jc_tirex2_batch", "tirex2.Batch")]
+            ("jc_tirex2_batch", "tirex2.Batch"), ("jc_gemm_problem", "ops.GemmProblem")]
 
 
 def test_struct_layouts_match_the_header(tmp_path):
@@ -132,6 +132,27 @@ def test_struct_layouts_match_the_header(tmp_path):
         assert got[(c, "size")] == ctypes.sizeof(cls), c
         for name, _ in cls._fields_:
             assert got[(c, name)] == getattr(cls, name).offset, f"{c}.{name}"
+
+
+def test_gemm_group_rejects_bad_groups():
+    # argument errors come back before any device work (no GPU needed)
+    from jitcast_b200 import ops
+
+    L = _lib.lib()
+    a = np.ones((64, 64), np.float32)
+    c = np.zeros((64, 64), np.float32)
+    good = ops.GemmProblem(a.ctypes.data, None, 64, a.ctypes.data, None, 64, None, c.ctypes.data, 64, 64, 64, 64, 0)
+    arr = (ops.GemmProblem * 5)(*([good] * 5))
+    assert L.jc_gemm_group_device(0, _lib.BF16, arr, 0, None) == _lib.ERR_INVALID_ARG
+    assert L.jc_gemm_group_device(0, _lib.BF16, arr, 5, None) == _lib.ERR_INVALID_ARG
+    assert L.jc_gemm_group_device(0, _lib.BF16, None, 1, None) == _lib.ERR_INVALID_ARG
+    bad = (ops.GemmProblem * 2)(good, ops.GemmProblem(a.ctypes.data, None, 64, a.ctypes.data, None, 64, None,
+                                                      c.ctypes.data, 64, 64, 64, 0, 0))
+    assert L.jc_gemm_group_device(0, _lib.BF16, bad, 2, None) == _lib.ERR_INVALID_ARG
+    assert "problem 1" in _lib.last_error()
+    flagged = (ops.GemmProblem * 1)(ops.GemmProblem(a.ctypes.data, None, 64, a.ctypes.data, None, 64, None,
+                                                    c.ctypes.data, 64, 64, 64, 64, _lib.BIAS))
+    assert L.jc_gemm_group_device(0, _lib.BF16, flagged, 1, None) == _lib.ERR_INVALID_ARG
 
 
 def test_wait_selftest_arguments():

@@ -5,7 +5,7 @@ Inputs follow the reference's batch-parity test (Chronos2BatchParityAccelTest.ja
 plus a daily sinusoid, NaN gaps, late starts, multi-row groups with known future covariates); the
 error is max|a − e| / max|e| on every quantile level. Bars (parity_bars): FP32 (the FP32-accumulate mode)
 1e-4 on the tiny model (the reference's FP32 device bar) and the north star's 1e-3 on config 2; TF32 1e-3, BF16
-and FP16 1e-2, or 1.5 × the error of the oracle run with its GEMM operands rounded to the mode's format where
+and FP16 1e-2, or 2 × the error of the oracle run with its GEMM operands rounded to the mode's format where
 that is larger (the reference's rule for reduced-precision device paths).
 """
 

@@ -57,7 +57,7 @@ def test_headline_chunk_matches_oracle(jc, headline, precision):
     c, w, block, exp = headline
     dev = torch.device("cuda", 0)
     lay = ts.BlockLayout.of(c, block)
-    assert lay.rows == CHUNK and lay.tokens == CHUNK * 130
+    assert lay.rows == CHUNK and lay.tokens == 130
     stream = torch.cuda.Stream(dev)
     with ts.TimestralEngine(c, w, precision=precision) as eng:
         dw = ts.DeviceWindow(ts.WindowInputs.of(c, lay), dev)
