@@ -80,6 +80,8 @@ def parse():
     ap.add_argument("--precision", default="fp16", choices=["fp16", "bf16", "tf32", "fp32"])
     ap.add_argument("--cpu-series", type=int, default=2, help="series in the CPU baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-engine", action="store_true",
+                    help="skip the multi-GPU engine measurement (N > 1: one process, one engine over all N GPUs)")
     ap.add_argument("--workload", default="config5", choices=["config5", "config2", "config4"],
                     help="config5 (default: the headline box-scale Timestral batch), config2 (Chronos-2, 256 "
                          "series) or config4 (TiRex-2, 512 series), one GPU")
@@ -223,6 +225,44 @@ def pinned_empty(shape: tuple) -> np.ndarray:
     import torch
 
     return torch.empty(shape, dtype=torch.float32, pin_memory=True).numpy()
+
+
+def engine_multi_gpu(args, cfg, weights, world: int) -> dict:
+    """The library's own multi-GPU path, as a Java caller reaches it: ONE TimestralEngine over devices 0..N-1 and
+    jc_forecast_timestral on host buffers (the block's rows sharded over the GPUs on series boundaries, one host
+    thread per GPU, each shard's finished quantiles copied into one pinned caller buffer; SeriesWindows.split,
+    host/SeriesWindows.java:37-56). Each call carries N chunks of ``--chunk`` series (every GPU runs a chunk, as
+    the per-process bench does); a step is the whole batch. Wall-clock time of the calls (each returns after its
+    gather), copies included."""
+    from jitcast_b200 import timestral as ts
+    from jitcast_b200 import workloads
+
+    engine = ts.TimestralEngine(cfg, weights, devices=tuple(range(world)), precision=args.precision)
+    per_call = args.chunk * world
+    calls = []
+    for c0 in range(0, args.series, per_call):
+        n = min(per_call, args.series - c0)
+        # the same chunk-seeded series as the per-process bench
+        x = np.concatenate([workloads.sinusoid_noise(min(args.chunk, c0 + n - s0), 4096, seed=s0)
+                            for s0 in range(c0, c0 + n, args.chunk)])
+        b = ts.BlockInput(x, np.ones_like(x, bool), np.arange(n, dtype=np.int32), 2)
+        wi = ts.WindowInputs.of(cfg, ts.BlockLayout.of(cfg, b))
+        lp = dataclasses.replace(wi.layout, **{k: pinned(getattr(wi.layout, k)) for k in ts.DeviceWindow.FIELDS})
+        hp = dataclasses.replace(wi, layout=lp, window=pinned(wi.window), observed=pinned(wi.observed))
+        calls.append((hp, pinned_empty((n, 2 * cfg.patch_size, cfg.num_quantiles))))
+    for hp, qp in calls:  # warm-up: plans and graphs on every GPU
+        engine.forecast(hp, out=qp)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for hp, qp in calls:
+            engine.forecast(hp, out=qp)
+    dt = (time.perf_counter() - t0) / args.steps
+    engine.close()
+    return {"value": args.series / dt, "unit": UNIT, "n_gpus": world, "ms_per_step": 1000.0 * dt,
+            "calls_per_step": len(calls), "series_per_call": per_call,
+            "path": "one process: jc_forecast_timestral on a TimestralEngine over devices 0..N-1 (rows sharded on "
+                    "series boundaries, one host thread per GPU, quantiles gathered into one pinned caller buffer); "
+                    "host buffers, copies timed, wall clock"}
 
 
 def workload_bench(args, world):
@@ -477,6 +517,19 @@ def main():
     # operands), scaled by the chunk's series: the activations are all but a few MB of it and grow with the rows.
     traffic = GEMM_BYTES_PER_LAUNCH_1024 * min(args.chunk, per_rank) / 1024.0 if args.precision == "fp16" else None
 
+    # the library's own multi-GPU engine (N > 1): every rank frees its GPU, rank 0 drives all N from one process
+    # while the others wait on a host-side (gloo) barrier, so no collective kernel waits on a GPU meanwhile
+    engine_line = None
+    n_chunks = len(chunks)
+    if world > 1 and not args.no_engine:
+        engine.close()
+        chunks.clear()  # the device windows and outputs
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        host_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=1200))
+        if rank == 0:
+            engine_line = engine_multi_gpu(args, cfg, weights, world)
+        dist.barrier(group=host_group)
     if rank != 0:
         engine.close()
         if world > 1:
@@ -502,11 +555,13 @@ def main():
                          "peak_kind": f"{pk_kind} bf16 dense, sustained",
                          "gemm_time_share": total_gemm_share},
             "cpu_baseline": cpu, "clocks": clocks.summary(),
-            "gpu_launches": launches_per_forward * len(chunks) * args.steps,
+            "gpu_launches": launches_per_forward * n_chunks * args.steps,
             "kernel_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
                                    **({"tflops": round(v["flops"] / v["ms"] / 1e9, 1)} if v["flops"] else {})}
                                for k, v in prof.items()},
             "host_ends_profile": {k: {"ms": round(v["ms"], 3), "launches": v["launches"]} for k, v in ends_prof.items()}}
+    if engine_line is not None:
+        line["engine_multi_gpu"] = engine_line
     print(json.dumps(line), flush=True)
     engine.close()
     if world > 1:

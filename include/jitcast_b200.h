@@ -515,6 +515,13 @@ jc_status jc_shard_rows(int rows, const int32_t* group_start, const int32_t* gro
  *                 padding, TimestralForward.bucket, TimestralForward.java:88-99); 0 one plan per exact row
  *                 count
  *   "profile"     1: run eagerly and time every kernel class with CUDA events (jc_engine_profile)
+ * Failure injection on the host, for tests of the error paths (no GPU fault is involved):
+ *   "fail_plan_allocs"  N: the next N plan allocations report out of device memory. As the reference's
+ *                 PlanCache.run (tornado/PlanCache.java:70-100), a failed allocation with other plans cached
+ *                 drops them and retries once; with none cached, or when the retry fails too, the call
+ *                 returns JC_ERR_OOM and the engine stays usable
+ *   "fail_slot"   s: the next forward's shard on engine slot s fails before it enqueues any work; the call
+ *                 gathers every shard, then returns JC_ERR_CUDA naming the slot (-1: none)
  */
 jc_status jc_engine_set_option(jc_engine* engine, const char* key, long long value);
 

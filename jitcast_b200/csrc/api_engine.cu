@@ -57,6 +57,12 @@ jc_status jc_engine_set_option(jc_engine* engine, const char* key, long long val
     engine->drop_plans();
   } else if (k == "buckets") {
     engine->buckets = value != 0;
+  } else if (k == "fail_plan_allocs") {
+    if (value < 0 || value > 1000000) return fail(JC_ERR_INVALID_ARG, "fail_plan_allocs must be in [0, 1e6]");
+    engine->fail_plan_allocs = static_cast<int>(value);
+  } else if (k == "fail_slot") {
+    if (value < -1 || value >= engine->slots()) return fail(JC_ERR_INVALID_ARG, "fail_slot must be -1 or a slot");
+    engine->fail_slot = static_cast<int>(value);
   } else if (k == "profile") {
     engine->profile = value != 0;
     for (int i = 0; i < engine->slots(); ++i) engine->profiler(i)->on = engine->profile;

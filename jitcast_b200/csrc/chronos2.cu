@@ -245,11 +245,11 @@ C2Plan* get_plan(Chronos2Engine& e, C2Device& dv, int rows, int nc, int h, std::
     }
   }
   while (static_cast<int>(dv.plans.size()) >= std::max(1, e.max_plans)) dv.plans.pop_back();
-  auto p = make_plan(e, rows, nc, h);
+  auto p = e.take_plan_failure() ? nullptr : make_plan(e, rows, nc, h);
   if (!p && !dv.plans.empty()) {
     cudaStreamSynchronize(dv.stream);
     dv.plans.clear();
-    p = make_plan(e, rows, nc, h);
+    p = e.take_plan_failure() ? nullptr : make_plan(e, rows, nc, h);
   }
   if (!p) {
     *err = "out of device memory for a plan of " + std::to_string(rows) + " rows";
@@ -458,6 +458,10 @@ bool ensure_ends(C2Plan& p, int P, int Q, bool host) {
 // ModelPrep.finish's quantiles [rows · Q · h·P].
 jc_status run_shard(Chronos2Engine& e, C2Device& dv, const jc_chronos2_block* b, int r0, int r1, float* raw_out,
                     bool host, cudaStream_t stream, std::string* err, const jc_chronos2_window* ends = nullptr) {
+  if (e.take_slot_failure(dv.slot)) {  // injected (engine option fail_slot), before any device work
+    *err = "injected shard failure (engine option fail_slot)";
+    return JC_ERR_CUDA;
+  }
   if (cudaSetDevice(dv.device) != cudaSuccess) {
     *err = "cannot select device " + std::to_string(dv.device);
     return JC_ERR_CUDA;
@@ -654,6 +658,7 @@ jc_status jc_engine_create_chronos2(const jc_chronos2_desc* desc, const jc_tenso
       return fail_cuda(cudaGetLastError(), "engine device setup");
     std::string err;
     if (!upload(*e, hw, *dv, &err)) return fail(JC_ERR_OOM, err);
+    dv->slot = static_cast<int>(e->devs.size());
     e->devs.push_back(std::move(dv));
   }
   *out = e.release();
@@ -684,7 +689,7 @@ jc_status jc_forward_chronos2(jc_engine* engine, const jc_chronos2_block* block,
     for (auto& t : th) t.join();
   }
   for (int i = 0; i < parts; ++i)
-    if (status[i] != JC_OK) return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+    if (status[i] != JC_OK) return fail(status[i], "slot " + std::to_string(i) + " (GPU " + std::to_string(e->devs[i]->device) + "): " + errs[i]);
   return JC_OK;
 }
 
@@ -728,7 +733,7 @@ jc_status jc_forecast_chronos2(jc_engine* engine, const jc_chronos2_window* bloc
     for (auto& t : th) t.join();
   }
   for (int i = 0; i < parts; ++i)
-    if (status[i] != JC_OK) return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+    if (status[i] != JC_OK) return fail(status[i], "slot " + std::to_string(i) + " (GPU " + std::to_string(e->devs[i]->device) + "): " + errs[i]);
   return JC_OK;
 }
 

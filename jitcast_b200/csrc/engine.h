@@ -5,6 +5,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <functional>
 #include <list>
@@ -133,6 +134,7 @@ class Profiler {
 // The device slot an engine owns on one GPU.
 struct DeviceSlot {
   int device = 0;
+  int slot = 0;  // its index among the engine's slots (two slots may share a GPU)
   cudaStream_t stream = nullptr;
   uint32_t* err = nullptr;
   DeviceMem weights;
@@ -163,6 +165,21 @@ struct jc_engine {
   int max_plans = 8;
   bool profile = false;
   bool buckets = true;  // plans (and graphs) for bucketed row counts
+  // Host-side failure injection (engine options "fail_plan_allocs" and "fail_slot"): the next N plan allocations
+  // report out of memory, and the next forward's shard on slot fail_slot fails before it enqueues anything.
+  // Shards of one call run on parallel host threads, hence the atomics.
+  std::atomic<int> fail_plan_allocs{0};
+  std::atomic<int> fail_slot{-1};
+  bool take_plan_failure() {
+    int n = fail_plan_allocs.load();
+    while (n > 0)
+      if (fail_plan_allocs.compare_exchange_weak(n, n - 1)) return true;
+    return false;
+  }
+  bool take_slot_failure(int slot) {
+    int s = slot;
+    return fail_slot.compare_exchange_strong(s, -1);
+  }
   virtual int slots() const = 0;
   virtual jc::DeviceSlot* slot(int i) = 0;
   virtual jc::Profiler* profiler(int i) = 0;

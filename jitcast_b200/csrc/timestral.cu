@@ -299,12 +299,12 @@ TsPlan* get_plan(TimestralEngine& e, TsDevice& dv, int rows, int enc, int h, int
     }
   }
   while (static_cast<int>(dv.plans.size()) >= std::max(1, e.max_plans)) dv.plans.pop_back();
-  auto p = make_plan(e, rows, enc, h, ll, cov);
+  auto p = e.take_plan_failure() ? nullptr : make_plan(e, rows, enc, h, ll, cov);
   if (!p && !dv.plans.empty()) {
     // out of memory: drop the cached plans and retry once (PlanCache.run, PlanCache.java:70-100)
     cudaStreamSynchronize(dv.stream);
     dv.plans.clear();
-    p = make_plan(e, rows, enc, h, ll, cov);
+    p = e.take_plan_failure() ? nullptr : make_plan(e, rows, enc, h, ll, cov);
   }
   if (!p) {
     *err = "out of device memory for a plan of " + std::to_string(rows) + " rows";
@@ -581,6 +581,10 @@ TsEnds ends_params(const TimestralEngine& e, const jc_timestral_window* w, int r
 // quantiles.
 jc_status run_shard(TimestralEngine& e, TsDevice& dv, const jc_timestral_block* b, int r0, int r1, float* raw_out,
                     bool host, cudaStream_t stream, std::string* err, const jc_timestral_window* ends = nullptr) {
+  if (e.take_slot_failure(dv.slot)) {  // injected (engine option fail_slot), before any device work
+    *err = "injected shard failure (engine option fail_slot)";
+    return JC_ERR_CUDA;
+  }
   if (cudaSetDevice(dv.device) != cudaSuccess) {
     *err = "cannot select device " + std::to_string(dv.device);
     return JC_ERR_CUDA;
@@ -764,6 +768,7 @@ jc_status jc_engine_create_timestral(const jc_timestral_desc* desc, const jc_ten
       return fail_cuda(cudaGetLastError(), "engine device setup");
     std::string err;
     if (!upload_weights(*e, hw, *dv, &err)) return fail(JC_ERR_OOM, err);
+    dv->slot = static_cast<int>(e->devs.size());
     e->devs.push_back(std::move(dv));
   }
   *out = e.release();
@@ -795,7 +800,7 @@ jc_status jc_forward_timestral(jc_engine* engine, const jc_timestral_block* bloc
   }
   for (int i = 0; i < parts; ++i)
     if (status[i] != JC_OK)
-      return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+      return fail(status[i], "slot " + std::to_string(i) + " (GPU " + std::to_string(e->devs[i]->device) + "): " + errs[i]);
   return JC_OK;
 }
 
@@ -840,7 +845,7 @@ jc_status jc_forecast_timestral(jc_engine* engine, const jc_timestral_window* bl
   }
   for (int i = 0; i < parts; ++i)
     if (status[i] != JC_OK)
-      return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+      return fail(status[i], "slot " + std::to_string(i) + " (GPU " + std::to_string(e->devs[i]->device) + "): " + errs[i]);
   return JC_OK;
 }
 

@@ -1410,11 +1410,11 @@ TxPlan* get_plan(Tirex2Engine& e, TxDevice& dv, int rows, int nk, int nv, std::s
     }
   }
   while (static_cast<int>(dv.plans.size()) >= std::max(1, e.max_plans)) dv.plans.pop_back();
-  auto p = make_plan(e, rows, nk, nv);
+  auto p = e.take_plan_failure() ? nullptr : make_plan(e, rows, nk, nv);
   if (!p && !dv.plans.empty()) {
     cudaStreamSynchronize(dv.stream);
     dv.plans.clear();
-    p = make_plan(e, rows, nk, nv);
+    p = e.take_plan_failure() ? nullptr : make_plan(e, rows, nk, nv);
   }
   if (!p) {
     *err = "out of device memory for a plan of " + std::to_string(rows) + " rows";
@@ -1720,6 +1720,10 @@ ShardLists shard_lists(const jc_tirex2_batch* b, int r0, int r1) {
 
 jc_status run_shard(Tirex2Engine& e, TxDevice& dv, const jc_tirex2_batch* b, int r0, int r1, float* out, bool host,
                     cudaStream_t stream, std::string* err) {
+  if (e.take_slot_failure(dv.slot)) {  // injected (engine option fail_slot), before any device work
+    *err = "injected shard failure (engine option fail_slot)";
+    return JC_ERR_CUDA;
+  }
   if (cudaSetDevice(dv.device) != cudaSuccess) {
     *err = "cannot select device " + std::to_string(dv.device);
     return JC_ERR_CUDA;
@@ -1889,6 +1893,7 @@ jc_status jc_engine_create_tirex2(const jc_tirex2_desc* desc, const jc_tensor_vi
       return fail_cuda(cudaGetLastError(), "mLSTM / sLSTM kernel setup");
     std::string err;
     if (!upload(*e, hw, *dv, &err)) return fail(JC_ERR_OOM, err);
+    dv->slot = static_cast<int>(e->devs.size());
     e->devs.push_back(std::move(dv));
   }
   *out = e.release();
@@ -1930,7 +1935,7 @@ jc_status jc_forward_tirex2(jc_engine* engine, const jc_tirex2_batch* batch, flo
     for (auto& t : th) t.join();
   }
   for (int i = 0; i < parts; ++i)
-    if (status[i] != JC_OK) return fail(status[i], "GPU " + std::to_string(e->devs[i]->device) + ": " + errs[i]);
+    if (status[i] != JC_OK) return fail(status[i], "slot " + std::to_string(i) + " (GPU " + std::to_string(e->devs[i]->device) + "): " + errs[i]);
   return JC_OK;
 }
 

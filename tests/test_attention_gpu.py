@@ -131,3 +131,18 @@ def test_encoder_longer_than_the_tile(jc):
     exp = reference(torch, c, rows, n, heads, 0.125, 0, torch.float16)
     got = run(torch, c, rows, n, heads, 0.125, 0, "fp16")
     assert rel_err(got, exp) < TOL["fp16"]
+
+
+@pytest.mark.parametrize("n,enc", [(64, 60), (129, 128), (130, 128), (136, 128), (131, 125)])
+@pytest.mark.parametrize("prec", ["fp16", "bf16"])
+def test_timestral_layout_many_rows(jc, n, enc, prec):
+    # the Timestral layout (mask mode 0) over many rows and heads, known rows and key gaps included: 1 to 8 decoder
+    # queries past the MMA tile, an encoder that is not a multiple of 16, a row shorter than the tile
+    torch = pytest.importorskip("torch")
+    rows, heads = 150, 8
+    c = make_case(torch, rows, n, heads, 0, seed=n + enc, enc=enc)
+    exp = reference(torch, c, rows, n, heads, 0.125, 0, getattr(torch, PREC[prec][1]))
+    got = run(torch, c, rows, n, heads, 0.125, 0, prec)
+    err = rel_err(got, exp)
+    print(f"timestral layout n={n} enc={enc} {prec}: rel max err {err:.2e}")
+    assert err < TOL[prec], f"n={n} enc={enc} {prec}: rel max err {err:.3e}"
