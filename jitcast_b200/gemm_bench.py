@@ -5,7 +5,8 @@
 
 Prints one JSON line: milliseconds per call (CUDA events on the launching stream after warm-up),
 achieved TFLOP/s, and the algorithmic bytes per call (A, W, C written, C read when accumulating).
-``--cublas`` adds the same shape through torch.matmul (cuBLAS) for comparison; ``--single`` keeps the GEMM on
+``--cublas`` adds the same shape through cuBLAS as the reference calls it (torch.mm / torch.addmm with 16-bit
+operands and an FP32 C) for comparison; ``--single`` keeps the GEMM on
 the single-CTA kernel (large shapes otherwise run on CTA pairs). BASELINE config 1 is
 ``--m 1024 --n 768 --k 256 --epilogue bias``.
 """
@@ -88,8 +89,13 @@ def main(argv=None) -> int:
            "us": ms * 1e3, "tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
            "algorithmic_bytes": bytes_, "gbs": bytes_ / (ms * 1e-3) / 1e9}
     if args.cublas and dt != torch.float32:
-        cb = torch.empty(m, n, device=dev, dtype=dt)
-        mc = timed(lambda: torch.matmul(a[:, :k], w[:, :k].t(), out=cb))
+        # the reference's cuBLAS call: 16-bit operands, an FP32 C, β = 1 when accumulating (cublasGemmEx FP16 → FP32,
+        # timestral/tornado/TimestralForward.java:483-492)
+        cb = torch.zeros(m, n, device=dev, dtype=torch.float32)
+        if flags & _lib.ACCUMULATE:
+            mc = timed(lambda: torch.addmm(cb, a[:, :k], w[:, :k].t(), out_dtype=torch.float32, out=cb))
+        else:
+            mc = timed(lambda: torch.mm(a[:, :k], w[:, :k].t(), out_dtype=torch.float32, out=cb))
         out["cublas_ms"] = mc
         out["cublas_tflops"] = 2.0 * m * n * k / (mc * 1e-3) / 1e12
     print(json.dumps(out), flush=True)
