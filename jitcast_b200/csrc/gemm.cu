@@ -19,6 +19,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <type_traits>
 
 namespace jc {
 
@@ -201,9 +202,8 @@ __device__ __forceinline__ void store_operand(const EpiParams& p, long long off,
   }
 }
 
-// Bias → activation → accumulate → stores, for one row's 32-column chunk.
-__device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int orow, int col0, int nv,
-                                                float (&v)[32], float& sq) {
+// Row scale → bias → activation, for one row's 32-column chunk.
+__device__ __forceinline__ void epi_act_chunk(const EpiParams& p, int row, int col0, int nv, float (&v)[32]) {
   if (p.row_scale) {
     const float s = p.row_scale[row];
 #pragma unroll
@@ -234,36 +234,146 @@ __device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int
     default:
       break;
   }
-  if (p.accumulate) {
-    const float* src = p.cin + (long long)orow * p.ldcin + col0;
-    if (nv == 32 && p.vec_ok == 2) {
-      float c[32];
+}
+
+// 32 (or nv) fp32 values of a row from src: every pointer and pitch of the epilogue allows `vec` (2: 32-byte, 1:
+// 16-byte vectors, 0: scalar).
+__device__ __forceinline__ void load_row32(const float* src, int nv, int vec, float (&c)[32]) {
+  if (nv == 32 && vec == 2) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) ld8_f32(src + 8 * q, c + 8 * q);
+    for (int q = 0; q < 4; ++q) ld8_f32(src + 8 * q, c + 8 * q);
+  } else if (nv == 32 && vec == 1) {
+    const float4* s4 = reinterpret_cast<const float4*>(src);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] += c[j];
-    } else if (nv == 32 && p.vec_ok == 1) {
-      const float4* s4 = reinterpret_cast<const float4*>(src);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 c = s4[q];
-        v[4 * q] += c.x;
-        v[4 * q + 1] += c.y;
-        v[4 * q + 2] += c.z;
-        v[4 * q + 3] += c.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < nv) v[j] += src[j];
+    for (int q = 0; q < 8; ++q) {
+      const float4 x = s4[q];
+      c[4 * q] = x.x, c[4 * q + 1] = x.y, c[4 * q + 2] = x.z, c[4 * q + 3] = x.w;
     }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) c[j] = j < nv ? src[j] : 0.0f;
   }
+}
+
+// The FP32 store, the operand-typed copy and Σv², for one row's 32-column chunk.
+__device__ __forceinline__ void epi_store_chunk(const EpiParams& p, int orow, int col0, int nv, const float (&v)[32],
+                                                float& sq) {
   if (p.c) store_f32(p.c + (long long)orow * p.ldc + col0, nv, p.vec_ok, v);
   if (p.o_kind != kOutNone) store_operand(p, (long long)orow * p.ldo + col0, nv, v);
   if (p.rowsq) {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (j < nv) sq += v[j] * v[j];
+  }
+}
+
+// Bias → activation → accumulate → stores, for one row's 32-column chunk.
+__device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int orow, int col0, int nv,
+                                                float (&v)[32], float& sq) {
+  epi_act_chunk(p, row, col0, nv, v);
+  if (p.accumulate) {
+    float c[32];
+    load_row32(p.cin + (long long)orow * p.ldcin + col0, nv, p.vec_ok, c);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] += c[j];
+  }
+  epi_store_chunk(p, orow, col0, nv, v, sq);
+}
+
+// Two 32-column chunks of the thread's accumulator row with a single wait, so their TMEM latencies overlap.
+__device__ __forceinline__ void load_chunk_pair(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(ta, ra);
+  tmem_ld_32x32b_x32(tb, rb);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    a[j] = __uint_as_float(ra[j]);
+    b[j] = __uint_as_float(rb[j]);
+  }
+}
+
+__device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(taddr, r);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// The residual epilogue (plain mode, += C) with the residual read early: each thread's residual for the first
+// 64-column unit of its row in a tile goes into registers BEFORE the epilogue waits for the tile's accumulator, so
+// those reads overlap the tile's MMAs; a later unit's residual is read together with its accumulator chunks,
+// instead of after them.
+struct ResidualPre {
+  float a[32], b[32];  // the thread's row in its first 64-column unit of the tile
+};
+
+// The residual-preloading epilogue covers the residual GEMMs (a layer's output projection into the residual
+// stream): plain mode, += C into an FP32 C, an optional bias, no activation, no operand-typed copy, no row scale or
+// Σv². Their only registers are the accumulator and residual chunks (the 10-warp CTA gives each thread 168).
+__host__ __device__ __forceinline__ bool residual_preloaded(const EpiParams& p) {
+  return p.mode == kEpiPlain && p.accumulate && p.c && p.act == kActNone && p.o_kind == kOutNone && !p.row_scale &&
+         !p.rowsq;
+}
+
+__device__ __forceinline__ int out_row(const EpiParams& p, int row) {
+  const int rr = row % p.rg;
+  return (row / p.rg) * p.rg_stride + rr + p.rg_off + (rr >= p.rg_split ? p.rg_shift : 0);
+}
+
+// The residual of the thread's first unit (columns n0 + 64·half ..), into registers.
+__device__ __forceinline__ void residual_preload(const EpiParams& p, int M, int N, int m0, int n0, int row_in_tile,
+                                                 int half, ResidualPre& r) {
+  const int row = m0 + row_in_tile;
+  const int col0 = n0 + 64 * half;
+  if (row >= M || col0 >= N) return;
+  const float* src = p.cin + (long long)out_row(p, row) * p.ldcin + col0;
+  load_row32(src, min(32, N - col0), p.vec_ok, r.a);
+  load_row32(src + 32, col0 + 32 < N ? min(32, N - col0 - 32) : 0, p.vec_ok, r.b);
+}
+
+// One 32-column chunk of the residual epilogue: + bias, += the residual, the FP32 store.
+__device__ __forceinline__ void residual_chunk(const EpiParams& p, int orow, int col0, int nv, float (&v)[32],
+                                               const float (&r)[32]) {
+  if (p.bias_on) add_bias(p, col0, nv, v);
+#pragma unroll
+  for (int k = 0; k < 32; ++k) v[k] += r[k];
+  store_f32(p.c + (long long)orow * p.ldc + col0, nv, p.vec_ok, v);
+}
+
+// epilogue_tile for the residual epilogue, a 32-column chunk at a time: the first unit's residual is already in
+// registers; each later chunk's residual is read together with its accumulator chunk rather than after it.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile_residual(const EpiParams& p, int M, int N, int m0, int n0,
+                                                       uint32_t tbase, int row_in_tile, int half,
+                                                       const ResidualPre& r) {
+  const int row = m0 + row_in_tile;
+  const bool live = row < M;
+  const int orow = live ? out_row(p, row) : 0;
+  const int c0 = n0 + 64 * half;
+  if (64 * half < BN && c0 < N) {  // warp-uniform
+    float v[32];
+    load_chunk(tbase + 64 * half, v);
+    if (live) residual_chunk(p, orow, c0, min(32, N - c0), v, r.a);
+    if (c0 + 32 < N) {
+      load_chunk(tbase + 64 * half + 32, v);
+      if (live) residual_chunk(p, orow, c0 + 32, min(32, N - c0 - 32), v, r.b);
+    }
+  }
+#pragma unroll 1
+  for (int u = half + 2; u < BN / 64; u += 2) {
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = n0 + 64 * u + 32 * c;
+      if (col0 >= N) break;  // warp-uniform
+      const int nv = min(32, N - col0);
+      float rv[32];
+      if (live) load_row32(p.cin + (long long)orow * p.ldcin + col0, nv, p.vec_ok, rv);
+      float v[32];
+      load_chunk(tbase + 64 * u + 32 * c, v);
+      if (live) residual_chunk(p, orow, col0, nv, v, rv);
+    }
   }
 }
 
@@ -292,27 +402,6 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams& p, int M, int
       const int col0 = n0 + 64 * u + 32 * c;
       if (col0 < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + col0));
     }
-}
-
-// Two 32-column chunks of the thread's accumulator row with a single wait, so their TMEM latencies overlap.
-__device__ __forceinline__ void load_chunk_pair(uint32_t ta, uint32_t tb, float (&a)[32], float (&b)[32]) {
-  uint32_t ra[32], rb[32];
-  tmem_ld_32x32b_x32(ta, ra);
-  tmem_ld_32x32b_x32(tb, rb);
-  tmem_ld_wait();
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    a[j] = __uint_as_float(ra[j]);
-    b[j] = __uint_as_float(rb[j]);
-  }
-}
-
-__device__ __forceinline__ void load_chunk(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  tmem_ld_32x32b_x32(taddr, r);
-  tmem_ld_wait();
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
 }
 
 // One accumulator tile (rows m0.., columns n0..) → HBM, for the thread's row. The tile's columns are
@@ -483,7 +572,9 @@ struct GemmGroup {
 };
 
 // ---- the kernel -----------------------------------------------------------------------------
-template <int BN, int OPK, int G>
+// RESID: the launch's one problem is a residual GEMM (residual_preloaded): its epilogue loop reads the residual
+// early. A separate instantiation, so the other kernels keep their register allocation.
+template <int BN, int OPK, int G, bool RESID>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ GemmGroup<G> grp, uint32_t* err) {
   using C = Cfg<BN, OPK>;
@@ -689,34 +780,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
-    int it = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
-      const int buf = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      int lt;
-      const GemmProblem& P = grp.of(t, lt);
-      const int m0 = (lt / P.n_blks) * C::BM, n0 = (lt % P.n_blks) * BN;
-      prefetch_residual<BN>(P.ep, P.M, P.N, m0, n0, row_in_tile, half);
-      const bool got = mbar_wait(acc_full + buf, aph);
-      const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
-      if (!all) {
-        if (lane == 0) atomicOr(err, kErrTimeoutAcc);
-        *abort_flag = 1;
-        break;
+    // the residual-preloading loop for a residual GEMM (RESID), else the general one
+    auto loop = [&](auto pre_tag) {
+      constexpr bool PRE = decltype(pre_tag)::value;
+      int it = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        int lt;
+        const GemmProblem& P = grp.of(t, lt);
+        const int m0 = (lt / P.n_blks) * C::BM, n0 = (lt % P.n_blks) * BN;
+        ResidualPre rp;
+        if constexpr (PRE)
+          residual_preload(P.ep, P.M, P.N, m0, n0, row_in_tile, half, rp);
+        else
+          prefetch_residual<BN>(P.ep, P.M, P.N, m0, n0, row_in_tile, half);
+        const bool got = mbar_wait(acc_full + buf, aph);
+        const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
+        if (!all) {
+          if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        // the next tile's residual / table lines, a whole epilogue ahead of their use
+        const int tn = t + gridDim.x;
+        if (tn < tiles) {
+          int ln;
+          const GemmProblem& Q = grp.of(tn, ln);
+          prefetch_residual<BN>(Q.ep, Q.M, Q.N, (ln / Q.n_blks) * C::BM, (ln % Q.n_blks) * BN, row_in_tile, half);
+        }
+        const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+        if constexpr (PRE)
+          epilogue_tile_residual<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half, rp);
+        else
+          epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half);
+        tc_fence_before();
+        mbar_arrive(acc_empty + buf);
       }
-      tc_fence_after();
-      // the next tile's residual / table lines, a whole epilogue ahead of their use
-      const int tn = t + gridDim.x;
-      if (tn < tiles) {
-        int ln;
-        const GemmProblem& Q = grp.of(tn, ln);
-        prefetch_residual<BN>(Q.ep, Q.M, Q.N, (ln / Q.n_blks) * C::BM, (ln % Q.n_blks) * BN, row_in_tile, half);
-      }
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half);
-      tc_fence_before();
-      mbar_arrive(acc_empty + buf);
-    }
+    };
+    if constexpr (RESID)
+      loop(std::true_type{});
+    else
+      loop(std::false_type{});
   }
   tc_fence_before();
   __syncthreads();
@@ -735,39 +841,49 @@ __global__ void __launch_bounds__(kThreads, 1)
 // flight instead of four 48 KB ones. Both CTAs' TMA loads complete on CTA 0's stage barrier (armed by CTA
 // 0 for both CTAs' bytes); CTA 0's commits arrive on both CTAs' stage-free and accumulator-ready barriers;
 // each CTA's epilogue warps release an accumulator with one arrive on CTA 0's barrier. No TMA multicast.
-template <int OPK_>
+// WIDE: 256 × 512 tiles, two N = 256 MMAs per K step into one 512-column accumulator. A row block is then read
+// from L2 once per 512 output columns instead of once per 256, 25 % fewer operand bytes per FLOP on the L2 → SM
+// path that bounds this kernel; with TMEM full, the next tile's MMAs wait for the epilogue, while the TMA
+// producer keeps filling the stages. Otherwise 256 × 256 tiles with two accumulators.
+template <int OPK_, bool WIDE_ = false>
 struct CfgPair {
   static constexpr int OPK = OPK_;
-  static constexpr int BN = 256;  // tile N; each CTA stages BN / 2 rows of W
-  static constexpr int BM = 128;  // rows per CTA; the tile is 2 · BM rows
+  static constexpr bool WIDE = WIDE_;
+  static constexpr int BN = WIDE ? 512 : 256;  // tile N; each CTA stages BN / 2 rows of W, in 128-row chunks
+  static constexpr int BM = 128;               // rows per CTA; the tile is 2 · BM rows
+  static constexpr int MMA_N = 256;            // N of one tcgen05.mma; BN / MMA_N of them per K step
+  static constexpr int NMMA = BN / MMA_N;
   static constexpr int ESZ = (OPK == kOpBF16 || OPK == kOpF16) ? 2 : 4;
   static constexpr int BK = 128 / ESZ;
   static constexpr int UK = 32 / ESZ;
   static constexpr int NSUB = BK / UK;
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = (BN / 2) * 128;
+  static constexpr int B_CHUNK = (MMA_N / 2) * 128;  // this CTA's 128 W rows of one MMA
+  static constexpr int B_BYTES = NMMA * B_CHUNK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 6;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = WIDE ? 4 : 6;
+  static constexpr int NACC = WIDE ? 1 : 2;  // accumulators of BN columns in the 512 TMEM columns
+  static constexpr int TMEM_COLS = 512;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
-  static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : OPK == kOpF16 ? 0u : 2u, 2 * BM, BN);
+  static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : OPK == kOpF16 ? 0u : 2u, 2 * BM, MMA_N);
   static_assert(OPK != kOpSplit, "the split FP32 mode runs on the single-CTA kernel");
   static_assert(SMEM <= 200 * 1024, "shared memory");
+  static_assert(NACC * BN == TMEM_COLS, "TMEM columns");
 };
 
-template <int OPK, int G>
+template <int OPK, int G, bool WIDE, bool RESID>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ GemmGroup<G> grp, uint32_t* err) {
-  using C = CfgPair<OPK>;
+  using C = CfgPair<OPK, WIDE>;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + C::NACC;
+  uint64_t* drain = acc_empty + C::NACC;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile uint32_t* abort_flag = tmem_holder + 1;
 
@@ -782,7 +898,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(full + s, 1);
       mbar_init(empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::NACC; ++b) {
       mbar_init(acc_full + b, 1);
       mbar_init(acc_empty + b, 2 * kEpiWarps);
     }
@@ -816,7 +932,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int lt;
         const GemmProblem& P = grp.of(t, lt);
         const int m0 = (lt / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM;
-        const int n0 = (lt % P.n_blks) * BN + static_cast<int>(rank) * (BN / 2);
+        // this CTA's 128 W rows of each MMA: rows n_tile + 256·j + 128·rank
+        const int n0 = (lt % P.n_blks) * BN + static_cast<int>(rank) * (C::MMA_N / 2);
         for (int kb = 0; kb < P.kblks; ++kb) {
           if (!mbar_wait(empty + stage, phase ^ 1) || *abort_flag) {
             atomicOr(err, kErrTimeoutEmpty);
@@ -827,7 +944,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * C::STAGE_BYTES;
           if (leader) mbar_arrive_expect_tx(full + stage, 2 * C::STAGE_BYTES);
           tma_load_2d_pair(sa, &P.a, full0 + 8 * stage, kb * C::BK, m0);
-          tma_load_2d_pair(sa + C::A_BYTES, &P.w, full0 + 8 * stage, kb * C::BK, n0);
+#pragma unroll
+          for (int j = 0; j < C::NMMA; ++j)
+            tma_load_2d_pair(sa + C::A_BYTES + j * C::B_CHUNK, &P.w, full0 + 8 * stage, kb * C::BK,
+                             n0 + j * C::MMA_N);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1;
@@ -845,8 +965,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = pair; t < tiles && ok; t += pairs, ++it) {
         int lt;
         const int kblks = grp.of(t, lt).kblks;
-        const int buf = it & 1;
-        const uint32_t aph = (it >> 1) & 1;
+        const int buf = it % C::NACC;
+        const uint32_t aph = (it / C::NACC) & 1;
         if (!mbar_wait(acc_empty + buf, aph ^ 1) || *abort_flag) {
           atomicOr(err, kErrTimeoutAccFree);
           *abort_flag = 1;
@@ -868,12 +988,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < C::NSUB; ++k) {
             const uint64_t ad = sdesc_k_sw128(sa + 32 * k);
-            const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
             const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            if (OPK == kOpTF32)
-              umma_tf32_pair(d, ad, bd, C::IDESC, acc);
-            else
-              umma_f16_pair(d, ad, bd, C::IDESC, acc);
+#pragma unroll
+            for (int j = 0; j < C::NMMA; ++j) {
+              const uint64_t bd = sdesc_k_sw128(sb + j * C::B_CHUNK + 32 * k);
+              if (OPK == kOpTF32)
+                umma_tf32_pair(d + j * C::MMA_N, ad, bd, C::IDESC, acc);
+              else
+                umma_f16_pair(d + j * C::MMA_N, ad, bd, C::IDESC, acc);
+            }
           }
           umma_commit_pair_multicast(empty + stage, 0x3);
           if (++stage == C::STAGES) {
@@ -894,35 +1017,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
-    int it = 0;
-    for (int t = pair; t < tiles; t += pairs, ++it) {
-      const int buf = it & 1;
-      const uint32_t aph = (it >> 1) & 1;
-      int lt;
-      const GemmProblem& P = grp.of(t, lt);
-      const int m0 = (lt / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (lt % P.n_blks) * BN;
-      prefetch_residual<BN>(P.ep, P.M, P.N, m0, n0, row_in_tile, half);
-      const bool got = mbar_wait(acc_full + buf, aph);
-      const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
-      if (!all) {
-        if (lane == 0) atomicOr(err, kErrTimeoutAcc);
-        *abort_flag = 1;
-        break;
+    // as in the single-CTA kernel: the residual-preloading loop for a residual GEMM (RESID), else the general one
+    auto loop = [&](auto pre_tag) {
+      constexpr bool PRE = decltype(pre_tag)::value;
+      int it = 0;
+      for (int t = pair; t < tiles; t += pairs, ++it) {
+        const int buf = it % C::NACC;
+        const uint32_t aph = (it / C::NACC) & 1;
+        int lt;
+        const GemmProblem& P = grp.of(t, lt);
+        const int m0 = (lt / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (lt % P.n_blks) * BN;
+        ResidualPre rp;
+        if constexpr (PRE)
+          residual_preload(P.ep, P.M, P.N, m0, n0, row_in_tile, half, rp);
+        else
+          prefetch_residual<BN>(P.ep, P.M, P.N, m0, n0, row_in_tile, half);
+        const bool got = mbar_wait(acc_full + buf, aph);
+        const bool all = __all_sync(0xffffffffu, got) && !*abort_flag;
+        if (!all) {
+          if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const int tn = t + pairs;
+        if (tn < tiles) {
+          int ln;
+          const GemmProblem& Q = grp.of(tn, ln);
+          prefetch_residual<BN>(Q.ep, Q.M, Q.N, (ln / Q.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM,
+                                (ln % Q.n_blks) * BN, row_in_tile, half);
+        }
+        const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+        if constexpr (PRE)
+          epilogue_tile_residual<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half, rp);
+        else
+          epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
       }
-      tc_fence_after();
-      const int tn = t + pairs;
-      if (tn < tiles) {
-        int ln;
-        const GemmProblem& Q = grp.of(tn, ln);
-        prefetch_residual<BN>(Q.ep, Q.M, Q.N, (ln / Q.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM,
-                              (ln % Q.n_blks) * BN, row_in_tile, half);
-      }
-      const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-      epilogue_tile<BN>(P.ep, P.M, P.N, m0, n0, tbase, row_in_tile, half);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
-    }
+    };
+    if constexpr (RESID)
+      loop(std::true_type{});
+    else
+      loop(std::false_type{});
   }
   tc_fence_before();
   __syncthreads();
@@ -987,10 +1125,10 @@ EpiParams epi_default() {
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Tile widths (bit 0: 64, bit 1: 128, bit 2: 256) that keep heads and the gate split whole.
+// Tile widths (bit 0: 64, bit 1: 128, bit 2: 256, bit 3: 512) that keep heads and the gate split whole.
 static int qkv_tile_choices(const EpiParams& e) {
   int bits = 0, i = 0;
-  for (int bn : {64, 128, 256}) {
+  for (int bn : {64, 128, 256, 512}) {
     const bool heads_ok = e.rope_cols == 0 || bn % e.head_dim == 0;
     if (heads_ok && e.n_split % bn == 0) bits |= 1 << i;
     ++i;
@@ -1016,7 +1154,7 @@ const char* check_gemm(const GemmArgs& g) {
     if (e.rope_cols > 0 && (!e.pos || !e.rope_table)) return "fused RoPE needs positions and a table";
     if (e.n_split % 64 != 0) return "the gate columns must start on a 64-column boundary";
     if (g.N > e.n_split && !e.g_out) return "gate columns without a gate output";
-    if (qkv_tile_choices(e) == 0) return "no tile width fits the q|k|v|gate layout";
+    if ((qkv_tile_choices(e) & 7) == 0) return "no tile width fits the q|k|v|gate layout";
   }
   if (e.accumulate && !e.cin) return "accumulate without C input";
   if (e.bias_on && !e.bias) return "bias flag without bias";
@@ -1056,38 +1194,48 @@ static bool build_group(GemmGroup<G>& grp, const GemmArgs* g, int count, int bm,
   return true;
 }
 
-template <int BN, int OPK, int G>
-static cudaError_t launch_cfg(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
+template <int BN, int OPK, int G, bool RESID>
+static cudaError_t launch_cfg_r(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
   using C = Cfg<BN, OPK>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemm_tc_kernel<BN, OPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        cudaFuncSetAttribute(gemm_tc_kernel<BN, OPK, G, RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
   GemmGroup<G> grp;
   if (!build_group(grp, g, count, C::BM, BN, C::BM, BN)) return cudaErrorInvalidValue;
   const int grid = grp.tiles < num_sms ? grp.tiles : num_sms;
-  gemm_tc_kernel<BN, OPK, G><<<grid, kThreads, C::SMEM, stream>>>(grp, err);
+  gemm_tc_kernel<BN, OPK, G, RESID><<<grid, kThreads, C::SMEM, stream>>>(grp, err);
   return cudaGetLastError();
 }
 
-template <int OPK, int G>
-static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
-  using C = CfgPair<OPK>;
+// A single residual GEMM (not the split mode, whose epilogue drains K slabs) runs the RESID instantiation.
+template <int BN, int OPK, int G>
+static cudaError_t launch_cfg(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
+  if constexpr (G == 1 && OPK != kOpSplit) {
+    if (residual_preloaded(g[0].ep)) return launch_cfg_r<BN, OPK, G, true>(g, count, stream, err, num_sms);
+  }
+  return launch_cfg_r<BN, OPK, G, false>(g, count, stream, err, num_sms);
+}
+
+template <int OPK, int G, bool WIDE, bool RESID>
+static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
+  using C = CfgPair<OPK, WIDE>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK, G, WIDE, RESID>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
   GemmGroup<G> grp;
-  if (!build_group(grp, g, count, 2 * C::BM, C::BN, C::BM, C::BN / 2)) return cudaErrorInvalidValue;
+  if (!build_group(grp, g, count, 2 * C::BM, C::BN, C::BM, C::MMA_N / 2)) return cudaErrorInvalidValue;
   const int pairs = grp.tiles < num_sms / 2 ? grp.tiles : num_sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
@@ -1101,7 +1249,25 @@ static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK, G>, grp, err);
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK, G, WIDE, RESID>, grp, err);
+}
+
+template <int OPK, int G, bool WIDE>
+static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
+  if constexpr (G == 1) {
+    if (residual_preloaded(g[0].ep)) return launch_pair_r<OPK, G, WIDE, true>(g, count, stream, err, num_sms);
+  }
+  return launch_pair_r<OPK, G, WIDE, false>(g, count, stream, err, num_sms);
+}
+
+// JC_GEMM_WIDE=0 in the environment keeps the CTA-pair kernel on 256 × 256 tiles (for comparisons).
+static bool wide_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = std::getenv("JC_GEMM_WIDE");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
 }
 
 // JC_GEMM_PAIR=0 in the environment keeps every GEMM on the single-CTA kernel (for comparisons).
@@ -1128,7 +1294,7 @@ static int sm_count() {
 
 // Tile widths every problem of a launch allows (bit 0: 64, bit 1: 128, bit 2: 256).
 static int allowed_widths(const GemmArgs* g, int count) {
-  int allowed = 7;
+  int allowed = 15;
   for (int i = 0; i < count; ++i)
     if (g[i].ep.mode == kEpiQKV) allowed &= qkv_tile_choices(g[i].ep);
   return allowed;
@@ -1179,14 +1345,32 @@ static cudaError_t launch_group(GemmArgs* g, int count, cudaStream_t stream, uin
   // CTA pairs for the 16-bit and TF32 modes when the 256 × 256 tiles still give every SM pair work and the
   // tile width keeps the q|k|v|gate layout whole
   const int allowed = allowed_widths(g, count);
+  // 256 × 512 pair tiles for long K (≥ 2,048: the un-overlapped epilogue is then a small share of a tile; at
+  // K = 1,024 it costs more than the saved operand bytes) where every problem's N is a multiple of 512 and the
+  // tiles still give every SM pair one
+  if (pair_enabled() && wide_enabled() && op != kOpSplit && g[0].bn == 0 && ((allowed >> 3) & 1)) {
+    long long wtiles = 0;
+    bool fits = true;
+    for (int i = 0; i < count; ++i) {
+      fits = fits && g[i].N % 512 == 0 && g[i].K >= 2048;
+      wtiles += (long long)((g[i].M + 255) / 256) * (g[i].N / 512);
+    }
+    if (fits && wtiles >= sms / 2) {
+      switch (op) {
+        case kOpBF16: return launch_pair<kOpBF16, G, true>(g, count, stream, err, sms);
+        case kOpF16: return launch_pair<kOpF16, G, true>(g, count, stream, err, sms);
+        default: return launch_pair<kOpTF32, G, true>(g, count, stream, err, sms);
+      }
+    }
+  }
   if (pair_enabled() && op != kOpSplit && (g[0].bn == 0 || g[0].bn == 256) && ((allowed >> 2) & 1)) {
     long long ptiles = 0;
     for (int i = 0; i < count; ++i) ptiles += (long long)((g[i].M + 255) / 256) * ((g[i].N + 255) / 256);
     if (ptiles >= sms / 2) {
       switch (op) {
-        case kOpBF16: return launch_pair<kOpBF16, G>(g, count, stream, err, sms);
-        case kOpF16: return launch_pair<kOpF16, G>(g, count, stream, err, sms);
-        default: return launch_pair<kOpTF32, G>(g, count, stream, err, sms);
+        case kOpBF16: return launch_pair<kOpBF16, G, false>(g, count, stream, err, sms);
+        case kOpF16: return launch_pair<kOpF16, G, false>(g, count, stream, err, sms);
+        default: return launch_pair<kOpTF32, G, false>(g, count, stream, err, sms);
       }
     }
   }

@@ -63,7 +63,7 @@ static float round_half(float v) {
   const float a = fabsf(v);
   if (a < 6.103515625e-05f) { /* subnormal half: a multiple of 2^-24 */
     const double q = nearbyint((double)a * 16777216.0) / 16777216.0;
-    return (float)(v < 0 ? -q : q);
+    return copysignf((float)q, v);
   }
   return round_mantissa(v, 10);
 }

@@ -65,3 +65,40 @@ def test_sign_flip_complement():
     assert list(comp) == list(range(8, -1, -1))
     with pytest.raises(ValueError):
         ts.sign_flip_complement([0.1, 0.5, 0.8])
+
+
+def test_operand_rounding_matches_the_formats():
+    # oracle.operand_format (a reduced-precision run of the reference arithmetic): BF16 and FP16 rounding equal
+    # torch's conversions bit for bit over a wide range of magnitudes (FP16 saturating at ±65504, subnormals
+    # kept); TF32 equals round-to-nearest-even at 10 mantissa bits
+    import torch
+
+    L = oracle.lib()
+    rng = np.random.default_rng(0)
+    v = (rng.standard_normal(20000) * np.exp(rng.uniform(-22, 14, 20000))).astype(np.float32)
+    v[:4] = [0.0, -0.0, 65519.0, -70000.0]
+    for name, dt in (("bf16", torch.bfloat16), ("fp16", torch.float16)):
+        got = np.array([L.jco_round_operand(float(x), oracle.OPERAND_FORMATS[name]) for x in v], np.float32)
+        src = np.clip(v, -65504, 65504) if name == "fp16" else v
+        exp = torch.from_numpy(src).to(dt).float().numpy()
+        np.testing.assert_array_equal(got.view(np.uint32), exp.view(np.uint32))
+    u = v.view(np.uint32).astype(np.uint64)
+    exp = ((u + 0xFFF + ((u >> 13) & 1)) >> 13 << 13).astype(np.uint32).view(np.float32)
+    got = np.array([L.jco_round_operand(float(x), oracle.OPERAND_FORMATS["tf32"]) for x in v], np.float32)
+    np.testing.assert_array_equal(got.view(np.uint32), exp.view(np.uint32))
+
+
+def test_operand_format_rounds_every_linear_and_is_restored():
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((40, 96)).astype(np.float32)
+    w = rng.standard_normal((24, 96)).astype(np.float32)
+    exact = oracle.linear(x, w)
+    with oracle.operand_format("bf16"):
+        reduced = oracle.linear(x, w)
+    import torch
+
+    xb = torch.from_numpy(x).bfloat16().double().numpy()
+    wb = torch.from_numpy(w).bfloat16().double().numpy()
+    np.testing.assert_array_equal(reduced, (xb @ wb.T).astype(np.float32))
+    np.testing.assert_array_equal(oracle.linear(x, w), exact)  # the reference's arithmetic again
+    assert oracle.lib().jco_operand_format() == 0
