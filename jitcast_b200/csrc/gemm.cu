@@ -845,10 +845,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // from L2 once per 512 output columns instead of once per 256, 25 % fewer operand bytes per FLOP on the L2 → SM
 // path that bounds this kernel; with TMEM full, the next tile's MMAs wait for the epilogue, while the TMA
 // producer keeps filling the stages. Otherwise 256 × 256 tiles with two accumulators.
-template <int OPK_, bool WIDE_ = false>
+// RS > 0: the staged residual epilogue (RESID == 2 below) gives each epilogue warp a ring of RS shared-memory
+// slots of 32 rows × 32 FP32 columns (4 KB, 128-byte swizzle); the operand stages shrink to make room.
+template <int OPK_, bool WIDE_ = false, int RS_ = 0>
 struct CfgPair {
   static constexpr int OPK = OPK_;
   static constexpr bool WIDE = WIDE_;
+  static constexpr int RS = RS_;
   static constexpr int BN = WIDE ? 512 : 256;  // tile N; each CTA stages BN / 2 rows of W, in 128-row chunks
   static constexpr int BM = 128;               // rows per CTA; the tile is 2 · BM rows
   static constexpr int MMA_N = 256;            // N of one tcgen05.mma; BN / MMA_N of them per K step
@@ -861,31 +864,152 @@ struct CfgPair {
   static constexpr int B_CHUNK = (MMA_N / 2) * 128;  // this CTA's 128 W rows of one MMA
   static constexpr int B_BYTES = NMMA * B_CHUNK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = WIDE ? 4 : 6;
+  static constexpr int STAGES = WIDE ? (RS ? 3 : 4) : (RS ? 4 : 6);
   static constexpr int NACC = WIDE ? 1 : 2;  // accumulators of BN columns in the 512 TMEM columns
   static constexpr int TMEM_COLS = 512;
-  static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + BAR_BYTES + 1024;
+  static constexpr int SLOT_BYTES = 32 * 32 * 4;
+  static constexpr int RING_BYTES = kEpiWarps * RS * SLOT_BYTES;
+  static constexpr int BAR_BYTES = 256 + kEpiWarps * RS * 8;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + RING_BYTES + BAR_BYTES + 1024;
   static constexpr uint32_t IDESC = idesc_f32acc(OPK == kOpBF16 ? 1u : OPK == kOpF16 ? 0u : 2u, 2 * BM, MMA_N);
   static_assert(OPK != kOpSplit, "the split FP32 mode runs on the single-CTA kernel");
-  static_assert(SMEM <= 200 * 1024, "shared memory");
+  static_assert(SMEM <= 227 * 1024, "shared memory");
   static_assert(NACC * BN == TMEM_COLS, "TMEM columns");
 };
 
-template <int OPK, int G, bool WIDE, bool RESID>
+// One epilogue warp of the staged residual epilogue (RESID == 2) over the pair's tiles. The warp's chunks form
+// one sequence over its tiles: chunk k of a tile covers the warp's 32 rows (TMEM lanes 32·quarter ..) and the
+// columns n0 + 64·(half + 2·(k / 2)) + 32·(k % 2), k < BN / 64, as in the general epilogue. Chunk j lives in slot
+// j % RS; lane 0 loads chunk j + RS − 1 after chunk j has been stored, once chunk j − 1's store has read its slot
+// (one bulk group per chunk). A chunk outside the output (columns ≥ N or rows ≥ M) moves nothing: lane 0 completes
+// its slot's barrier phase with a plain arrival. P.a2 maps the residual C_in and P.w2 the output C, 32 × 32 boxes.
+template <class C>
+__device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, int pair, int pairs, int tiles,
+                                                         uint32_t rank, uint32_t tmem, uint64_t* acc_full,
+                                                         uint32_t acc_empty0, volatile uint32_t* abort_flag,
+                                                         uint32_t* err, uint8_t* ring, uint64_t* rbar, int quarter,
+                                                         int half, int lane) {
+  constexpr int BN = C::BN, RS = C::RS, KPT = BN / 64;
+  const int my_tiles = pair < tiles ? (tiles - pair + pairs - 1) / pairs : 0;
+  const int jobs = my_tiles * KPT;
+  const EpiParams& ep = P.ep;
+  // the chunk's column and row origin; false if it lies outside the output
+  auto where = [&](int j, int& col0, int& row0) {
+    const int t = pair + (j / KPT) * pairs, k = j % KPT;
+    row0 = (t / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM + quarter * 32;
+    col0 = (t % P.n_blks) * BN + 64 * (half + 2 * (k >> 1)) + 32 * (k & 1);
+    return col0 < P.N && row0 < P.M;
+  };
+  auto issue = [&](int j) {  // lane 0
+    uint64_t* bar = rbar + j % RS;
+    int col0, row0;
+    if (where(j, col0, row0)) {
+      mbar_arrive_expect_tx(bar, C::SLOT_BYTES);
+      tma_load_2d(ring + (j % RS) * C::SLOT_BYTES, &P.a2, bar, col0, row0);
+    } else {
+      mbar_arrive(bar);
+    }
+  };
+  int issued = 0;
+  if (lane == 0)
+    for (; issued < RS - 1 && issued < jobs; ++issued) issue(issued);
+  bool ok = true;
+  int j = 0;
+  for (int it = 0; it < my_tiles && ok; ++it) {
+    const int buf = it % C::NACC;
+    const bool got = mbar_wait(acc_full + buf, (it / C::NACC) & 1);
+    if (!(__all_sync(0xffffffffu, got) && !*abort_flag)) {
+      if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+      *abort_flag = 1;
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+#pragma unroll 1
+    for (int k = 0; k < KPT; ++k, ++j) {
+      int col0, row0;
+      const bool live = where(j, col0, row0);
+      const uint32_t slot = smem_u32(ring + (j % RS) * C::SLOT_BYTES);
+      uint32_t acc[32];
+      if (live) tmem_ld_32x32b_x32(tbase + 64 * (half + 2 * (k >> 1)) + 32 * (k & 1), acc);
+      const bool have = mbar_wait(rbar + j % RS, (j / RS) & 1);
+      if (!__all_sync(0xffffffffu, have)) {
+        if (live) tmem_ld_wait();
+        if (lane == 0) atomicOr(err, kErrTimeoutResidual);
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      if (live) {
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int q = 0; q < 32; ++q) v[q] = __uint_as_float(acc[q]);
+        if (ep.bias_on) add_bias(ep, col0, min(32, P.N - col0), v);
+        // the thread's row of the slot: 16-byte chunk q at q ^ (row % 8), the 128-byte swizzle
+        const uint32_t rowp = slot + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t a = rowp + ((q ^ (lane & 7)) << 4);
+          const float4 r = lds_f32x4(a);
+          sts_f32x4(a, make_float4(v[4 * q] + r.x, v[4 * q + 1] + r.y, v[4 * q + 2] + r.z, v[4 * q + 3] + r.w));
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) {
+        if (live) tma_store_2d(&P.w2, ring + (j % RS) * C::SLOT_BYTES, col0, row0);
+        bulk_commit();
+        if (issued < jobs) {
+          bulk_wait_read<1>();  // chunk j − 1's store has read the slot chunk j + RS − 1 reuses
+          issue(issued++);
+        }
+      }
+    }
+    if (!ok) break;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
+  }
+  if (lane == 0) {
+    // loads still in flight after an abort land before the CTA's shared memory is released
+    for (int q = j; q < issued; ++q) mbar_wait(rbar + q % RS, (q / RS) & 1);
+    bulk_wait<0>();
+  }
+  __syncwarp();
+}
+
+// Slots per epilogue warp of the staged residual ring: three with 256-wide tiles; two beside the wide tiles'
+// 48 KB stages.
+template <bool WIDE>
+constexpr int residual_slots() {
+  return WIDE ? 2 : 3;
+}
+
+// RESID: 0 the general epilogue; 1 a residual GEMM with the register-preloading epilogue; 2 a residual GEMM with
+// the staged epilogue. The staged epilogue moves the FP32 residual and the result by TMA: each epilogue warp
+// loads its 32 rows × 32 columns of the residual into a slot of its ring two chunks ahead (the next tile's first
+// chunks while the MMAs of that tile still run), adds the accumulator chunk and the bias in place, and stores the
+// slot back with one bulk-tensor store. The residual and the result thereby bypass the per-thread load and store
+// path, whose uncoalesced 32-row requests (one row per thread) kept the SM's L1 busy for most of the epilogue.
+template <int OPK, int G, bool WIDE, int RESID>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ GemmGroup<G> grp, uint32_t* err) {
-  using C = CfgPair<OPK, WIDE>;
+  using C = CfgPair<OPK, WIDE, RESID == 2 ? residual_slots<WIDE>() : 0>;
   constexpr int BN = C::BN;
+  static_assert(RESID != 2 || G == 1, "the staged residual epilogue serves single GEMMs");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* ring = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + C::RING_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* acc_full = empty + C::STAGES;
   uint64_t* acc_empty = acc_full + C::NACC;
   uint64_t* drain = acc_empty + C::NACC;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile uint32_t* abort_flag = tmem_holder + 1;
+  uint64_t* rbar = drain + 2;  // kEpiWarps × RS residual-slot barriers
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -903,11 +1027,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(acc_empty + b, 2 * kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < kEpiWarps * C::RS; ++i) mbar_init(rbar + i, 1);
     *abort_flag = 0;
     fence_mbar_init();
     for (int i = 0; i < grp.count; ++i) {
       prefetch_tmap(&grp.p[i].a);
       prefetch_tmap(&grp.p[i].w);
+      if constexpr (RESID == 2) {
+        prefetch_tmap(&grp.p[i].a2);
+        prefetch_tmap(&grp.p[i].w2);
+      }
     }
   }
   if (warp == 1) {
@@ -1057,7 +1186,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
       }
     };
-    if constexpr (RESID)
+    if constexpr (RESID == 2)
+      staged_residual_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
+                                  ring + (warp - 2) * C::RS * C::SLOT_BYTES, rbar + (warp - 2) * C::RS, quarter, half,
+                                  lane);
+    else if constexpr (RESID == 1)
       loop(std::true_type{});
     else
       loop(std::false_type{});
@@ -1222,9 +1355,9 @@ static cudaError_t launch_cfg(const GemmArgs* g, int count, cudaStream_t stream,
   return launch_cfg_r<BN, OPK, G, false>(g, count, stream, err, num_sms);
 }
 
-template <int OPK, int G, bool WIDE, bool RESID>
+template <int OPK, int G, bool WIDE, int RESID>
 static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
-  using C = CfgPair<OPK, WIDE>;
+  using C = CfgPair<OPK, WIDE, RESID == 2 ? residual_slots<WIDE>() : 0>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1236,6 +1369,13 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
   }
   GemmGroup<G> grp;
   if (!build_group(grp, g, count, 2 * C::BM, C::BN, C::BM, C::MMA_N / 2)) return cudaErrorInvalidValue;
+  if constexpr (RESID == 2) {
+    // the staged residual epilogue's 32 × 32 FP32 boxes of C_in (a2) and C (w2)
+    const GemmArgs& x = g[0];
+    if (!make_map(&grp.p[0].a2, x.ep.cin, kOpTF32, x.M, x.N, x.ep.ldcin, 32) ||
+        !make_map(&grp.p[0].w2, x.ep.c, kOpTF32, x.M, x.N, x.ep.ldc, 32))
+      return cudaErrorInvalidValue;
+  }
   const int pairs = grp.tiles < num_sms / 2 ? grp.tiles : num_sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
@@ -1252,12 +1392,32 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
   return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK, G, WIDE, RESID>, grp, err);
 }
 
+// JC_GEMM_STAGED=0 in the environment keeps residual GEMMs on the register-preloading epilogue (for comparisons).
+static bool staged_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = std::getenv("JC_GEMM_STAGED");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+// A residual GEMM whose C_in and C the staged epilogue can move by TMA: rows in place (no remap), 16-byte aligned
+// bases and pitches.
+static bool residual_staged_ok(const GemmArgs& g) {
+  const EpiParams& e = g.ep;
+  return staged_enabled() && residual_preloaded(e) && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0 &&
+         aligned16(e.cin) && aligned16(e.c) && e.ldcin % 4 == 0 && e.ldc % 4 == 0 && e.ldcin >= g.N &&
+         e.ldc >= g.N;
+}
+
 template <int OPK, int G, bool WIDE>
 static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
   if constexpr (G == 1) {
-    if (residual_preloaded(g[0].ep)) return launch_pair_r<OPK, G, WIDE, true>(g, count, stream, err, num_sms);
+    if (residual_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 2>(g, count, stream, err, num_sms);
+    if (residual_preloaded(g[0].ep)) return launch_pair_r<OPK, G, WIDE, 1>(g, count, stream, err, num_sms);
   }
-  return launch_pair_r<OPK, G, WIDE, false>(g, count, stream, err, num_sms);
+  return launch_pair_r<OPK, G, WIDE, 0>(g, count, stream, err, num_sms);
 }
 
 // JC_GEMM_WIDE=0 in the environment keeps the CTA-pair kernel on 256 × 256 tiles (for comparisons).

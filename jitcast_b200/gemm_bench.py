@@ -6,7 +6,8 @@
 Prints one JSON line: milliseconds per call (CUDA events on the launching stream after warm-up),
 achieved TFLOP/s, and the algorithmic bytes per call (A, W, C written, C read when accumulating).
 ``--cublas`` adds the same shape through cuBLAS as the reference calls it (torch.mm / torch.addmm with 16-bit
-operands and an FP32 C) for comparison; ``--single`` keeps the GEMM on
+operands and an FP32 C) for comparison; ``--rounds R`` alternates the two R times (``--iters`` calls each) and
+reports the median round of each, so that both see the same clocks; ``--single`` keeps the GEMM on
 the single-CTA kernel (large shapes otherwise run on CTA pairs). BASELINE config 1 is
 ``--m 1024 --n 768 --k 256 --epilogue bias``.
 """
@@ -30,6 +31,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--epilogue", default="plain", choices=["plain", "bias", "bias_silu", "accumulate"])
     ap.add_argument("--cublas", action="store_true")
+    ap.add_argument("--rounds", type=int, default=1, help="alternate ours and cuBLAS this many times (median)")
     ap.add_argument("--single", action="store_true", help="keep the GEMM on the single-CTA kernel")
     args = ap.parse_args(argv)
     if args.single:
@@ -80,24 +82,37 @@ def main(argv=None) -> int:
             torch.cuda.synchronize()
         return s.elapsed_time(e) / args.iters
 
-    ms = timed(call)
-    _lib.check(L.jc_device_sync(0))
+    cublas_fn = None
+    if args.cublas and dt != torch.float32:
+        # the reference's cuBLAS call: 16-bit operands, an FP32 C, β = 1 when accumulating (cublasGemmEx FP16 → FP32,
+        # timestral/tornado/TimestralForward.java:483-492)
+        cb = torch.zeros(m, n, device=dev, dtype=torch.float32)
+        if flags & _lib.ACCUMULATE:
+            cublas_fn = lambda: torch.addmm(cb, a[:, :k], w[:, :k].t(), out_dtype=torch.float32, out=cb)  # noqa: E731
+        else:
+            cublas_fn = lambda: torch.mm(a[:, :k], w[:, :k].t(), out_dtype=torch.float32, out=cb)  # noqa: E731
+    ours_ms, cublas_ms = [], []
+    for _ in range(max(1, args.rounds)):
+        ours_ms.append(timed(call))
+        _lib.check(L.jc_device_sync(0))
+        if cublas_fn is not None:
+            cublas_ms.append(timed(cublas_fn))
+    ms = float(np.median(ours_ms))
     esz = 2 if dt != torch.float32 else 4
     bytes_ = (m * k + n * k) * esz * (2 if args.precision == "fp32" else 1) + m * n * 4 * (
         2 if flags & _lib.ACCUMULATE else 1)
     out = {"m": m, "n": n, "k": k, "precision": args.precision, "epilogue": args.epilogue, "ms": ms,
            "us": ms * 1e3, "tflops": 2.0 * m * n * k / (ms * 1e-3) / 1e12,
            "algorithmic_bytes": bytes_, "gbs": bytes_ / (ms * 1e-3) / 1e9}
-    if args.cublas and dt != torch.float32:
-        # the reference's cuBLAS call: 16-bit operands, an FP32 C, β = 1 when accumulating (cublasGemmEx FP16 → FP32,
-        # timestral/tornado/TimestralForward.java:483-492)
-        cb = torch.zeros(m, n, device=dev, dtype=torch.float32)
-        if flags & _lib.ACCUMULATE:
-            mc = timed(lambda: torch.addmm(cb, a[:, :k], w[:, :k].t(), out_dtype=torch.float32, out=cb))
-        else:
-            mc = timed(lambda: torch.mm(a[:, :k], w[:, :k].t(), out_dtype=torch.float32, out=cb))
+    if cublas_ms:
+        mc = float(np.median(cublas_ms))
         out["cublas_ms"] = mc
         out["cublas_tflops"] = 2.0 * m * n * k / (mc * 1e-3) / 1e12
+        out["ours_over_cublas"] = mc / ms
+    if args.rounds > 1:
+        out["rounds"] = args.rounds
+        out["ours_ms_rounds"] = ours_ms
+        out["cublas_ms_rounds"] = cublas_ms
     print(json.dumps(out), flush=True)
     return 0
 

@@ -92,9 +92,12 @@ def test_device_buffers(jc, precision, m, n, k):
 @pytest.mark.parametrize("precision", ["tf32", "bf16", "fp16"])
 @pytest.mark.parametrize("m,n,k,flags", [(4133, 4160, 1000, 0),          # CTA-pair tiles, ragged M, N and K
                                          (8192, 1024, 4096, 2),          # residual add, long K
+                                         (9000, 1000, 1024, 2),          # residual add, ragged M and N
+                                         (20000, 200, 512, 1 | 2),       # bias + residual, N below one tile
                                          (19000, 768, 256, 1 | 4)])      # bias + SiLU, short K
 def test_cta_pair_tiles(jc, precision, m, n, k, flags):
-    # shapes with at least one 256 × 256 tile per SM pair run on the two-CTA (cta_group::2) kernel
+    # shapes with at least one 256 × 256 tile per SM pair run on the two-CTA (cta_group::2) kernel; the residual
+    # adds run its staged epilogue (TMA boxes of the residual, clipped at the ragged edges)
     import torch
 
     rng = np.random.default_rng(m + n + k + flags)
