@@ -8,8 +8,9 @@
 //                                    both FP16 (a BF16 V is converted in shared memory)
 //
 // and each thread owns one query row in between: it reads its row of S from TMEM twice (row max, then
-// exp2 and the row sum), applies the row's mask, and writes P as 16-bit values straight into the
-// swizzled A-operand layout. The epilogue reads its row of O from TMEM, divides by the row sum,
+// exp2), applies the row's mask, and writes P as 16-bit values straight into the swizzled A-operand
+// layout. The row sums come from the tensor cores too (P times a 16-column tile of ones, beside the O MMA).
+// The epilogue reads its row of O and its row sum from TMEM, divides by the sum,
 // multiplies the gate (Timestral) and stores 16-byte vectors. Queries past the first 128 (the decoder
 // tokens of a Timestral row, the [REG] and future tokens of a Chronos-2 row) run on the CUDA cores
 // from the same shared-memory K and V, one warp per query.
@@ -40,7 +41,7 @@ struct TcShape {
   int nx;         // live keys past the MMA's 128 (mode 1, at most kTcExtraKeys): CUDA-core scores and P·V
   int o_col;      // first TMEM column of O
   int tmem_cols;  // TMEM columns allocated (power of two)
-  int k_off, v_off, p_off, bar_off;  // byte offsets into the 1024-aligned dynamic shared memory
+  int k_off, v_off, p_off, bar_off, ones_off;  // byte offsets into the 1024-aligned dynamic shared memory
 };
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   // softmax of this thread's row of S into the swizzled FP16 A-operand tile of P. A 32-key chunk no
   // query of the warp may read (past the diagonal of a causal row) is skipped by the whole warp.
   const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  float l = 0.0f;
+  float l = 0.0f;  // the extra keys' share of the row sum; the tile keys' share comes from the row-sum MMA
   if (ok1) {
     float mx = -INFINITY;
 #pragma unroll
@@ -389,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
       tmem_ld_wait();
       if (__all_sync(0xffffffffu, mw == ~0u)) {  // every key of the chunk open to every query of the warp
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+        for (int j = 0; j < 32; j += 2) mx = fmax3(mx, __uint_as_float(r[j]), __uint_as_float(r[j + 1]));
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
@@ -422,7 +423,6 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
           for (int j = 0; j < 32; j += 2) {
             const float p0 = ex2f(fmaf(__uint_as_float(r[j]), sl2, -mo));
             const float p1 = ex2f(fmaf(__uint_as_float(r[j + 1]), sl2, -mo));
-            l += p0 + p1;
             pk[j >> 1] = pack2<__half>(p0, p1);
           }
         } else {
@@ -430,7 +430,6 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
           for (int j = 0; j < 32; j += 2) {
             const float p0 = (mw >> j) & 1u ? ex2f(fmaf(__uint_as_float(r[j]), sl2, -mo)) : 0.0f;
             const float p1 = (mw >> (j + 1)) & 1u ? ex2f(fmaf(__uint_as_float(r[j + 1]), sl2, -mo)) : 0.0f;
-            l += p0 + p1;
             pk[j >> 1] = pack2<__half>(p0, p1);
           }
         }
@@ -447,6 +446,8 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
             make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
     }
   }
+  // the B operand of the row-sum MMA: 16 rows of FP16 ones (2 KB; every 16-key step reads the same atom)
+  reinterpret_cast<uint4*>(smem + sh.ones_off)[tid] = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -456,9 +457,15 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
     // O into TMEM columns [0, 64) (S is consumed); V read MN-major: instruction descriptor bit 16
     const uint32_t idesc = idesc_f32acc(0u, kTcQ, 64) | (1u << 16);  // FP16 P and V
     const uint32_t pa = smem_u32(ps), va = smem_u32(vs);
-    for (int j = 0; j < sh.nkm / 16; ++j)
-      umma_bf16(tmem, sdesc_k_sw128(pa + (j >> 2) * (kTcQ * 128) + 32 * (j & 3)), sdesc_k_sw128(va + 2048 * j), idesc,
-                j > 0);
+    // and the row sums Σ P into TMEM columns [64, 80): P times 16 columns of ones (B K-major), FP32 accumulation
+    // of the FP16 P that the O MMA reads
+    const uint32_t isum = idesc_f32acc(0u, kTcQ, 16);
+    const uint32_t oa = smem_u32(smem + sh.ones_off);
+    for (int j = 0; j < sh.nkm / 16; ++j) {
+      const uint64_t pd = sdesc_k_sw128(pa + (j >> 2) * (kTcQ * 128) + 32 * (j & 3));
+      umma_bf16(tmem, pd, sdesc_k_sw128(va + 2048 * j), idesc, j > 0);
+      umma_bf16(tmem + 64, pd, sdesc_k_sw128(oa + 32 * (j & 3)), isum, j > 0);
+    }
     umma_commit(&bars[2]);
   }
   // this thread's gate row, fetched while the O MMA runs
@@ -474,6 +481,8 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   const bool ok3 = *abort_flag == 0;
   // tcgen05.ld and its wait are warp-collective: every lane runs them, only rows < n store
   if (ok3) {
+    l += __uint_as_float(tmem_ld_32x32b_x1(lane_base + 64));
+    tmem_ld_wait();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     T* op = static_cast<T*>(a.out_hi) + (row0 + q) * a.ld_out + hh * 64;
 #pragma unroll
@@ -557,7 +566,8 @@ cudaError_t launch_time_attention_tc(const AttnArgs& a, cudaStream_t s) {
   // done), else after V
   sh.p_off = p_bytes <= sh.v_off ? 0 : qkv_end;
   sh.bar_off = sh.p_off == 0 ? qkv_end : qkv_end + p_bytes;
-  int smem = sh.bar_off + 3 * 8 + 4 * 10 + 1024;
+  sh.ones_off = (sh.bar_off + 3 * 8 + 4 * 10 + 1023) & ~1023;
+  int smem = sh.ones_off + 2048 + 1024;
   // never more CTAs on an SM than its 512 TMEM columns hold, so no tcgen05.alloc has to wait: ask for
   // enough shared memory that one more CTA would not fit in the SM's 228 KB (1 KB reserved per CTA)
   const int fit = 512 / sh.tmem_cols;
