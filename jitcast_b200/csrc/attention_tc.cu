@@ -12,8 +12,8 @@
 // layout. The row sums come from the tensor cores too (P times a 16-column tile of ones, beside the O MMA).
 // The epilogue reads its row of O and its row sum from TMEM, divides by the sum,
 // multiplies the gate (Timestral) and stores 16-byte vectors. Queries past the first 128 (the decoder
-// tokens of a Timestral row, the [REG] and future tokens of a Chronos-2 row) run on the CUDA cores
-// from the same shared-memory K and V, one warp per query.
+// tokens of a Timestral row, the [REG] and future tokens of a Chronos-2 row) run 8 at a time on the
+// warp-level tensor cores (mma.sync) from the same shared-memory K and V, each warp a quarter of the keys.
 //
 // Masks: BlockLayout.timeAllowed (timestral/BlockLayout.java:209-221; mask mode 0) or per-key
 // liveness in both directions (Chronos-2 ModelLayout; mask mode 1). Semantics: CpuTimestral.java:191-262
@@ -24,6 +24,7 @@
 #include <type_traits>
 
 #include "attention.cuh"
+#include "mma_sync.cuh"
 #include "ptx.cuh"
 
 namespace jc {
@@ -97,6 +98,135 @@ __device__ __forceinline__ uint32_t allowed_word(const AttnArgs& a, const uint32
 }
 
 constexpr int kTailQ = 8;  // queries past the MMA tile handled per round
+constexpr int kTailPitch = 68;  // floats per query row of the partial P·V scratch (64 + 4: no bank conflicts)
+
+// Lane (g, t) = (lane / 4, lane % 4) of a warp's m16n8k16 tile: rows 0..7 are a round's queries (rows 8..15
+// zero); the lane holds query g's A fragments (dims 16k + 2t, +1 and 16k + 8 + 2t, +1 of k-step k), its keys
+// 8j + 2t, +1 of each 8-key n-tile of S and its output dims 8j + 2t, +1.
+template <typename T>
+__device__ __forceinline__ void tail_q(const AttnArgs& a, long long row0, int hh, int t0, int nt, int lane,
+                                       uint32_t (&qa)[4][2]) {
+  const int g = lane >> 2, t = lane & 3;
+  const bool live = g < nt;
+  const uint32_t* qr = reinterpret_cast<const uint32_t*>(static_cast<const T*>(a.qkv) +
+                                                         (row0 + t0 + (live ? g : 0)) * a.ld_qkv + hh * 64);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    qa[k][0] = live ? __ldg(qr + 8 * k + t) : 0u;
+    qa[k][1] = live ? __ldg(qr + 8 * k + 4 + t) : 0u;
+  }
+}
+
+// One round of up to kTailQ queries past the MMA tile (tokens t0 .. t0 + nt), on the four warps' warp-level tensor
+// cores (mma.sync m16n8k16, FP32 accumulation): warp w owns the 16-key steps w, w + 4, .. of the row's keys. It
+// forms S = q·Kᵀ for them (B = the K tile by ldmatrix), applies the mask and publishes its per-query max; after a
+// barrier each warp takes the row max, forms P = 2^(S − max) as FP16 A fragments, publishes its partial sum and
+// its partial O = P·V (B = the FP16 V tile by ldmatrix.trans); after a second barrier a thread per (query, 4 dims)
+// adds the four partials, divides by the row sum, multiplies the gate and stores. Keys the query may not read get
+// probability 0; the K/V rows staged past the row's n tokens hold finite values (the next row's tokens or TMA's
+// zero fill), so they add nothing. The caller orders the scratch against later writes to Q's tile.
+template <typename T>
+__device__ __forceinline__ void tail_round(const AttnArgs& a, const TcShape& sh, const uint32_t* bits, bool known,
+                                           const uint8_t* ks, const uint8_t* vs, long long row0, int hh, int t0,
+                                           int nt, float sl2, int warp, int lane, int tid, const uint32_t (&qa)[4][2],
+                                           float* tmax, float* tsum, float* tpart) {
+  constexpr int KW = kTcMaxTokens / 64;  // k-steps per warp at most
+  const int g = lane >> 2, t = lane & 3;
+  const bool live = g < nt;
+  const int tok = t0 + g;
+  const uint32_t ks_a = smem_u32(ks), vs_a = smem_u32(vs);
+  const int steps = sh.nkl / 16;
+  float s[KW][4];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < KW; ++i) {
+    s[i][0] = s[i][1] = s[i][2] = s[i][3] = -INFINITY;
+    const int kk = warp + 4 * i;
+    if (kk >= steps) continue;  // warp-uniform
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {  // the step's two 8-key n-tiles
+      const int key0 = 16 * kk + 8 * h;
+      uint32_t b[8];
+      const int kr = key0 + (lane & 7);
+      ldsm_x4(ks_a + sw128(kr, 8 * (lane >> 3)), b[0], b[1], b[2], b[3]);
+      ldsm_x4(ks_a + sw128(kr, 32 + 8 * (lane >> 3)), b[4], b[5], b[6], b[7]);
+      float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t av[4] = {qa[k][0], 0u, qa[k][1], 0u};
+        MmaT<T>::mma(c, av, b[2 * k], b[2 * k + 1]);
+      }
+      const int key = key0 + 2 * t;
+      const uint32_t w = live ? allowed_word(a, bits, known, tok, key >> 5) : 0u;
+      if ((w >> (key & 31)) & 1u) s[i][2 * h] = c[0] * sl2;
+      if ((w >> ((key + 1) & 31)) & 1u) s[i][2 * h + 1] = c[1] * sl2;
+    }
+    mx = fmax3(mx, fmax3(s[i][0], s[i][1], s[i][2]), s[i][3]);
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  if (t == 0) tmax[warp * kTailQ + g] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(tmax[g], tmax[kTailQ + g]), fmaxf(tmax[2 * kTailQ + g], tmax[3 * kTailQ + g]));
+  const float base = mx == -INFINITY ? 0.0f : mx;
+  float l = 0.0f;
+  float o[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < KW; ++i) {
+    const int kk = warp + 4 * i;
+    if (kk >= steps) continue;  // warp-uniform
+    float p[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      p[e] = s[i][e] == -INFINITY ? 0.0f : ex2f(s[i][e] - base);
+      l += p[e];
+    }
+    const uint32_t av[4] = {pack2<__half>(p[0], p[1]), 0u, pack2<__half>(p[2], p[3]), 0u};
+    const int vr = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {  // dims 16d .. 16d + 15: two 8-dim n-tiles
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vs_a + sw128(vr, 16 * d + 8 * (lane >> 4)), b0, b1, b2, b3);
+      MmaT<__half>::mma(o[2 * d], av, b0, b1);
+      MmaT<__half>::mma(o[2 * d + 1], av, b2, b3);
+    }
+  }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  if (t == 0) tsum[warp * kTailQ + g] = l;
+  float* part = tpart + (warp * kTailQ + g) * kTailPitch;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) *reinterpret_cast<float2*>(part + 8 * j + 2 * t) = make_float2(o[j][0], o[j][1]);
+  __syncthreads();
+  // a thread per (query, 4 dims): the partials in warp order, 1/l, the gate, one 8-byte store
+  const int qg = tid >> 4, d4 = 4 * (tid & 15);
+  if (qg < nt) {
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float4 v = *reinterpret_cast<const float4*>(tpart + (w * kTailQ + qg) * kTailPitch + d4);
+      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+      sum += tsum[w * kTailQ + qg];
+    }
+    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+    float x[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+    const long long tk = row0 + t0 + qg;
+    if (a.gate) {
+      const uint2 gu = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.gate) + tk * a.ld_gate + hh * 64 + d4));
+      const float2 g0 = unpack2<T>(gu.x), g1 = unpack2<T>(gu.y);
+      x[0] *= g0.x, x[1] *= g0.y, x[2] *= g1.x, x[3] *= g1.y;
+    }
+    if constexpr (std::is_same<T, __half>::value) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[e] = fminf(fmaxf(x[e], -65504.0f), 65504.0f);
+    }
+    *reinterpret_cast<uint2*>(static_cast<T*>(a.out_hi) + tk * a.ld_out + hh * 64 + d4) =
+        make_uint2(pack2<T>(x[0], x[1]), pack2<T>(x[2], x[3]));
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -112,18 +242,16 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3);
   uint32_t* abort_flag = tmem_slot + 1;
   uint32_t* bits = tmem_slot + 2;  // [8]: one bit per key
-  // tail-query scratch in Q's tile once the S MMA has read it: q (fp32), scores then probabilities, row sums
-  float* tq = reinterpret_cast<float*>(qs);                 // [kTailQ][64]
-  float* tsc = tq + kTailQ * 64;                            // [kTailQ][kTcMaxTokens]
-  float* tl = tsc + kTailQ * kTcMaxTokens;                  // [kTailQ]
-  float* tred = tl + kTailQ;                                // [kTcThreads][8] partial P·V sums
+  // tail-round scratch in Q's tile once the S MMA has read it: per warp and query the partial max, sum and P·V
+  float* tmax = reinterpret_cast<float*>(qs);         // [4][kTailQ]
+  float* tsum = tmax + 4 * kTailQ;                     // [4][kTailQ]
+  float* tpart = tsum + 4 * kTailQ;                    // [4][kTailQ][kTailPitch]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hh = blockIdx.x % a.heads;
   const int row = blockIdx.x / a.heads;
   const int n = a.n;
   const bool known = a.mask_mode == 0 && a.known[row] != 0;
-  const T* qkv = static_cast<const T*>(a.qkv);
 
   const long long row0 = static_cast<long long>(row) * n;
   if (tid == 0) {
@@ -159,15 +287,9 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // the first tail round's q and gate rows (queries past the MMA tile), one 16-byte chunk per thread,
-  // in flight during the TMA wait
-  uint4 pq = make_uint4(0u, 0u, 0u, 0u), pg = make_uint4(0u, 0u, 0u, 0u);
-  if (tid < min(kTailQ, n - kTcQ) * 8) {
-    const long long tok = row0 + kTcQ + (tid >> 3);
-    pq = __ldg(reinterpret_cast<const uint4*>(qkv + tok * a.ld_qkv + hh * 64) + (tid & 7));
-    if (a.gate)
-      pg = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.gate) + tok * a.ld_gate + hh * 64) + (tid & 7));
-  }
+  // the first tail round's q fragments (queries past the MMA tile), in flight during the TMA wait
+  uint32_t tqa[4][2];
+  if (n > kTcQ) tail_q<T>(a, row0, hh, kTcQ, min(kTailQ, n - kTcQ), lane, tqa);
   // this thread's query and its allowed keys as bit words
   const int q = tid;
   const bool my_row = q < n;
@@ -238,140 +360,12 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   }
   if (sh.nx > 0) __syncthreads();  // every Q row read before the tail rounds overwrite Q's tile
 
-  // queries past the MMA tile, kTailQ at a time by all threads on the CUDA cores: scores with a thread
-  // per key (its K row in registers), softmax with a warp per query, P·V with a thread per (query, 8 dims)
-  // over a share of the keys, then the shares summed in a fixed order
+  // queries past the MMA tile, kTailQ per round over all four warps (scratch in Q's tile)
   if (ok1) {
     for (int t0 = kTcQ; t0 < n; t0 += kTailQ) {
       const int nt = min(kTailQ, n - t0);
-      if (tid < nt * 8) {
-        uint4 u = pq;
-        if (t0 != kTcQ)
-          u = __ldg(reinterpret_cast<const uint4*>(qkv + (row0 + t0 + (tid >> 3)) * a.ld_qkv + hh * 64) + (tid & 7));
-        const float2 f0 = unpack2<T>(u.x), f1 = unpack2<T>(u.y), f2 = unpack2<T>(u.z), f3 = unpack2<T>(u.w);
-        float4* dst = reinterpret_cast<float4*>(tq + (tid >> 3) * 64 + 8 * (tid & 7));
-        dst[0] = make_float4(f0.x, f0.y, f1.x, f1.y);
-        dst[1] = make_float4(f2.x, f2.y, f3.x, f3.y);
-      }
-      __syncthreads();
-      for (int k = tid; k < sh.nkl; k += kTcThreads) {
-        float kv[64];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint4 u = *reinterpret_cast<const uint4*>(ks + sw128(k, 8 * c));
-          const float2 f0 = unpack2<T>(u.x), f1 = unpack2<T>(u.y), f2 = unpack2<T>(u.z), f3 = unpack2<T>(u.w);
-          kv[8 * c + 0] = f0.x, kv[8 * c + 1] = f0.y, kv[8 * c + 2] = f1.x, kv[8 * c + 3] = f1.y;
-          kv[8 * c + 4] = f2.x, kv[8 * c + 5] = f2.y, kv[8 * c + 6] = f3.x, kv[8 * c + 7] = f3.y;
-        }
-        for (int j = 0; j < nt; ++j) {
-          const float4* qj = reinterpret_cast<const float4*>(tq + j * 64);
-          float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll
-          for (int c = 0; c < 16; c += 2) {
-            const float4 qa = qj[c], qb = qj[c + 1];
-            acc0 = fmaf(qa.x, kv[4 * c + 0], fmaf(qa.y, kv[4 * c + 1], fmaf(qa.z, kv[4 * c + 2], fmaf(qa.w, kv[4 * c + 3], acc0))));
-            acc1 = fmaf(qb.x, kv[4 * c + 4], fmaf(qb.y, kv[4 * c + 5], fmaf(qb.z, kv[4 * c + 6], fmaf(qb.w, kv[4 * c + 7], acc1))));
-          }
-          const bool al = k < n && ((allowed_word(a, bits, known, t0 + j, k >> 5) >> (k & 31)) & 1u);
-          tsc[j * kTcMaxTokens + k] = al ? (acc0 + acc1) * sl2 : -INFINITY;
-        }
-      }
-      __syncthreads();
-      for (int j = warp; j < nt; j += kTcThreads / 32) {
-        float* sj = tsc + j * kTcMaxTokens;
-        float mx = -INFINITY;
-        for (int k = lane; k < sh.nkl; k += 32) mx = fmaxf(mx, sj[k]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float l = 0.0f;
-        for (int k = lane; k < sh.nkl; k += 32) {
-          const float p = sj[k] == -INFINITY ? 0.0f : ex2f(sj[k] - mx);
-          sj[k] = p;
-          l += p;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) tl[j] = l;
-      }
-      __syncthreads();
-      // P·V: a thread owns 8 dims (one 16-byte chunk of a V row) of one query over every G-th key, two keys
-      // per iteration into separate accumulators; keys with p = 0 are skipped by select (their V rows may
-      // hold another row's values)
-      const int items = nt * 8;
-      const int groups = kTcThreads / items;  // ≥ 2 for nt ≤ kTailQ
-      if (tid < items * groups) {
-        const int item = tid % items, g = tid / items;
-        const int j = item >> 3, c = item & 7;
-        const float* pj = tsc + j * kTcMaxTokens;
-        float acc[2][8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc[0][u] = acc[1][u] = 0.0f;
-        int k = g;
-        for (; k + groups < sh.nkl; k += 2 * groups) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int kk = k + h * groups;
-            const float p = pj[kk];
-            const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(kk, 8 * c));
-            const float2 v0 = unpack2<__half>(vv.x), v1 = unpack2<__half>(vv.y), v2 = unpack2<__half>(vv.z),
-                         v3 = unpack2<__half>(vv.w);
-            const float vf[8] = {v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, v3.x, v3.y};
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc[h][u] = p != 0.0f ? fmaf(p, vf[u], acc[h][u]) : acc[h][u];
-          }
-        }
-        if (k < sh.nkl) {
-          const float p = pj[k];
-          const uint4 vv = *reinterpret_cast<const uint4*>(vs + sw128(k, 8 * c));
-          const float2 v0 = unpack2<__half>(vv.x), v1 = unpack2<__half>(vv.y), v2 = unpack2<__half>(vv.z),
-                       v3 = unpack2<__half>(vv.w);
-          const float vf[8] = {v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, v3.x, v3.y};
-#pragma unroll
-          for (int u = 0; u < 8; ++u) acc[0][u] = p != 0.0f ? fmaf(p, vf[u], acc[0][u]) : acc[0][u];
-        }
-        float4* red = reinterpret_cast<float4*>(tred + (g * items + item) * 8);
-        red[0] = make_float4(acc[0][0] + acc[1][0], acc[0][1] + acc[1][1], acc[0][2] + acc[1][2], acc[0][3] + acc[1][3]);
-        red[1] = make_float4(acc[0][4] + acc[1][4], acc[0][5] + acc[1][5], acc[0][6] + acc[1][6], acc[0][7] + acc[1][7]);
-      }
-      __syncthreads();
-      // output: a thread per (query, 16-byte chunk): the shares in order, 1/l, the gate, one vector store
-      if (tid < items) {
-        const int j = tid >> 3, c = tid & 7;
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = 0.0f;
-        for (int g = 0; g < groups; ++g) {
-          const float4* r = reinterpret_cast<const float4*>(tred + (g * items + tid) * 8);
-          const float4 r0 = r[0], r1 = r[1];
-          o[0] += r0.x, o[1] += r0.y, o[2] += r0.z, o[3] += r0.w;
-          o[4] += r1.x, o[5] += r1.y, o[6] += r1.z, o[7] += r1.w;
-        }
-        const float l = tl[j];
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        const long long tok = row0 + t0 + j;
-        uint4 gu = pg;
-        if (a.gate && t0 != kTcQ)
-          gu = __ldg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.gate) + tok * a.ld_gate + hh * 64) + c);
-        const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
-        uint32_t pk[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float x0 = o[2 * u] * inv, x1 = o[2 * u + 1] * inv;
-          if (a.gate) {
-            const float2 g2 = unpack2<T>(gw[u]);
-            x0 *= g2.x;
-            x1 *= g2.y;
-          }
-          if constexpr (std::is_same<T, __half>::value) {
-            x0 = fminf(fmaxf(x0, -65504.0f), 65504.0f);
-            x1 = fminf(fmaxf(x1, -65504.0f), 65504.0f);
-          }
-          pk[u] = pack2<T>(x0, x1);
-        }
-        *reinterpret_cast<uint4*>(static_cast<T*>(a.out_hi) + tok * a.ld_out + hh * 64 + 8 * c) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-      __syncthreads();
+      if (t0 != kTcQ) tail_q<T>(a, row0, hh, t0, nt, lane, tqa);
+      tail_round<T>(a, sh, bits, known, ks, vs, row0, hh, t0, nt, sl2, warp, lane, tid, tqa, tmax, tsum, tpart);
     }
   }
 
@@ -401,6 +395,8 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
 #pragma unroll
       for (int i = 0; i < kTcExtraKeys; ++i) mx = fmaxf(mx, xs[i]);
     }
+    // the last tail round's reads of its scratch end before P is written over Q's tile
+    if (n > kTcQ) __syncthreads();
     const float mo = mx == -INFINITY ? 0.0f : mx * sl2;
     if (sh.nx > 0) {
 #pragma unroll
