@@ -404,6 +404,44 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams& p, int M, int
     }
 }
 
+// Bias and RoPE of one q|k|v head chunk pair: a = the head's columns ca .. ca + 31 (relative to n0), b = the
+// columns hd / 2 further (cb), s = the pair index of a's first column. Pairs from rope_pairs on, and heads past
+// rope_cols (v), keep their values.
+__device__ __forceinline__ void qkv_bias_rope(const EpiParams& p, int n0, int ca, int cb, int s, int pos,
+                                              float (&a)[32], float (&b)[32]) {
+  const int hd = p.head_dim, hh = hd / 2;
+  if (p.bias_on) {
+    add_bias(p, n0 + ca, 32, a);
+    add_bias(p, n0 + cb, 32, b);
+  }
+  // the pairs of this chunk that rotate (a partial rotary factor leaves the rest as they are)
+  const int nr = min(32, (p.rope_pairs > 0 ? p.rope_pairs : hh) - s);
+  if (n0 + ca < p.rope_cols && nr > 0) {
+    float cs[32], sn[32];
+    const float* tc = p.rope_table + (long long)pos * hd + s;
+    if (nr == 16 && p.vec_ok >= 1) {  // a half-rotary head: 16 cos and 16 sin in 16-byte vectors
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(tc) + q);
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(tc + hh) + q);
+        cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
+        sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
+      }
+    } else {
+      load_ro(tc, nr, p.vec_ok, cs);
+      load_ro(tc + hh, nr, p.vec_ok, sn);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < nr) {
+        const float x = a[j], y = b[j];
+        a[j] = x * cs[j] + -y * sn[j];
+        b[j] = y * cs[j] + x * sn[j];
+      }
+    }
+  }
+}
+
 // One accumulator tile (rows m0.., columns n0..) → HBM, for the thread's row. The tile's columns are
 // split into 64-column units (a head of q|k|v in the RoPE mode); `half` (0 or 1) takes every other unit.
 template <int BN>
@@ -472,36 +510,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
         float a[32], b[32];
         load_chunk_pair(tbase + ca, tbase + cb, a, b);
         if (!live) continue;
-        if (p.bias_on) {
-          add_bias(p, n0 + ca, 32, a);
-          add_bias(p, n0 + cb, 32, b);
-        }
-        // the pairs of this chunk that rotate (a partial rotary factor leaves the rest as they are)
-        const int nr = min(32, (p.rope_pairs > 0 ? p.rope_pairs : hh) - s);
-        if (n0 + ca < p.rope_cols && nr > 0) {
-          float cs[32], sn[32];
-          const float* tc = p.rope_table + (long long)pos * hd + s;
-          if (nr == 16 && p.vec_ok >= 1) {  // a half-rotary head: 16 cos and 16 sin in 16-byte vectors
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float4 c4 = __ldg(reinterpret_cast<const float4*>(tc) + q);
-              const float4 s4 = __ldg(reinterpret_cast<const float4*>(tc + hh) + q);
-              cs[4 * q] = c4.x, cs[4 * q + 1] = c4.y, cs[4 * q + 2] = c4.z, cs[4 * q + 3] = c4.w;
-              sn[4 * q] = s4.x, sn[4 * q + 1] = s4.y, sn[4 * q + 2] = s4.z, sn[4 * q + 3] = s4.w;
-            }
-          } else {
-            load_ro(tc, nr, p.vec_ok, cs);
-            load_ro(tc + hh, nr, p.vec_ok, sn);
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (j < nr) {
-              const float x = a[j], y = b[j];
-              a[j] = x * cs[j] + -y * sn[j];
-              b[j] = y * cs[j] + x * sn[j];
-            }
-          }
-        }
+        qkv_bias_rope(p, n0, ca, cb, s, pos, a, b);
         store_operand(p, (long long)orow * p.ldo + n0 + ca, 32, a);
         store_operand(p, (long long)orow * p.ldo + n0 + cb, 32, b);
       }
@@ -845,8 +854,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // from L2 once per 512 output columns instead of once per 256, 25 % fewer operand bytes per FLOP on the L2 → SM
 // path that bounds this kernel; with TMEM full, the next tile's MMAs wait for the epilogue, while the TMA
 // producer keeps filling the stages. Otherwise 256 × 256 tiles with two accumulators.
-// RS > 0: the staged residual epilogue (RESID == 2 below) gives each epilogue warp a ring of RS shared-memory
-// slots of 32 rows × 32 FP32 columns (4 KB, 128-byte swizzle); the operand stages shrink to make room.
+// RS > 0: the staged epilogues (EPI 2 and 3 below) give each epilogue warp a ring of RS shared-memory slots of
+// 4 KB (32 rows × 128 bytes, 128-byte swizzle); the operand stages shrink to make room.
 template <int OPK_, bool WIDE_ = false, int RS_ = 0>
 struct CfgPair {
   static constexpr int OPK = OPK_;
@@ -877,7 +886,7 @@ struct CfgPair {
   static_assert(NACC * BN == TMEM_COLS, "TMEM columns");
 };
 
-// One epilogue warp of the staged residual epilogue (RESID == 2) over the pair's tiles. The warp's chunks form
+// One epilogue warp of the staged residual epilogue (EPI == 2) over the pair's tiles. The warp's chunks form
 // one sequence over its tiles: chunk k of a tile covers the warp's 32 rows (TMEM lanes 32·quarter ..) and the
 // columns n0 + 64·(half + 2·(k / 2)) + 32·(k % 2), k < BN / 64, as in the general epilogue. Chunk j lives in slot
 // j % RS; lane 0 loads chunk j + RS − 1 after chunk j has been stored, once chunk j − 1's store has read its slot
@@ -980,25 +989,111 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
   __syncwarp();
 }
 
-// Slots per epilogue warp of the staged residual ring: three with 256-wide tiles; two beside the wide tiles'
-// 48 KB stages.
-template <bool WIDE>
-constexpr int residual_slots() {
-  return WIDE ? 2 : 3;
+
+// One epilogue warp of the staged q|k|v|gate epilogue (EPI == 3) over the pair's tiles: a 16-bit output per
+// 64-column unit — a head of q|k|v with its bias and RoPE, or 64 gate columns with bias and sigmoid — goes
+// through a slot of the warp's ring (32 rows × 64 16-bit columns, 4 KB, 128-byte swizzle) and out by one
+// bulk-tensor store (P.a2 maps the q|k|v output, P.w2 the gate output, boxes of 64 × 32). Unit j lives in slot
+// j % RS; lane 0 reuses a slot once the store that last read it has done so (one bulk group per unit).
+template <class C>
+__device__ __forceinline__ void staged_qkv_epilogue(const GemmProblem& P, int pair, int pairs, int tiles,
+                                                    uint32_t rank, uint32_t tmem, uint64_t* acc_full,
+                                                    uint32_t acc_empty0, volatile uint32_t* abort_flag,
+                                                    uint32_t* err, uint8_t* ring, int quarter, int half, int lane) {
+  constexpr int BN = C::BN, RS = C::RS;
+  const EpiParams& ep = P.ep;
+  const bool f16 = ep.o_kind == kOutF16;
+  int j = 0;
+  int it = 0;
+  for (int t = pair; t < tiles; t += pairs, ++it) {
+    const int buf = it % C::NACC;
+    const bool got = mbar_wait(acc_full + buf, (it / C::NACC) & 1);
+    if (!(__all_sync(0xffffffffu, got) && !*abort_flag)) {
+      if (lane == 0) atomicOr(err, kErrTimeoutAcc);
+      *abort_flag = 1;
+      break;
+    }
+    tc_fence_after();
+    const int m0 = (t / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (t % P.n_blks) * BN;
+    const int row0 = m0 + quarter * 32, row = row0 + lane;
+    const bool rows_live = row0 < P.M;  // warp-uniform
+    const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
+    const bool heads = n0 < ep.n_split;
+    const int pos = heads && row < P.M ? ep.pos[row] : 0;
+#pragma unroll 1
+    for (int u = half; u < BN / 64; u += 2, ++j) {
+      const int c0 = n0 + 64 * u;
+      if (c0 >= P.N) break;  // warp-uniform
+      float a[32], b[32];
+      load_chunk_pair(tbase + 64 * u, tbase + 64 * u + 32, a, b);
+      if (heads) {
+        qkv_bias_rope(ep, n0, 64 * u, 64 * u + 32, 0, pos, a, b);
+      } else {
+        if (ep.bias_on) {
+          add_bias(ep, c0, 32, a);
+          add_bias(ep, c0 + 32, 32, b);
+        }
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+          a[q] = sigmoid_f(a[q]);
+          b[q] = sigmoid_f(b[q]);
+        }
+      }
+      uint8_t* slot = ring + (j % RS) * C::SLOT_BYTES;
+      if (lane == 0) bulk_wait_read<RS - 1>();  // the store that last read this slot has read it
+      __syncwarp();
+      // the thread's row of the slot: 16-byte chunk q (columns 8q ..) at q ^ (row % 8), the 128-byte swizzle
+      const uint32_t rowp = smem_u32(slot) + lane * 128;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float* v = q < 4 ? a + 8 * q : b + 8 * (q - 4);
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[e] = f16 ? pack_f16(v[2 * e], v[2 * e + 1]) : pack_bf16(v[2 * e], v[2 * e + 1]);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((q ^ (lane & 7)) << 4)), "r"(w[0]),
+                     "r"(w[1]), "r"(w[2]), "r"(w[3])
+                     : "memory");
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (rows_live) {
+          if (heads)
+            tma_store_2d(&P.a2, slot, c0, row0);
+          else
+            tma_store_2d(&P.w2, slot, c0 - ep.n_split, row0);
+        }
+        bulk_commit();
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
+  }
+  if (lane == 0) bulk_wait<0>();
+  __syncwarp();
 }
 
-// RESID: 0 the general epilogue; 1 a residual GEMM with the register-preloading epilogue; 2 a residual GEMM with
-// the staged epilogue. The staged epilogue moves the FP32 residual and the result by TMA: each epilogue warp
+// Slots per epilogue warp of the staged epilogues' rings: the residual epilogue three with 256-wide tiles and two
+// beside the wide tiles' 48 KB stages; the q|k|v|gate epilogue two.
+template <bool WIDE, int EPI>
+constexpr int epi_slots() {
+  return EPI == 2 ? (WIDE ? 2 : 3) : EPI == 3 ? 2 : 0;
+}
+
+// EPI: 0 the general epilogue; 1 a residual GEMM with the register-preloading epilogue; 2 a residual GEMM with
+// the staged epilogue; 3 the staged q|k|v|gate epilogue. The staged epilogues move their outputs (and the
+// residual GEMM its FP32 residual) by TMA through shared memory: each epilogue warp
 // loads its 32 rows × 32 columns of the residual into a slot of its ring two chunks ahead (the next tile's first
 // chunks while the MMAs of that tile still run), adds the accumulator chunk and the bias in place, and stores the
 // slot back with one bulk-tensor store. The residual and the result thereby bypass the per-thread load and store
 // path, whose uncoalesced 32-row requests (one row per thread) kept the SM's L1 busy for most of the epilogue.
-template <int OPK, int G, bool WIDE, int RESID>
+template <int OPK, int G, bool WIDE, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ GemmGroup<G> grp, uint32_t* err) {
-  using C = CfgPair<OPK, WIDE, RESID == 2 ? residual_slots<WIDE>() : 0>;
+  using C = CfgPair<OPK, WIDE, epi_slots<WIDE, EPI>()>;
   constexpr int BN = C::BN;
-  static_assert(RESID != 2 || G == 1, "the staged residual epilogue serves single GEMMs");
+  static_assert(EPI < 2 || G == 1, "the staged epilogues serve single GEMMs");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem + C::STAGES * C::STAGE_BYTES;
@@ -1033,7 +1128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < grp.count; ++i) {
       prefetch_tmap(&grp.p[i].a);
       prefetch_tmap(&grp.p[i].w);
-      if constexpr (RESID == 2) {
+      if constexpr (EPI >= 2) {
         prefetch_tmap(&grp.p[i].a2);
         prefetch_tmap(&grp.p[i].w2);
       }
@@ -1146,7 +1241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;
     const int row_in_tile = quarter * 32 + lane;
     const uint32_t acc_empty0 = mapa_shared(smem_u32(acc_empty), 0);
-    // as in the single-CTA kernel: the residual-preloading loop for a residual GEMM (RESID), else the general one
+    // as in the single-CTA kernel: the residual-preloading loop for a residual GEMM (EPI 1), else the general one
     auto loop = [&](auto pre_tag) {
       constexpr bool PRE = decltype(pre_tag)::value;
       int it = 0;
@@ -1186,11 +1281,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
       }
     };
-    if constexpr (RESID == 2)
+    if constexpr (EPI == 3)
+      staged_qkv_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
+                             ring + (warp - 2) * C::RS * C::SLOT_BYTES, quarter, half, lane);
+    else if constexpr (EPI == 2)
       staged_residual_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
                                   ring + (warp - 2) * C::RS * C::SLOT_BYTES, rbar + (warp - 2) * C::RS, quarter, half,
                                   lane);
-    else if constexpr (RESID == 1)
+    else if constexpr (EPI == 1)
       loop(std::true_type{});
     else
       loop(std::false_type{});
@@ -1355,26 +1453,37 @@ static cudaError_t launch_cfg(const GemmArgs* g, int count, cudaStream_t stream,
   return launch_cfg_r<BN, OPK, G, false>(g, count, stream, err, num_sms);
 }
 
-template <int OPK, int G, bool WIDE, int RESID>
+template <int OPK, int G, bool WIDE, int EPI>
 static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
-  using C = CfgPair<OPK, WIDE, RESID == 2 ? residual_slots<WIDE>() : 0>;
+  using C = CfgPair<OPK, WIDE, epi_slots<WIDE, EPI>()>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK, G, WIDE, RESID>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<OPK, G, WIDE, EPI>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
   GemmGroup<G> grp;
   if (!build_group(grp, g, count, 2 * C::BM, C::BN, C::BM, C::MMA_N / 2)) return cudaErrorInvalidValue;
-  if constexpr (RESID == 2) {
+  if constexpr (EPI == 2) {
     // the staged residual epilogue's 32 × 32 FP32 boxes of C_in (a2) and C (w2)
     const GemmArgs& x = g[0];
     if (!make_map(&grp.p[0].a2, x.ep.cin, kOpTF32, x.M, x.N, x.ep.ldcin, 32) ||
         !make_map(&grp.p[0].w2, x.ep.c, kOpTF32, x.M, x.N, x.ep.ldc, 32))
       return cudaErrorInvalidValue;
+  }
+  if constexpr (EPI == 3) {
+    // the staged q|k|v|gate epilogue's 64 × 32 16-bit boxes of the q|k|v output (a2) and the gate output (w2)
+    const GemmArgs& x = g[0];
+    const int ok = x.ep.o_kind == kOutF16 ? kOpF16 : kOpBF16;
+    if (!make_map(&grp.p[0].a2, x.ep.o_hi, ok, x.M, x.ep.n_split, x.ep.ldo, 32)) return cudaErrorInvalidValue;
+    if (x.N > x.ep.n_split) {
+      if (!make_map(&grp.p[0].w2, x.ep.g_out, ok, x.M, x.N - x.ep.n_split, x.ep.ldg, 32)) return cudaErrorInvalidValue;
+    } else {
+      grp.p[0].w2 = grp.p[0].a2;
+    }
   }
   const int pairs = grp.tiles < num_sms / 2 ? grp.tiles : num_sms / 2;
   cudaLaunchConfig_t cfg = {};
@@ -1389,10 +1498,11 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK, G, WIDE, RESID>, grp, err);
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<OPK, G, WIDE, EPI>, grp, err);
 }
 
-// JC_GEMM_STAGED=0 in the environment keeps residual GEMMs on the register-preloading epilogue (for comparisons).
+// JC_GEMM_STAGED=0 in the environment keeps residual GEMMs on the register-preloading epilogue and q|k|v|gate GEMMs
+// on the general one (for comparisons).
 static bool staged_enabled() {
   static int on = -1;
   if (on < 0) {
@@ -1411,8 +1521,22 @@ static bool residual_staged_ok(const GemmArgs& g) {
          e.ldc >= g.N;
 }
 
+// A q|k|v|gate GEMM whose 16-bit outputs the staged epilogue can store by TMA: 64-wide heads, the gate (if any)
+// in the same 16-bit kind, rows in place, no other output, 16-byte aligned bases and pitches.
+static bool qkv_staged_ok(const GemmArgs& g) {
+  const EpiParams& e = g.ep;
+  const bool o16 = e.o_kind == kOutF16 || e.o_kind == kOutBF16;
+  const bool gate_ok = g.N == e.n_split || (e.g_out && e.g_kind == e.o_kind && aligned16(e.g_out) && e.ldg % 8 == 0);
+  return staged_enabled() && e.mode == kEpiQKV && o16 && gate_ok && e.head_dim == 64 && e.n_split % 64 == 0 &&
+         (g.N - e.n_split) % 64 == 0 && e.o_hi && aligned16(e.o_hi) && e.ldo % 8 == 0 && e.ldo >= e.n_split &&
+         !e.c && !e.rowsq && !e.row_scale && !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
+}
+
 template <int OPK, int G, bool WIDE>
 static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
+  if constexpr (G == 1 && OPK != kOpTF32) {
+    if (qkv_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
+  }
   if constexpr (G == 1) {
     if (residual_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 2>(g, count, stream, err, num_sms);
     if (residual_preloaded(g[0].ep)) return launch_pair_r<OPK, G, WIDE, 1>(g, count, stream, err, num_sms);
