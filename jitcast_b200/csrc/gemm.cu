@@ -990,13 +990,28 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
 }
 
 
-// One epilogue warp of the staged q|k|v|gate epilogue (EPI == 3) over the pair's tiles: a 16-bit output per
-// 64-column unit — a head of q|k|v with its bias and RoPE, or 64 gate columns with bias and sigmoid — goes
-// through a slot of the warp's ring (32 rows × 64 16-bit columns, 4 KB, 128-byte swizzle) and out by one
-// bulk-tensor store (P.a2 maps the q|k|v output, P.w2 the gate output, boxes of 64 × 32). Unit j lives in slot
-// j % RS; lane 0 reuses a slot once the store that last read it has done so (one bulk group per unit).
+// One epilogue warp of the staged 16-bit epilogue (EPI == 3) over the pair's tiles, for the q|k|v|gate and the
+// SwiGLU GEMMs: each 64-column block of 16-bit output — a head of q|k|v with its bias and RoPE, 64 gate columns
+// with bias and sigmoid, or the SwiGLU products of two 64-column tile units — goes through a slot of the warp's
+// ring (32 rows × 64 16-bit columns, 4 KB, 128-byte swizzle) and out by one bulk-tensor store (P.a2 maps the
+// q|k|v or SwiGLU output, P.w2 the gate output, boxes of 64 × 32). Block j lives in slot j % RS; lane 0 reuses a
+// slot once the store that last read it has done so (one bulk group per block).
+// The thread's 32 values as 16-bit into 16-byte chunks q0 .. q0 + 3 of its 128-byte slot row (128-byte swizzle).
+__device__ __forceinline__ void slot_row16(uint32_t rowp, int lane, int q0, bool f16, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[e] = f16 ? pack_f16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]) : pack_bf16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + (((q0 + q) ^ (lane & 7)) << 4)), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3])
+                 : "memory");
+  }
+}
+
 template <class C>
-__device__ __forceinline__ void staged_qkv_epilogue(const GemmProblem& P, int pair, int pairs, int tiles,
+__device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int pair, int pairs, int tiles,
                                                     uint32_t rank, uint32_t tmem, uint64_t* acc_full,
                                                     uint32_t acc_empty0, volatile uint32_t* abort_flag,
                                                     uint32_t* err, uint8_t* ring, int quarter, int half, int lane) {
@@ -1018,47 +1033,59 @@ __device__ __forceinline__ void staged_qkv_epilogue(const GemmProblem& P, int pa
     const int row0 = m0 + quarter * 32, row = row0 + lane;
     const bool rows_live = row0 < P.M;  // warp-uniform
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-    const bool heads = n0 < ep.n_split;
+    const bool swiglu = ep.mode == kEpiSwiGLU;
+    const bool heads = !swiglu && n0 < ep.n_split;
     const int pos = heads && row < P.M ? ep.pos[row] : 0;
+    // SwiGLU: block i = tile units 2i, 2i + 1 → output columns n0 / 2 + 64 i ..; otherwise block i = unit i
 #pragma unroll 1
-    for (int u = half; u < BN / 64; u += 2, ++j) {
-      const int c0 = n0 + 64 * u;
+    for (int i = half; i < (swiglu ? BN / 128 : BN / 64); i += 2, ++j) {
+      const int c0 = n0 + 64 * (swiglu ? 2 * i : i);
       if (c0 >= P.N) break;  // warp-uniform
-      float a[32], b[32];
-      load_chunk_pair(tbase + 64 * u, tbase + 64 * u + 32, a, b);
-      if (heads) {
-        qkv_bias_rope(ep, n0, 64 * u, 64 * u + 32, 0, pos, a, b);
-      } else {
-        if (ep.bias_on) {
-          add_bias(ep, c0, 32, a);
-          add_bias(ep, c0 + 32, 32, b);
-        }
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          a[q] = sigmoid_f(a[q]);
-          b[q] = sigmoid_f(b[q]);
-        }
-      }
       uint8_t* slot = ring + (j % RS) * C::SLOT_BYTES;
+      const uint32_t rowp = smem_u32(slot) + lane * 128;
       if (lane == 0) bulk_wait_read<RS - 1>();  // the store that last read this slot has read it
       __syncwarp();
-      // the thread's row of the slot: 16-byte chunk q (columns 8q ..) at q ^ (row % 8), the 128-byte swizzle
-      const uint32_t rowp = smem_u32(slot) + lane * 128;
+      if (swiglu) {
+        // tile columns 64u .. 64u + 31 are the SiLU half of output columns n0 / 2 + 32u .., 64u + 32 .. the linear one
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int u = 2 * i + h;
+          float a[32], b[32];
+          load_chunk_pair(tbase + 64 * u, tbase + 64 * u + 32, a, b);
+          if (ep.bias_on) {
+            add_bias(ep, n0 + 64 * u, 32, a);
+            add_bias(ep, n0 + 64 * u + 32, 32, b);
+          }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float* v = q < 4 ? a + 8 * q : b + 8 * (q - 4);
-        uint32_t w[4];
+          for (int q = 0; q < 32; ++q) a[q] = silu_f(a[q]) * b[q];
+          slot_row16(rowp, lane, 4 * h, f16, a);
+        }
+      } else {
+        float a[32], b[32];
+        load_chunk_pair(tbase + 64 * i, tbase + 64 * i + 32, a, b);
+        if (heads) {
+          qkv_bias_rope(ep, n0, 64 * i, 64 * i + 32, 0, pos, a, b);
+        } else {
+          if (ep.bias_on) {
+            add_bias(ep, c0, 32, a);
+            add_bias(ep, c0 + 32, 32, b);
+          }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) w[e] = f16 ? pack_f16(v[2 * e], v[2 * e + 1]) : pack_bf16(v[2 * e], v[2 * e + 1]);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + ((q ^ (lane & 7)) << 4)), "r"(w[0]),
-                     "r"(w[1]), "r"(w[2]), "r"(w[3])
-                     : "memory");
+          for (int q = 0; q < 32; ++q) {
+            a[q] = sigmoid_f(a[q]);
+            b[q] = sigmoid_f(b[q]);
+          }
+        }
+        slot_row16(rowp, lane, 0, f16, a);
+        slot_row16(rowp, lane, 4, f16, b);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         if (rows_live) {
-          if (heads)
+          if (swiglu)
+            tma_store_2d(&P.a2, slot, c0 / 2, row0);
+          else if (heads)
             tma_store_2d(&P.a2, slot, c0, row0);
           else
             tma_store_2d(&P.w2, slot, c0 - ep.n_split, row0);
@@ -1282,8 +1309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
     if constexpr (EPI == 3)
-      staged_qkv_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
-                             ring + (warp - 2) * C::RS * C::SLOT_BYTES, quarter, half, lane);
+      staged_16bit_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
+                               ring + (warp - 2) * C::RS * C::SLOT_BYTES, quarter, half, lane);
     else if constexpr (EPI == 2)
       staged_residual_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
                                   ring + (warp - 2) * C::RS * C::SLOT_BYTES, rbar + (warp - 2) * C::RS, quarter, half,
@@ -1475,11 +1502,12 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
       return cudaErrorInvalidValue;
   }
   if constexpr (EPI == 3) {
-    // the staged q|k|v|gate epilogue's 64 × 32 16-bit boxes of the q|k|v output (a2) and the gate output (w2)
+    // the staged 16-bit epilogue's 64 × 32 boxes of the q|k|v or SwiGLU output (a2) and the gate output (w2)
     const GemmArgs& x = g[0];
     const int ok = x.ep.o_kind == kOutF16 ? kOpF16 : kOpBF16;
-    if (!make_map(&grp.p[0].a2, x.ep.o_hi, ok, x.M, x.ep.n_split, x.ep.ldo, 32)) return cudaErrorInvalidValue;
-    if (x.N > x.ep.n_split) {
+    const int o_cols = x.ep.mode == kEpiSwiGLU ? x.N / 2 : x.ep.n_split;
+    if (!make_map(&grp.p[0].a2, x.ep.o_hi, ok, x.M, o_cols, x.ep.ldo, 32)) return cudaErrorInvalidValue;
+    if (x.ep.mode == kEpiQKV && x.N > x.ep.n_split) {
       if (!make_map(&grp.p[0].w2, x.ep.g_out, ok, x.M, x.N - x.ep.n_split, x.ep.ldg, 32)) return cudaErrorInvalidValue;
     } else {
       grp.p[0].w2 = grp.p[0].a2;
@@ -1532,10 +1560,20 @@ static bool qkv_staged_ok(const GemmArgs& g) {
          !e.c && !e.rowsq && !e.row_scale && !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
 }
 
+// A SwiGLU GEMM whose 16-bit output the staged epilogue can store by TMA: whole 128-column unit pairs, rows in
+// place, no other output, a 16-byte aligned base and pitch.
+static bool swiglu_staged_ok(const GemmArgs& g) {
+  const EpiParams& e = g.ep;
+  return staged_enabled() && e.mode == kEpiSwiGLU && (e.o_kind == kOutF16 || e.o_kind == kOutBF16) &&
+         g.N % 128 == 0 && e.o_hi && aligned16(e.o_hi) && e.ldo % 8 == 0 && e.ldo >= g.N / 2 && !e.c && !e.rowsq &&
+         !e.row_scale && !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
+}
+
 template <int OPK, int G, bool WIDE>
 static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
   if constexpr (G == 1 && OPK != kOpTF32) {
-    if (qkv_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
+    if (qkv_staged_ok(g[0]) || swiglu_staged_ok(g[0]))
+      return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
   }
   if constexpr (G == 1) {
     if (residual_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 2>(g, count, stream, err, num_sms);
