@@ -202,13 +202,33 @@ __device__ __forceinline__ void store_operand(const EpiParams& p, long long off,
   }
 }
 
-// Row scale → bias → activation, for one row's 32-column chunk.
-__device__ __forceinline__ void epi_act_chunk(const EpiParams& p, int row, int col0, int nv, float (&v)[32]) {
-  if (p.row_scale) {
-    const float s = p.row_scale[row];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] *= s;
+// A folded RMSNorm's scale of GEMM row `row`: 1 / sqrt(Σ_u norm_sq[row · units + u] / d + eps), the partial sums
+// added in unit order.
+__device__ __forceinline__ float norm_scale(const EpiParams& p, int row) {
+  const float* q = p.norm_sq + (long long)row * p.norm_units;
+  float ss = 0.0f;
+  if ((p.norm_units & 3) == 0) {
+    for (int u = 0; u < p.norm_units; u += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(q + u));
+      ss += v.x;
+      ss += v.y;
+      ss += v.z;
+      ss += v.w;
+    }
+  } else {
+    for (int u = 0; u < p.norm_units; ++u) ss += __ldg(q + u);
   }
+  return 1.0f / sqrtf(ss * p.norm_inv_d + p.norm_eps);
+}
+
+__device__ __forceinline__ void scale32(float (&v)[32], float s) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] *= s;
+}
+
+// Norm scale → bias → activation, for one row's 32-column chunk (rs: the row's norm scale, if the GEMM folds one).
+__device__ __forceinline__ void epi_act_chunk(const EpiParams& p, float rs, int col0, int nv, float (&v)[32]) {
+  if (p.norm_sq) scale32(v, rs);
   if (p.bias_on) add_bias(p, col0, nv, v);
   switch (p.act) {  // one branch per chunk, not per element
     case kActSilu:
@@ -268,9 +288,9 @@ __device__ __forceinline__ void epi_store_chunk(const EpiParams& p, int orow, in
 }
 
 // Bias → activation → accumulate → stores, for one row's 32-column chunk.
-__device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, int row, int orow, int col0, int nv,
+__device__ __forceinline__ void epi_plain_chunk(const EpiParams& p, float rs, int orow, int col0, int nv,
                                                 float (&v)[32], float& sq) {
-  epi_act_chunk(p, row, col0, nv, v);
+  epi_act_chunk(p, rs, col0, nv, v);
   if (p.accumulate) {
     float c[32];
     load_row32(p.cin + (long long)orow * p.ldcin + col0, nv, p.vec_ok, c);
@@ -313,7 +333,7 @@ struct ResidualPre {
 // stream): plain mode, += C into an FP32 C, an optional bias, no activation, no operand-typed copy, no row scale or
 // Σv². Their only registers are the accumulator and residual chunks (the 10-warp CTA gives each thread 168).
 __host__ __device__ __forceinline__ bool residual_preloaded(const EpiParams& p) {
-  return p.mode == kEpiPlain && p.accumulate && p.c && p.act == kActNone && p.o_kind == kOutNone && !p.row_scale &&
+  return p.mode == kEpiPlain && p.accumulate && p.c && p.act == kActNone && p.o_kind == kOutNone && !p.norm_sq &&
          !p.rowsq;
 }
 
@@ -451,11 +471,12 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
   const bool live = row < M;
   const int rr = row % p.rg;
   const int orow = live ? (row / p.rg) * p.rg_stride + rr + p.rg_off + (rr >= p.rg_split ? p.rg_shift : 0) : 0;
-  float sq = 0.0f;
+  const float rs = p.norm_sq && live ? norm_scale(p, row) : 1.0f;
   if (p.mode == kEpiPlain || (p.mode == kEpiQKV && n0 >= p.n_split)) {
     const bool gate = p.mode == kEpiQKV;
 #pragma unroll 1
     for (int u = half; u < BN / 64; u += 2) {
+      float sq = 0.0f;  // Σv² of the unit, for a folded norm's producer
 #pragma unroll 1
       for (int c = 2 * u; c < 2 * u + 2; ++c) {
         const int col0 = n0 + 32 * c;
@@ -465,9 +486,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
         if (!live) continue;
         const int nv = min(32, N - col0);
         if (!gate) {
-          epi_plain_chunk(p, row, orow, col0, nv, v, sq);
+          epi_plain_chunk(p, rs, orow, col0, nv, v, sq);
           continue;
         }
+        if (p.norm_sq) scale32(v, rs);
         if (p.bias_on) add_bias(p, col0, nv, v);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = sigmoid_f(v[j]);
@@ -479,6 +501,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
         else
           store_f32(static_cast<float*>(p.g_out) + off, nv, p.vec_ok, v);
       }
+      if (p.rowsq && live && n0 + 64 * u < N) p.rowsq[(long long)orow * p.rowsq_units + (n0 >> 6) + u] = sq;
     }
   } else if (p.mode == kEpiSwiGLU) {
     // tile columns (64u .. 64u+31) are the SiLU half of output columns (n0/2 + 32u ..), (64u+32 ..) the linear half
@@ -489,6 +512,10 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
       float a[32], b[32];
       load_chunk_pair(tbase + 64 * u, tbase + 64 * u + 32, a, b);
       if (!live) continue;
+      if (p.norm_sq) {
+        scale32(a, rs);
+        scale32(b, rs);
+      }
       if (p.bias_on) {
         add_bias(p, col0, 32, a);
         add_bias(p, col0 + 32, 32, b);
@@ -510,13 +537,16 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
         float a[32], b[32];
         load_chunk_pair(tbase + ca, tbase + cb, a, b);
         if (!live) continue;
+        if (p.norm_sq) {
+          scale32(a, rs);
+          scale32(b, rs);
+        }
         qkv_bias_rope(p, n0, ca, cb, s, pos, a, b);
         store_operand(p, (long long)orow * p.ldo + n0 + ca, 32, a);
         store_operand(p, (long long)orow * p.ldo + n0 + cb, 32, b);
       }
     }
   }
-  if (p.rowsq && live) atomicAdd(p.rowsq + orow, sq);
 }
 
 // Which epilogue warp half (0 or 1) of a TMEM lane quarter reads the tile's 32-column chunk `c` in
@@ -560,7 +590,8 @@ __device__ __forceinline__ void drain_partial(const EpiParams& p, int N, int n0,
 // one persistent grid. G = 1 is the plain single GEMM.
 struct alignas(64) GemmProblem {
   CUtensorMap a, w;    // A [M, K] and W [N, K]
-  CUtensorMap a2, w2;  // the split mode's lo parts (unused otherwise)
+  CUtensorMap a2, w2;  // the split mode's lo parts; the staged epilogues' maps of their outputs and residual
+  CUtensorMap o2;      // the staged residual epilogue's 16-bit copy of its output (a folded norm's producer)
   EpiParams ep;
   int M, N, kblks, n_blks, tile0;
 };
@@ -886,19 +917,38 @@ struct CfgPair {
   static_assert(NACC * BN == TMEM_COLS, "TMEM columns");
 };
 
-// One epilogue warp of the staged residual epilogue (EPI == 2) over the pair's tiles. The warp's chunks form
+// The thread's 32 values as 16-bit into 16-byte chunks q0 .. q0 + 3 of its 128-byte slot row (128-byte swizzle).
+__device__ __forceinline__ void slot_row16(uint32_t rowp, int lane, int q0, bool f16, const float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[e] = f16 ? pack_f16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]) : pack_bf16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + (((q0 + q) ^ (lane & 7)) << 4)), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3])
+                 : "memory");
+  }
+}
+
+// One epilogue warp of the staged residual epilogue (EPI 2, or EPI 4 with NORM) over the pair's tiles. The warp's chunks form
 // one sequence over its tiles: chunk k of a tile covers the warp's 32 rows (TMEM lanes 32·quarter ..) and the
 // columns n0 + 64·(half + 2·(k / 2)) + 32·(k % 2), k < BN / 64, as in the general epilogue. Chunk j lives in slot
 // j % RS; lane 0 loads chunk j + RS − 1 after chunk j has been stored, once chunk j − 1's store has read its slot
 // (one bulk group per chunk). A chunk outside the output (columns ≥ N or rows ≥ M) moves nothing: lane 0 completes
 // its slot's barrier phase with a plain arrival. P.a2 maps the residual C_in and P.w2 the output C, 32 × 32 boxes.
-template <class C>
+// NORM (a folded RMSNorm's producer): the last of the warp's RS slots instead collects each 64-column unit's 16-bit
+// copy of the output, stored by one box of 64 × 32 through P.o2, and each thread stores its row's Σv² over the
+// unit to rowsq. Bulk groups then go FP16 unit store (an empty group when there is none), FP32 chunk store at the
+// end of a unit, FP32 chunk store alone otherwise.
+template <class C, bool NORM>
 __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, int pair, int pairs, int tiles,
                                                          uint32_t rank, uint32_t tmem, uint64_t* acc_full,
                                                          uint32_t acc_empty0, volatile uint32_t* abort_flag,
                                                          uint32_t* err, uint8_t* ring, uint64_t* rbar, int quarter,
                                                          int half, int lane) {
-  constexpr int BN = C::BN, RS = C::RS, KPT = BN / 64;
+  constexpr int BN = C::BN, RS = NORM ? C::RS - 1 : C::RS, KPT = BN / 64;  // RS: the FP32 slots
+  static_assert(RS >= 2, "the FP32 ring needs two slots");
   const int my_tiles = pair < tiles ? (tiles - pair + pairs - 1) / pairs : 0;
   const int jobs = my_tiles * KPT;
   const EpiParams& ep = P.ep;
@@ -922,6 +972,9 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
   int issued = 0;
   if (lane == 0)
     for (; issued < RS - 1 && issued < jobs; ++issued) issue(issued);
+  const bool f16 = ep.o_kind == kOutF16;
+  const uint32_t hrow = smem_u32(ring + RS * C::SLOT_BYTES) + lane * 128;  // NORM: this thread's row of the unit slot
+  float sq = 0.0f;
   bool ok = true;
   int j = 0;
   for (int it = 0; it < my_tiles && ok; ++it) {
@@ -950,6 +1003,10 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
         ok = false;
         break;
       }
+      if (NORM && (k & 1) == 0) {
+        if (lane == 0) bulk_wait_read<1>();  // the last unit's 16-bit store has read the unit slot
+        __syncwarp();
+      }
       if (live) {
         tmem_ld_wait();
         float v[32];
@@ -962,16 +1019,36 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
         for (int q = 0; q < 8; ++q) {
           const uint32_t a = rowp + ((q ^ (lane & 7)) << 4);
           const float4 r = lds_f32x4(a);
-          sts_f32x4(a, make_float4(v[4 * q] + r.x, v[4 * q + 1] + r.y, v[4 * q + 2] + r.z, v[4 * q + 3] + r.w));
+          v[4 * q] += r.x, v[4 * q + 1] += r.y, v[4 * q + 2] += r.z, v[4 * q + 3] += r.w;
+          sts_f32x4(a, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+        }
+        if constexpr (NORM) {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) sq += v[q] * v[q];
+          slot_row16(hrow, lane, 4 * (k & 1), f16, v);
         }
         fence_proxy_async_smem();
       }
       __syncwarp();
+      const bool unit_end = NORM && (k & 1) == 1;
+      if (unit_end) {
+        const int row = row0 + lane;
+        if (live && row < P.M) ep.rowsq[(long long)row * ep.rowsq_units + (col0 >> 6)] = sq;
+        sq = 0.0f;
+      }
       if (lane == 0) {
+        if (unit_end) {
+          if (live) tma_store_2d(&P.o2, ring + RS * C::SLOT_BYTES, col0 - 32, row0);
+          bulk_commit();
+        }
         if (live) tma_store_2d(&P.w2, ring + (j % RS) * C::SLOT_BYTES, col0, row0);
         bulk_commit();
         if (issued < jobs) {
-          bulk_wait_read<1>();  // chunk j − 1's store has read the slot chunk j + RS − 1 reuses
+          // chunk j − 1's store has read the slot chunk j + RS − 1 reuses (the unit's 16-bit store may be pending too)
+          if (unit_end)
+            bulk_wait_read<2>();
+          else
+            bulk_wait_read<1>();
           issue(issued++);
         }
       }
@@ -996,20 +1073,6 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
 // ring (32 rows × 64 16-bit columns, 4 KB, 128-byte swizzle) and out by one bulk-tensor store (P.a2 maps the
 // q|k|v or SwiGLU output, P.w2 the gate output, boxes of 64 × 32). Block j lives in slot j % RS; lane 0 reuses a
 // slot once the store that last read it has done so (one bulk group per block).
-// The thread's 32 values as 16-bit into 16-byte chunks q0 .. q0 + 3 of its 128-byte slot row (128-byte swizzle).
-__device__ __forceinline__ void slot_row16(uint32_t rowp, int lane, int q0, bool f16, const float (&v)[32]) {
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t w[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e)
-      w[e] = f16 ? pack_f16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]) : pack_bf16(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + (((q0 + q) ^ (lane & 7)) << 4)), "r"(w[0]),
-                 "r"(w[1]), "r"(w[2]), "r"(w[3])
-                 : "memory");
-  }
-}
-
 template <class C>
 __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int pair, int pairs, int tiles,
                                                     uint32_t rank, uint32_t tmem, uint64_t* acc_full,
@@ -1036,6 +1099,7 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
     const bool swiglu = ep.mode == kEpiSwiGLU;
     const bool heads = !swiglu && n0 < ep.n_split;
     const int pos = heads && row < P.M ? ep.pos[row] : 0;
+    const float rs = ep.norm_sq && row < P.M ? norm_scale(ep, row) : 1.0f;
     // SwiGLU: block i = tile units 2i, 2i + 1 → output columns n0 / 2 + 64 i ..; otherwise block i = unit i
 #pragma unroll 1
     for (int i = half; i < (swiglu ? BN / 128 : BN / 64); i += 2, ++j) {
@@ -1052,6 +1116,10 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
           const int u = 2 * i + h;
           float a[32], b[32];
           load_chunk_pair(tbase + 64 * u, tbase + 64 * u + 32, a, b);
+          if (ep.norm_sq) {
+            scale32(a, rs);
+            scale32(b, rs);
+          }
           if (ep.bias_on) {
             add_bias(ep, n0 + 64 * u, 32, a);
             add_bias(ep, n0 + 64 * u + 32, 32, b);
@@ -1063,6 +1131,10 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
       } else {
         float a[32], b[32];
         load_chunk_pair(tbase + 64 * i, tbase + 64 * i + 32, a, b);
+        if (ep.norm_sq) {
+          scale32(a, rs);
+          scale32(b, rs);
+        }
         if (heads) {
           qkv_bias_rope(ep, n0, 64 * i, 64 * i + 32, 0, pos, a, b);
         } else {
@@ -1102,14 +1174,16 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
 }
 
 // Slots per epilogue warp of the staged epilogues' rings: the residual epilogue three with 256-wide tiles and two
-// beside the wide tiles' 48 KB stages; the q|k|v|gate epilogue two.
+// beside the wide tiles' 48 KB stages; the 16-bit epilogue two; the residual epilogue of a folded norm's producer
+// three (two FP32 slots and the unit slot of its 16-bit copy; 256-wide tiles only).
 template <bool WIDE, int EPI>
 constexpr int epi_slots() {
-  return EPI == 2 ? (WIDE ? 2 : 3) : EPI == 3 ? 2 : 0;
+  return EPI == 2 ? (WIDE ? 2 : 3) : EPI == 3 ? 2 : EPI == 4 ? 3 : 0;
 }
 
 // EPI: 0 the general epilogue; 1 a residual GEMM with the register-preloading epilogue; 2 a residual GEMM with
-// the staged epilogue; 3 the staged q|k|v|gate epilogue. The staged epilogues move their outputs (and the
+// the staged epilogue; 3 the staged 16-bit (q|k|v|gate, SwiGLU) epilogue; 4 the staged residual epilogue of a
+// folded norm's producer. The staged epilogues move their outputs (and the
 // residual GEMM its FP32 residual) by TMA through shared memory: each epilogue warp
 // loads its 32 rows × 32 columns of the residual into a slot of its ring two chunks ahead (the next tile's first
 // chunks while the MMAs of that tile still run), adds the accumulator chunk and the bias in place, and stores the
@@ -1121,6 +1195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = CfgPair<OPK, WIDE, epi_slots<WIDE, EPI>()>;
   constexpr int BN = C::BN;
   static_assert(EPI < 2 || G == 1, "the staged epilogues serve single GEMMs");
+  static_assert(EPI != 4 || !WIDE, "a folded norm's producer runs 256-wide tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem + C::STAGES * C::STAGE_BYTES;
@@ -1159,6 +1234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tmap(&grp.p[i].a2);
         prefetch_tmap(&grp.p[i].w2);
       }
+      if constexpr (EPI == 4) prefetch_tmap(&grp.p[i].o2);
     }
   }
   if (warp == 1) {
@@ -1311,10 +1387,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (EPI == 3)
       staged_16bit_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
                                ring + (warp - 2) * C::RS * C::SLOT_BYTES, quarter, half, lane);
-    else if constexpr (EPI == 2)
-      staged_residual_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
-                                  ring + (warp - 2) * C::RS * C::SLOT_BYTES, rbar + (warp - 2) * C::RS, quarter, half,
-                                  lane);
+    else if constexpr (EPI == 2 || EPI == 4)
+      staged_residual_epilogue<C, EPI == 4>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag,
+                                            err, ring + (warp - 2) * C::RS * C::SLOT_BYTES, rbar + (warp - 2) * C::RS,
+                                            quarter, half, lane);
     else if constexpr (EPI == 1)
       loop(std::true_type{});
     else
@@ -1415,6 +1491,8 @@ const char* check_gemm(const GemmArgs& g) {
     if ((qkv_tile_choices(e) & 7) == 0) return "no tile width fits the q|k|v|gate layout";
   }
   if (e.accumulate && !e.cin) return "accumulate without C input";
+  if (e.rowsq && e.rowsq_units < (g.N + 63) / 64) return "rowsq needs a partial sum per 64-column unit";
+  if (e.norm_sq && (e.norm_units < 1 || !(e.norm_inv_d > 0.0f))) return "a folded norm needs its unit sums and 1/d";
   if (e.bias_on && !e.bias) return "bias flag without bias";
   if (e.rg < 1) return "row group must be positive";
   return nullptr;
@@ -1494,11 +1572,15 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
   }
   GemmGroup<G> grp;
   if (!build_group(grp, g, count, 2 * C::BM, C::BN, C::BM, C::MMA_N / 2)) return cudaErrorInvalidValue;
-  if constexpr (EPI == 2) {
-    // the staged residual epilogue's 32 × 32 FP32 boxes of C_in (a2) and C (w2)
+  if constexpr (EPI == 2 || EPI == 4) {
+    // the staged residual epilogue's 32 × 32 FP32 boxes of C_in (a2) and C (w2), and the 64 × 32 16-bit boxes of
+    // a norm producer's copy of C (o2)
     const GemmArgs& x = g[0];
     if (!make_map(&grp.p[0].a2, x.ep.cin, kOpTF32, x.M, x.N, x.ep.ldcin, 32) ||
         !make_map(&grp.p[0].w2, x.ep.c, kOpTF32, x.M, x.N, x.ep.ldc, 32))
+      return cudaErrorInvalidValue;
+    if (EPI == 4 &&
+        !make_map(&grp.p[0].o2, x.ep.o_hi, x.ep.o_kind == kOutF16 ? kOpF16 : kOpBF16, x.M, x.N, x.ep.ldo, 32))
       return cudaErrorInvalidValue;
   }
   if constexpr (EPI == 3) {
@@ -1557,7 +1639,7 @@ static bool qkv_staged_ok(const GemmArgs& g) {
   const bool gate_ok = g.N == e.n_split || (e.g_out && e.g_kind == e.o_kind && aligned16(e.g_out) && e.ldg % 8 == 0);
   return staged_enabled() && e.mode == kEpiQKV && o16 && gate_ok && e.head_dim == 64 && e.n_split % 64 == 0 &&
          (g.N - e.n_split) % 64 == 0 && e.o_hi && aligned16(e.o_hi) && e.ldo % 8 == 0 && e.ldo >= e.n_split &&
-         !e.c && !e.rowsq && !e.row_scale && !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
+         !e.c && !e.rowsq && !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
 }
 
 // A SwiGLU GEMM whose 16-bit output the staged epilogue can store by TMA: whole 128-column unit pairs, rows in
@@ -1566,11 +1648,25 @@ static bool swiglu_staged_ok(const GemmArgs& g) {
   const EpiParams& e = g.ep;
   return staged_enabled() && e.mode == kEpiSwiGLU && (e.o_kind == kOutF16 || e.o_kind == kOutBF16) &&
          g.N % 128 == 0 && e.o_hi && aligned16(e.o_hi) && e.ldo % 8 == 0 && e.ldo >= g.N / 2 && !e.c && !e.rowsq &&
-         !e.row_scale && !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
+         !e.accumulate && e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
+}
+
+// A folded norm's producer the staged residual epilogue can run: a residual GEMM as above that also writes a
+// 16-bit copy of C (whole 64-column units) and the per-unit Σv².
+static bool residual_norm_ok(const GemmArgs& g) {
+  const EpiParams& e = g.ep;
+  return staged_enabled() && e.mode == kEpiPlain && e.accumulate && e.c && e.act == kActNone && !e.norm_sq &&
+         e.rowsq && e.rowsq_units == g.N / 64 && g.N % 64 == 0 && (e.o_kind == kOutF16 || e.o_kind == kOutBF16) &&
+         e.o_hi && aligned16(e.o_hi) && e.ldo % 8 == 0 && e.ldo >= g.N && e.rg >= g.M && e.rg_split >= g.M &&
+         e.rg_off == 0 && aligned16(e.cin) && aligned16(e.c) && e.ldcin % 4 == 0 && e.ldc % 4 == 0 && e.ldcin >= g.N &&
+         e.ldc >= g.N;
 }
 
 template <int OPK, int G, bool WIDE>
 static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
+  if constexpr (G == 1 && !WIDE) {
+    if (residual_norm_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 4>(g, count, stream, err, num_sms);
+  }
   if constexpr (G == 1 && OPK != kOpTF32) {
     if (qkv_staged_ok(g[0]) || swiglu_staged_ok(g[0]))
       return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
@@ -1674,7 +1770,8 @@ static cudaError_t launch_group(GemmArgs* g, int count, cudaStream_t stream, uin
     long long wtiles = 0;
     bool fits = true;
     for (int i = 0; i < count; ++i) {
-      fits = fits && g[i].N % 512 == 0 && g[i].K >= 2048;
+      // (a folded norm's producer keeps 256-wide tiles, whose staged epilogue writes its 16-bit copy)
+      fits = fits && g[i].N % 512 == 0 && g[i].K >= 2048 && !g[i].ep.rowsq;
       wtiles += (long long)((g[i].M + 255) / 256) * (g[i].N / 512);
     }
     if (fits && wtiles >= sms / 2) {

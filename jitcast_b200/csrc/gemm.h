@@ -76,10 +76,15 @@ struct EpiParams {
   void* g_out;  // gate output (sigmoid) in OutKind g_kind: kOutF32, kOutBF16 or kOutF16
   long long ldg;
   int g_kind;
-  // Optional: Σ over the row of the fp32 output squared, atomically added per row.
+  // A folded RMSNorm. Its producer (the GEMM that writes the residual stream x) stores, besides x, the Σ of the
+  // squares of the FP32 output over each 64-column unit u: rowsq[out_row · rowsq_units + u] (optional). Its
+  // consumer (the next GEMM, whose A is x's 16-bit copy and whose W holds the norm's weights) scales each output
+  // row by 1 / sqrt(Σ_u norm_sq[row · norm_units + u] · norm_inv_d + norm_eps) before the bias (optional).
   float* rowsq;
-  // Optional: each output row scaled by row_scale[r] before the bias (a folded RMSNorm).
-  const float* row_scale;
+  int rowsq_units;
+  const float* norm_sq;
+  int norm_units;
+  float norm_inv_d, norm_eps;
   int vec_ok;  // all output pointers / leading dims allow 16-byte vector access
 };
 

@@ -120,6 +120,42 @@ __global__ void fill_rows_kernel(float* x, long long ldx, const float* __restric
   }
 }
 
+// The 16-bit copy and the per-64-column-unit Σv² of rows t0 .. t1 − 1 of every group of n rows of x (a folded
+// RMSNorm's producer for rows no GEMM writes): a thread per (row, unit).
+__global__ void norm_copy_rows_kernel(const float* __restrict__ x, long long ldx, int units, int kind, void* xh,
+                                      long long ldh, float* rowsq, int rows, int t0, int t1, int n) {
+  const int h = t1 - t0;
+  const long long total = (long long)rows * h * units;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int u = static_cast<int>(i % units);
+    const long long t = i / units;
+    const long long row = (t / h) * n + t0 + t % h;
+    const float4* src = reinterpret_cast<const float4*>(x + row * ldx + 64 * u);
+    float ss = 0.0f;
+#pragma unroll 4
+    for (int q = 0; q < 16; ++q) {
+      const float4 v = src[q];
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      const long long o = row * ldh + 64 * u + 4 * q;
+      uint2 w;
+      if (kind == kOutBF16) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+        w.x = *reinterpret_cast<uint32_t*>(&a);
+        w.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(xh) + o) = w;
+      } else {
+        __half2 a = __floats2half2_rn(fminf(fmaxf(v.x, -65504.0f), 65504.0f), fminf(fmaxf(v.y, -65504.0f), 65504.0f));
+        __half2 b = __floats2half2_rn(fminf(fmaxf(v.z, -65504.0f), 65504.0f), fminf(fmaxf(v.w, -65504.0f), 65504.0f));
+        w.x = *reinterpret_cast<uint32_t*>(&a);
+        w.y = *reinterpret_cast<uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(xh) + o) = w;
+      }
+    }
+    rowsq[row * units + u] = ss;
+  }
+}
+
 __global__ void add_i32_kernel(const int* __restrict__ in, int* __restrict__ out, long long n, int add) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     out[i] = in[i] + add;
@@ -173,6 +209,13 @@ void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, flo
   }
   rmsnorm_kernel<<<blocks, 256, 0, s>>>(x, ldx, w, cols, eps, out_kind, y_hi, y_lo, ldy, rows, gather_rows,
                                         gather_stride, gather_off);
+}
+
+void launch_norm_copy_rows(const float* x, long long ldx, int cols, int kind, void* xh, long long ldh, float* rowsq,
+                           int rows, int t0, int t1, int n, cudaStream_t s) {
+  const long long total = (long long)rows * (t1 - t0) * (cols / 64);
+  if (total <= 0) return;
+  norm_copy_rows_kernel<<<grid_for(total, 256), 256, 0, s>>>(x, ldx, cols / 64, kind, xh, ldh, rowsq, rows, t0, t1, n);
 }
 
 void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int t0, int t1, int n,

@@ -21,6 +21,12 @@ void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, flo
                     void* y_lo, long long ldy, long long rows, int gather_rows, int gather_stride, int gather_off,
                     cudaStream_t s);
 
+// A folded RMSNorm's producer for rows t0 .. t1 − 1 of every group of n rows of x [.., cols] (cols % 64 == 0, 16-byte
+// aligned rows): their 16-bit copy (kind kOutF16 or kOutBF16) into xh and their Σv² per 64-column unit into
+// rowsq[row · cols / 64 + u].
+void launch_norm_copy_rows(const float* x, long long ldx, int cols, int kind, void* xh, long long ldh, float* rowsq,
+                           int rows, int t0, int t1, int n, cudaStream_t s);
+
 // x[(r·n + t), :] = q for every row r and token t in [t0, t1) (the decoder tokens, a [REG] token).
 void launch_fill_rows(float* x, long long ldx, const float* q, int cols, int rows, int t0, int t1, int n,
                       cudaStream_t s);

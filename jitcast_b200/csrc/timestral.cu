@@ -14,6 +14,7 @@
 // TimestralKernels; the arithmetic is CpuTimestral.predictBlock's (timestral/cpu/CpuTimestral.java:
 // 127-188) between BlockPrep.of and BlockPrep.finish.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -56,6 +57,7 @@ struct TsPlan {
   void* qkv = nullptr;
   void* gate = nullptr;
   float* raw = nullptr;
+  float* rowsq = nullptr;  // the folded norms' Σx² per row and 64-column unit [T, d / 64]
   int *pos = nullptr, *key_valid = nullptr, *known = nullptr, *role = nullptr, *gs = nullptr, *ge = nullptr;
   float* table = nullptr;
   GraphRunner graph;
@@ -84,6 +86,11 @@ struct TimestralEngine : jc_engine {
   int P = 0, d = 0, heads = 0, dh = 0, F = 0, Q = 0, rope_dim = 0;
   float theta = 0, partial = 0, eps = 0;
   int op = kOpBF16;
+  // The 16-bit modes fold the attention and MLP RMSNorms into the GEMMs around them: the GEMM that writes the
+  // residual stream x also writes x's 16-bit copy and its Σx² per 64-column unit, and the next GEMM, whose W
+  // carries the norm's weights, scales each output row by 1 / sqrt(Σx² / d + eps). JC_FOLD_NORM=0 in the
+  // environment keeps the standalone RMSNorm kernel (for comparisons).
+  bool fold_norms = false;
   std::vector<int> kinds;
   std::vector<float> inv_freq;
   std::vector<std::unique_ptr<TsDevice>> devs;
@@ -188,6 +195,11 @@ bool bind_weights(const TimestralEngine& e, const jc_timestral_desc& desc, Binde
   return b.require_all_bound();
 }
 
+// W[:, k] *= g[k]: a folded RMSNorm's weights g moved into the next GEMM's W [rows, cols].
+void scale_columns(std::vector<float>& w, int cols, const float* g) {
+  for (size_t i = 0; i < w.size(); ++i) w[i] *= g[i % cols];
+}
+
 bool upload_weights(TimestralEngine& e, const HostTs& hw, TsDevice& dv, std::string* err) {
   const int d = e.d, p = e.P, F = e.F, Q = e.Q, op = e.op;
   DeviceMem& m = dv.weights;
@@ -206,6 +218,7 @@ bool upload_weights(TimestralEngine& e, const HostTs& hw, TsDevice& dv, std::str
       if (!(ta.norm = upload_f32(m, A.norm, d, err))) return false;
       std::vector<float> q = qkv_heads_major(A.wqkv, d, e.heads, e.dh);
       if (A.gated) q.insert(q.end(), A.gate, A.gate + static_cast<size_t>(d) * d);
+      if (e.fold_norms) scale_columns(q, d, A.norm);
       if (!upload_linear(m, op, q.data(), nullptr, d, A.gated ? 4 * d : 3 * d, &ta.qkvg, err) ||
           !upload_linear(m, op, A.wo, nullptr, d, d, &ta.wo, err))
         return false;
@@ -213,6 +226,7 @@ bool upload_weights(TimestralEngine& e, const HostTs& hw, TsDevice& dv, std::str
     }
     if (!(tl.mlp_norm = upload_f32(m, L.mlp_norm, d, err))) return false;
     std::vector<float> up = swiglu_interleave(L.w12, F, d);
+    if (e.fold_norms) scale_columns(up, d, L.mlp_norm);
     if (!upload_linear(m, op, up.data(), nullptr, d, 2 * F, &tl.w12, err) ||
         !upload_linear(m, op, L.w3, nullptr, F, d, &tl.w3, err))
       return false;
@@ -244,6 +258,7 @@ std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, i
             alloc_op(m, op, T, d, &p->att) && alloc_op(m, op, T, e.F, &p->act) && alloc_op(m, op, decT, d, &p->dec) &&
             alloc_op(m, op, decT, 4 * d, &p->head_h) &&
             (p->raw = static_cast<float*>(m.alloc(sizeof(float) * decT * e.P * e.Q))) &&
+            (!e.fold_norms || (p->rowsq = static_cast<float*>(m.alloc(sizeof(float) * T * (d / 64))))) &&
             (p->pos = static_cast<int*>(m.alloc(sizeof(int) * T))) &&
             (p->key_valid = static_cast<int*>(m.alloc(sizeof(int) * encT))) &&
             (p->known = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
@@ -355,6 +370,23 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
     }                               \
   } while (0)
 
+  const int out_kind = out_of_op(op);
+  // the folded norms (fold_norms): a GEMM that writes x also writes its 16-bit copy into hn and Σx² per unit;
+  // the GEMM that reads hn scales its rows by the norm
+  const bool fold = e.fold_norms;
+  auto produce = [&](GemmArgs& g) {
+    if (!fold) return;
+    set_op_out(g.ep, op, p.hn);
+    g.ep.rowsq = p.rowsq;
+    g.ep.rowsq_units = d / 64;
+  };
+  auto consume = [&](GemmArgs& g) {
+    if (!fold) return;
+    g.ep.norm_sq = p.rowsq;
+    g.ep.norm_units = d / 64;
+    g.ep.norm_inv_d = 1.0f / static_cast<float>(d);
+    g.ep.norm_eps = e.eps;
+  };
   prof.begin(s, "convert", 0);
   launch_convert(op, p.tok_f32, P2, p.tok.hi, p.tok.lo, p.tok.ld, encT, P2, s);
   prof.end(s);
@@ -377,18 +409,23 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
   g.ep.accumulate = 1;
   g.ep.rg = E;
   g.ep.rg_stride = n;
+  produce(g);
   JC_TRY(gemm(dv, g, s, "gemm.embed"));
   prof.begin(s, "fill", 0);
   launch_fill_rows(p.x, d, w.forecast_query, d, R, E, n, n, s);
+  if (fold) launch_norm_copy_rows(p.x, d, d, out_kind, p.hn.hi, p.hn.ld, p.rowsq, R, E, n, n, s);
   prof.end(s);
 
-  const int out_kind = out_of_op(op);
-  for (const TsLayer& L : w.layers) {
+  for (size_t li = 0; li < w.layers.size(); ++li) {
+    const TsLayer& L = w.layers[li];
     for (const TsAttn& A : L.attns) {
-      prof.begin(s, "rmsnorm", 0);
-      launch_rmsnorm(p.x, d, A.norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
-      prof.end(s);
+      if (!fold) {
+        prof.begin(s, "rmsnorm", 0);
+        launch_rmsnorm(p.x, d, A.norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
+        prof.end(s);
+      }
       g = gemm_args(op, p.hn, T, A.qkvg);
+      consume(g);
       g.ep.mode = kEpiQKV;
       g.ep.o_kind = e.qkv_out_kind();
       g.ep.o_hi = p.qkv;
@@ -438,12 +475,16 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       g.ep.cin = p.x;
       g.ep.ldcin = d;
       g.ep.accumulate = 1;
+      produce(g);
       JC_TRY(gemm(dv, g, s, "gemm.wo"));
     }
-    prof.begin(s, "rmsnorm", 0);
-    launch_rmsnorm(p.x, d, L.mlp_norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
-    prof.end(s);
+    if (!fold) {
+      prof.begin(s, "rmsnorm", 0);
+      launch_rmsnorm(p.x, d, L.mlp_norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
+      prof.end(s);
+    }
     g = gemm_args(op, p.hn, T, L.w12);
+    consume(g);
     g.ep.mode = kEpiSwiGLU;
     set_op_out(g.ep, op, p.act);
     JC_TRY(gemm(dv, g, s, "gemm.w12"));
@@ -453,6 +494,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
     g.ep.cin = p.x;
     g.ep.ldcin = d;
     g.ep.accumulate = 1;
+    if (li + 1 < w.layers.size()) produce(g);  // the last x goes to out_norm, which reads it directly
     JC_TRY(gemm(dv, g, s, "gemm.w3"));
   }
   // out_norm on the decoder tokens only (the head reads nothing else), gathered per row
@@ -734,6 +776,10 @@ jc_status jc_engine_create_timestral(const jc_timestral_desc* desc, const jc_ten
   e->eps = c.norm_eps;
   e->rope_dim = static_cast<int>(e->dh * c.rope_partial_factor);
   e->op = op_of_precision(precision);
+  {
+    const char* v = std::getenv("JC_FOLD_NORM");
+    e->fold_norms = op_is_16bit(e->op) && !(v && v[0] == '0');
+  }
   if (e->rope_dim <= 0 || e->rope_dim % 2 != 0)
     return fail(JC_ERR_INVALID_ARG, "rope_partial_factor gives rope_dim " + std::to_string(e->rope_dim));
   if (e->dh != 64)
