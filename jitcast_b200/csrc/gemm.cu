@@ -221,6 +221,31 @@ __device__ __forceinline__ float norm_scale(const EpiParams& p, int row) {
   return 1.0f / sqrtf(ss * p.norm_inv_d + p.norm_eps);
 }
 
+// The folded norm's scale of row row0 + lane (1 for rows ≥ M), for a warp whose lanes own rows row0 .. row0 + 31.
+// With a unit count that is a multiple of 4 the warp reads its rows' partial sums as one contiguous block of
+// 16-byte vectors (coalesced, instead of a 32-row gather per vector), sums each vector, adds the vectors of a row
+// across lanes by shuffles and hands each lane its row's sum. Every epilogue uses it, so their results agree.
+__device__ __forceinline__ float norm_scale_warp(const EpiParams& p, int row0, int lane, int M) {
+  const int U = p.norm_units, F = U >> 2;  // F: vectors per row
+  if ((U & 3) != 0 || (F & (F - 1)) != 0 || F > 32) return row0 + lane < M ? norm_scale(p, row0 + lane) : 1.0f;
+  const float4* blk = reinterpret_cast<const float4*>(p.norm_sq + (long long)row0 * U);
+  const int per = 32 / F;                        // rows per 32 vectors
+  const int valid = max(0, min(32, M - row0)) * F;  // vectors of rows < M
+  float mine = 0.0f;
+  for (int k = 0; k < F; ++k) {
+    const int i = lane + 32 * k;  // vector i: row i / F
+    float s = 0.0f;
+    if (i < valid) {
+      const float4 v = __ldg(blk + i);
+      s = ((v.x + v.y) + v.z) + v.w;
+    }
+    for (int o = 1; o < F; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float t = __shfl_sync(0xffffffffu, s, (lane % per) * F);
+    if (lane / per == k) mine = t;
+  }
+  return row0 + lane < M ? 1.0f / sqrtf(mine * p.norm_inv_d + p.norm_eps) : 1.0f;
+}
+
 __device__ __forceinline__ void scale32(float (&v)[32], float s) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] *= s;
@@ -427,6 +452,20 @@ __device__ __forceinline__ void prefetch_residual(const EpiParams& p, int M, int
 // Bias and RoPE of one q|k|v head chunk pair: a = the head's columns ca .. ca + 31 (relative to n0), b = the
 // columns hd / 2 further (cb), s = the pair index of a's first column. Pairs from rope_pairs on, and heads past
 // rope_cols (v), keep their values.
+template <int NC>
+__device__ __forceinline__ void rope_rotate(float (&a)[32], float (&b)[32], const float (&cs)[NC],
+                                            const float (&sn)[NC], int nr) {
+  // pair j: (a, b) ← (a cos − b sin, b cos + a sin), each product rounded once, the same in every epilogue
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    if (j < nr) {
+      const float x = a[j], y = b[j];
+      a[j] = fmaf(x, cs[j], __fmul_rn(-y, sn[j]));
+      b[j] = fmaf(y, cs[j], __fmul_rn(x, sn[j]));
+    }
+  }
+}
+
 __device__ __forceinline__ void qkv_bias_rope(const EpiParams& p, int n0, int ca, int cb, int s, int pos,
                                               float (&a)[32], float (&b)[32]) {
   const int hd = p.head_dim, hh = hd / 2;
@@ -451,14 +490,7 @@ __device__ __forceinline__ void qkv_bias_rope(const EpiParams& p, int n0, int ca
       load_ro(tc, nr, p.vec_ok, cs);
       load_ro(tc + hh, nr, p.vec_ok, sn);
     }
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (j < nr) {
-        const float x = a[j], y = b[j];
-        a[j] = x * cs[j] + -y * sn[j];
-        b[j] = y * cs[j] + x * sn[j];
-      }
-    }
+    rope_rotate(a, b, cs, sn, nr);
   }
 }
 
@@ -471,7 +503,7 @@ __device__ __forceinline__ void epilogue_tile(const EpiParams& p, int M, int N, 
   const bool live = row < M;
   const int rr = row % p.rg;
   const int orow = live ? (row / p.rg) * p.rg_stride + rr + p.rg_off + (rr >= p.rg_split ? p.rg_shift : 0) : 0;
-  const float rs = p.norm_sq && live ? norm_scale(p, row) : 1.0f;
+  const float rs = p.norm_sq ? norm_scale_warp(p, row - (row_in_tile & 31), row_in_tile & 31, M) : 1.0f;
   if (p.mode == kEpiPlain || (p.mode == kEpiQKV && n0 >= p.n_split)) {
     const bool gate = p.mode == kEpiQKV;
 #pragma unroll 1
@@ -1067,7 +1099,7 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
 }
 
 
-// One epilogue warp of the staged 16-bit epilogue (EPI == 3) over the pair's tiles, for the q|k|v|gate and the
+// One epilogue warp of the staged 16-bit epilogue (EPI 3 or 5) over the pair's tiles, for the q|k|v|gate and the
 // SwiGLU GEMMs: each 64-column block of 16-bit output — a head of q|k|v with its bias and RoPE, 64 gate columns
 // with bias and sigmoid, or the SwiGLU products of two 64-column tile units — goes through a slot of the warp's
 // ring (32 rows × 64 16-bit columns, 4 KB, 128-byte swizzle) and out by one bulk-tensor store (P.a2 maps the
@@ -1078,13 +1110,46 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
                                                     uint32_t rank, uint32_t tmem, uint64_t* acc_full,
                                                     uint32_t acc_empty0, volatile uint32_t* abort_flag,
                                                     uint32_t* err, uint8_t* ring, int quarter, int half, int lane) {
-  constexpr int BN = C::BN, RS = C::RS;
+  constexpr int BN = C::BN;
+  // two output slots; a third, where the ring has one, holds the warp's rows of the packed RoPE table
+  constexpr int RS = 2;
+  constexpr bool TSLOT = C::RS >= 3;
   const EpiParams& ep = P.ep;
   const bool f16 = ep.o_kind == kOutF16;
+  const uint32_t tslot = smem_u32(ring + 2 * C::SLOT_BYTES) + lane * 128;  // this thread's row of the table slot
   int j = 0;
   int it = 0;
   for (int t = pair; t < tiles; t += pairs, ++it) {
     const int buf = it % C::NACC;
+    const int m0 = (t / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (t % P.n_blks) * BN;
+    const int row0 = m0 + quarter * 32, row = row0 + lane;
+    const bool rows_live = row0 < P.M;  // warp-uniform
+    const bool swiglu = ep.mode == kEpiSwiGLU;
+    const bool heads = !swiglu && n0 < ep.n_split;
+    // what the tile's epilogue reads from memory, before it waits for the accumulator: the rows' norm scales, their
+    // positions and (packed table) their RoPE table rows
+    const float rs = ep.norm_sq ? norm_scale_warp(ep, row0, lane, P.M) : 1.0f;
+    const int pos = heads && row < P.M ? ep.pos[row] : 0;
+    const bool packed = TSLOT && heads && ep.rope_pack && n0 < ep.rope_cols && ep.rope_pairs > 0 &&
+                        ep.rope_pairs <= 16;  // warp-uniform
+    if (packed) {
+      __syncwarp();  // the last tile's reads of the table slot are done
+      const int pos0 = __shfl_sync(0xffffffffu, pos, 0);
+      const float4* src = reinterpret_cast<const float4*>(ep.rope_pack);
+      const uint32_t tbase0 = tslot - lane * 128;
+      if (__all_sync(0xffffffffu, row < P.M && pos == pos0 + lane)) {
+        // consecutive positions: one contiguous 4 KB block, read coalesced and spread over the rows
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int i = lane + 32 * k, r = i >> 3, c = i & 7;
+          sts_f32x4(tbase0 + r * 128 + ((c ^ (r & 7)) << 4), __ldg(src + (long long)(pos0 + r) * 8 + c));
+        }
+      } else if (row < P.M) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) sts_f32x4(tslot + ((c ^ (lane & 7)) << 4), __ldg(src + (long long)pos * 8 + c));
+      }
+      __syncwarp();
+    }
     const bool got = mbar_wait(acc_full + buf, (it / C::NACC) & 1);
     if (!(__all_sync(0xffffffffu, got) && !*abort_flag)) {
       if (lane == 0) atomicOr(err, kErrTimeoutAcc);
@@ -1092,14 +1157,7 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
       break;
     }
     tc_fence_after();
-    const int m0 = (t / P.n_blks) * 2 * C::BM + static_cast<int>(rank) * C::BM, n0 = (t % P.n_blks) * BN;
-    const int row0 = m0 + quarter * 32, row = row0 + lane;
-    const bool rows_live = row0 < P.M;  // warp-uniform
     const uint32_t tbase = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + buf * BN;
-    const bool swiglu = ep.mode == kEpiSwiGLU;
-    const bool heads = !swiglu && n0 < ep.n_split;
-    const int pos = heads && row < P.M ? ep.pos[row] : 0;
-    const float rs = ep.norm_sq && row < P.M ? norm_scale(ep, row) : 1.0f;
     // SwiGLU: block i = tile units 2i, 2i + 1 → output columns n0 / 2 + 64 i ..; otherwise block i = unit i
 #pragma unroll 1
     for (int i = half; i < (swiglu ? BN / 128 : BN / 64); i += 2, ++j) {
@@ -1135,7 +1193,23 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
           scale32(a, rs);
           scale32(b, rs);
         }
-        if (heads) {
+        if (heads && packed) {
+          if (ep.bias_on) {
+            add_bias(ep, c0, 32, a);
+            add_bias(ep, c0 + 32, 32, b);
+          }
+          if (c0 < ep.rope_cols) {
+            float cs[16], sn[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 cv = lds_f32x4(tslot + ((q ^ (lane & 7)) << 4));
+              const float4 sv = lds_f32x4(tslot + (((q + 4) ^ (lane & 7)) << 4));
+              cs[4 * q] = cv.x, cs[4 * q + 1] = cv.y, cs[4 * q + 2] = cv.z, cs[4 * q + 3] = cv.w;
+              sn[4 * q] = sv.x, sn[4 * q + 1] = sv.y, sn[4 * q + 2] = sv.z, sn[4 * q + 3] = sv.w;
+            }
+            rope_rotate(a, b, cs, sn, ep.rope_pairs);
+          }
+        } else if (heads) {
           qkv_bias_rope(ep, n0, 64 * i, 64 * i + 32, 0, pos, a, b);
         } else {
           if (ep.bias_on) {
@@ -1174,16 +1248,18 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
 }
 
 // Slots per epilogue warp of the staged epilogues' rings: the residual epilogue three with 256-wide tiles and two
-// beside the wide tiles' 48 KB stages; the 16-bit epilogue two; the residual epilogue of a folded norm's producer
-// three (two FP32 slots and the unit slot of its 16-bit copy; 256-wide tiles only).
+// beside the wide tiles' 48 KB stages; the 16-bit epilogue two output slots, plus a slot for the packed RoPE table
+// rows with 256-wide tiles; the residual epilogue of a folded norm's producer three (two FP32 slots and the unit
+// slot of its 16-bit copy; 256-wide tiles only).
 template <bool WIDE, int EPI>
 constexpr int epi_slots() {
-  return EPI == 2 ? (WIDE ? 2 : 3) : EPI == 3 ? 2 : EPI == 4 ? 3 : 0;
+  return EPI == 2 ? (WIDE ? 2 : 3) : EPI == 3 ? (WIDE ? 2 : 3) : EPI == 4 ? 3 : EPI == 5 ? 2 : 0;
 }
 
 // EPI: 0 the general epilogue; 1 a residual GEMM with the register-preloading epilogue; 2 a residual GEMM with
-// the staged epilogue; 3 the staged 16-bit (q|k|v|gate, SwiGLU) epilogue; 4 the staged residual epilogue of a
-// folded norm's producer. The staged epilogues move their outputs (and the
+// the staged epilogue; 3 the staged 16-bit epilogue of a q|k|v|gate GEMM (with a slot for the packed RoPE rows);
+// 4 the staged residual epilogue of a folded norm's producer; 5 the staged 16-bit epilogue of a SwiGLU GEMM. The
+// staged epilogues move their outputs (and the
 // residual GEMM its FP32 residual) by TMA through shared memory: each epilogue warp
 // loads its 32 rows × 32 columns of the residual into a slot of its ring two chunks ahead (the next tile's first
 // chunks while the MMAs of that tile still run), adds the accumulator chunk and the bias in place, and stores the
@@ -1384,7 +1460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_cluster(acc_empty0 + 8 * buf);
       }
     };
-    if constexpr (EPI == 3)
+    if constexpr (EPI == 3 || EPI == 5)
       staged_16bit_epilogue<C>(grp.p[0], pair, pairs, tiles, rank, tmem, acc_full, acc_empty0, abort_flag, err,
                                ring + (warp - 2) * C::RS * C::SLOT_BYTES, quarter, half, lane);
     else if constexpr (EPI == 2 || EPI == 4)
@@ -1583,7 +1659,7 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
         !make_map(&grp.p[0].o2, x.ep.o_hi, x.ep.o_kind == kOutF16 ? kOpF16 : kOpBF16, x.M, x.N, x.ep.ldo, 32))
       return cudaErrorInvalidValue;
   }
-  if constexpr (EPI == 3) {
+  if constexpr (EPI == 3 || EPI == 5) {
     // the staged 16-bit epilogue's 64 × 32 boxes of the q|k|v or SwiGLU output (a2) and the gate output (w2)
     const GemmArgs& x = g[0];
     const int ok = x.ep.o_kind == kOutF16 ? kOpF16 : kOpBF16;
@@ -1668,8 +1744,8 @@ static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream
     if (residual_norm_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 4>(g, count, stream, err, num_sms);
   }
   if constexpr (G == 1 && OPK != kOpTF32) {
-    if (qkv_staged_ok(g[0]) || swiglu_staged_ok(g[0]))
-      return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
+    if (qkv_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
+    if (swiglu_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 5>(g, count, stream, err, num_sms);
   }
   if constexpr (G == 1) {
     if (residual_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 2>(g, count, stream, err, num_sms);

@@ -72,6 +72,9 @@ struct EpiParams {
   int rope_pairs;
   const int* pos;           // [M] index into rope_table rows
   const float* rope_table;  // [positions, head_dim]: cos at e, sin at head_dim/2 + e
+  // Optional, with rope_pairs ≤ 16: the same values packed [positions, 32]: cos of pairs 0..15, then their sin
+  // (zeros past rope_pairs). The staged epilogue reads a warp's 32 consecutive positions as one 4 KB block.
+  const float* rope_pack;
   int n_split;
   void* g_out;  // gate output (sigmoid) in OutKind g_kind: kOutF32, kOutBF16 or kOutF16
   long long ldg;

@@ -60,6 +60,7 @@ struct TsPlan {
   float* rowsq = nullptr;  // the folded norms' Σx² per row and 64-column unit [T, d / 64]
   int *pos = nullptr, *key_valid = nullptr, *known = nullptr, *role = nullptr, *gs = nullptr, *ge = nullptr;
   float* table = nullptr;
+  float* rope_pack = nullptr;  // the table's rotating pairs packed per position (rope_dim / 2 ≤ 16), or null
   GraphRunner graph;
   std::vector<int> h_pos, h_gs, h_ge;  // host staging of the transformed integer inputs
   // the host ends on the device (jc_forecast_timestral), allocated on first use: per-patch frames and
@@ -265,7 +266,8 @@ std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, i
             (p->role = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
             (p->gs = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
             (p->ge = static_cast<int*>(m.alloc(sizeof(int) * rows))) &&
-            (p->table = static_cast<float*>(m.alloc(sizeof(float) * (2 * enc + h) * e.dh)));
+            (p->table = static_cast<float*>(m.alloc(sizeof(float) * (2 * enc + h) * e.dh))) &&
+            (e.rope_dim / 2 > 16 || (p->rope_pack = static_cast<float*>(m.alloc(sizeof(float) * (2 * enc + h) * 32))));
   if (!ok) {
     cudaGetLastError();
     return nullptr;
@@ -284,6 +286,18 @@ std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, i
   }
   if (cudaMemcpy(p->table, table.data(), sizeof(float) * table.size(), cudaMemcpyHostToDevice) != cudaSuccess)
     return nullptr;
+  if (p->rope_pack) {
+    // per position: cos of the rotating pairs 0 .. rope_dim / 2 − 1 at 0 .., their sin at 16 .. (zeros elsewhere)
+    const int rp = e.rope_dim / 2;
+    std::vector<float> pack(static_cast<size_t>(2 * enc + h) * 32, 0.0f);
+    for (int q = 0; q < 2 * enc + h; ++q)
+      for (int k = 0; k < rp; ++k) {
+        pack[static_cast<size_t>(q) * 32 + k] = table[static_cast<size_t>(q) * e.dh + k];
+        pack[static_cast<size_t>(q) * 32 + 16 + k] = table[static_cast<size_t>(q) * e.dh + half + k];
+      }
+    if (cudaMemcpy(p->rope_pack, pack.data(), sizeof(float) * pack.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+      return nullptr;
+  }
   // every row starts as a valid, independent dummy series (zero tokens, positions 0 .., all keys valid, its
   // own group), so rows past a call's own (bucket padding) compute harmlessly and never reach a real row
   {
@@ -435,6 +449,7 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
       g.ep.rope_pairs = e.rope_dim / 2;  // partial rotary: the pairs past rope_dim/2 keep cos 1, sin 0
       g.ep.pos = p.pos;
       g.ep.rope_table = p.table;
+      g.ep.rope_pack = p.rope_pack;
       g.ep.n_split = 3 * d;
       g.ep.g_out = p.gate;
       g.ep.ldg = d;
