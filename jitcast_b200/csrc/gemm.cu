@@ -1099,9 +1099,10 @@ __device__ __forceinline__ void staged_residual_epilogue(const GemmProblem& P, i
 }
 
 
-// One epilogue warp of the staged 16-bit epilogue (EPI 3 or 5) over the pair's tiles, for the q|k|v|gate and the
-// SwiGLU GEMMs: each 64-column block of 16-bit output — a head of q|k|v with its bias and RoPE, 64 gate columns
-// with bias and sigmoid, or the SwiGLU products of two 64-column tile units — goes through a slot of the warp's
+// One epilogue warp of the staged 16-bit epilogue (EPI 3 or 5) over the pair's tiles, for the q|k|v|gate, the
+// SwiGLU and the plain 16-bit-output GEMMs: each 64-column block of 16-bit output — a head of q|k|v with its bias
+// and RoPE, 64 gate columns with bias and sigmoid, the SwiGLU products of two 64-column tile units, or 64 columns
+// with bias and activation — goes through a slot of the warp's
 // ring (32 rows × 64 16-bit columns, 4 KB, 128-byte swizzle) and out by one bulk-tensor store (P.a2 maps the
 // q|k|v or SwiGLU output, P.w2 the gate output, boxes of 64 × 32). Block j lives in slot j % RS; lane 0 reuses a
 // slot once the store that last read it has done so (one bulk group per block).
@@ -1125,7 +1126,8 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
     const int row0 = m0 + quarter * 32, row = row0 + lane;
     const bool rows_live = row0 < P.M;  // warp-uniform
     const bool swiglu = ep.mode == kEpiSwiGLU;
-    const bool heads = !swiglu && n0 < ep.n_split;
+    const bool plain = ep.mode == kEpiPlain;
+    const bool heads = !swiglu && !plain && n0 < ep.n_split;
     // what the tile's epilogue reads from memory, before it waits for the accumulator: the rows' norm scales, their
     // positions and (packed table) their RoPE table rows
     const float rs = ep.norm_sq ? norm_scale_warp(ep, row0, lane, P.M) : 1.0f;
@@ -1211,6 +1213,10 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
           }
         } else if (heads) {
           qkv_bias_rope(ep, n0, 64 * i, 64 * i + 32, 0, pos, a, b);
+        } else if (plain) {
+          // bias → activation as in the general epilogue (the norm scale is applied above; 1 leaves it exact)
+          epi_act_chunk(ep, 1.0f, c0, 32, a);
+          epi_act_chunk(ep, 1.0f, c0 + 32, 32, b);
         } else {
           if (ep.bias_on) {
             add_bias(ep, c0, 32, a);
@@ -1231,7 +1237,7 @@ __device__ __forceinline__ void staged_16bit_epilogue(const GemmProblem& P, int 
         if (rows_live) {
           if (swiglu)
             tma_store_2d(&P.a2, slot, c0 / 2, row0);
-          else if (heads)
+          else if (heads || plain)
             tma_store_2d(&P.a2, slot, c0, row0);
           else
             tma_store_2d(&P.w2, slot, c0 - ep.n_split, row0);
@@ -1258,7 +1264,8 @@ constexpr int epi_slots() {
 
 // EPI: 0 the general epilogue; 1 a residual GEMM with the register-preloading epilogue; 2 a residual GEMM with
 // the staged epilogue; 3 the staged 16-bit epilogue of a q|k|v|gate GEMM (with a slot for the packed RoPE rows);
-// 4 the staged residual epilogue of a folded norm's producer; 5 the staged 16-bit epilogue of a SwiGLU GEMM. The
+// 4 the staged residual epilogue of a folded norm's producer; 5 the staged 16-bit epilogue of a SwiGLU GEMM or of
+// a plain GEMM with only a 16-bit output. The
 // staged epilogues move their outputs (and the
 // residual GEMM its FP32 residual) by TMA through shared memory: each epilogue warp
 // loads its 32 rows × 32 columns of the residual into a slot of its ring two chunks ahead (the next tile's first
@@ -1663,7 +1670,7 @@ static cudaError_t launch_pair_r(const GemmArgs* g, int count, cudaStream_t stre
     // the staged 16-bit epilogue's 64 × 32 boxes of the q|k|v or SwiGLU output (a2) and the gate output (w2)
     const GemmArgs& x = g[0];
     const int ok = x.ep.o_kind == kOutF16 ? kOpF16 : kOpBF16;
-    const int o_cols = x.ep.mode == kEpiSwiGLU ? x.N / 2 : x.ep.n_split;
+    const int o_cols = x.ep.mode == kEpiSwiGLU ? x.N / 2 : x.ep.mode == kEpiPlain ? x.N : x.ep.n_split;
     if (!make_map(&grp.p[0].a2, x.ep.o_hi, ok, x.M, o_cols, x.ep.ldo, 32)) return cudaErrorInvalidValue;
     if (x.ep.mode == kEpiQKV && x.N > x.ep.n_split) {
       if (!make_map(&grp.p[0].w2, x.ep.g_out, ok, x.M, x.N - x.ep.n_split, x.ep.ldg, 32)) return cudaErrorInvalidValue;
@@ -1738,6 +1745,15 @@ static bool residual_norm_ok(const GemmArgs& g) {
          e.ldc >= g.N;
 }
 
+// A plain GEMM whose only output is 16-bit (an activation's output, such as an FFN's hidden layer) the staged
+// epilogue can store by TMA: whole 64-column units, rows in place, a 16-byte aligned base and pitch.
+static bool plain16_staged_ok(const GemmArgs& g) {
+  const EpiParams& e = g.ep;
+  return staged_enabled() && e.mode == kEpiPlain && (e.o_kind == kOutF16 || e.o_kind == kOutBF16) && g.N % 64 == 0 &&
+         e.o_hi && aligned16(e.o_hi) && e.ldo % 8 == 0 && e.ldo >= g.N && !e.c && !e.rowsq && !e.accumulate &&
+         e.rg >= g.M && e.rg_split >= g.M && e.rg_off == 0;
+}
+
 template <int OPK, int G, bool WIDE>
 static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream, uint32_t* err, int num_sms) {
   if constexpr (G == 1 && !WIDE) {
@@ -1745,7 +1761,8 @@ static cudaError_t launch_pair(const GemmArgs* g, int count, cudaStream_t stream
   }
   if constexpr (G == 1 && OPK != kOpTF32) {
     if (qkv_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 3>(g, count, stream, err, num_sms);
-    if (swiglu_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 5>(g, count, stream, err, num_sms);
+    if (swiglu_staged_ok(g[0]) || plain16_staged_ok(g[0]))
+      return launch_pair_r<OPK, G, WIDE, 5>(g, count, stream, err, num_sms);
   }
   if constexpr (G == 1) {
     if (residual_staged_ok(g[0])) return launch_pair_r<OPK, G, WIDE, 2>(g, count, stream, err, num_sms);
