@@ -39,6 +39,18 @@ __global__ void convert_kernel(int kind, const float* __restrict__ src, long lon
   }
 }
 
+// Columns 0 .. cols − 1 of each destination row only (the destination is a column block of a wider buffer).
+__global__ void convert_cols_kernel(int kind, const float* __restrict__ src, long long lds, void* hi, void* lo,
+                                    long long ldd, long long rows, int cols) {
+  const long long total = rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cols;
+    const int c = static_cast<int>(i - r * cols);
+    put(kind, hi, lo, r * ldd + c, src[r * lds + c]);
+  }
+}
+
 // One warp per output row.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w, int cols,
                                float eps, int kind, void* hi, void* lo, long long ldy, long long rows, int grows,
@@ -175,6 +187,13 @@ void launch_convert(int op, const float* src, long long lds, void* dst_hi, void*
   if (rows <= 0) return;
   convert_kernel<<<grid_for(rows * ldd, 256), 256, 0, s>>>(out_kind_of(op), src, lds, dst_hi, dst_lo, ldd, rows,
                                                            cols);
+}
+
+void launch_convert_cols(int op, const float* src, long long lds, void* dst_hi, void* dst_lo, long long ldd,
+                         long long rows, int cols, cudaStream_t s) {
+  if (rows <= 0 || cols <= 0) return;
+  convert_cols_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(out_kind_of(op), src, lds, dst_hi, dst_lo, ldd, rows,
+                                                                 cols);
 }
 
 void launch_rmsnorm(const float* x, long long ldx, const float* w, int cols, float eps, int out_kind, void* y_hi,

@@ -13,6 +13,10 @@ namespace jc {
 // src is fp32 with row pitch lds. For kOpSplit dst_lo receives the TF32 residual.
 void launch_convert(int op, const float* src, long long lds, void* dst_hi, void* dst_lo, long long ldd, long long rows,
                     int cols, cudaStream_t s);
+// The same conversion into columns 0 .. cols − 1 of each destination row only, leaving the rest of the row (the
+// destination is a column block of a wider buffer).
+void launch_convert_cols(int op, const float* src, long long lds, void* dst_hi, void* dst_lo, long long ldd,
+                         long long rows, int cols, cudaStream_t s);
 
 // y[r, :] = x[r, :] · rsqrt(mean(x[r, :]²) + eps) · w  for rows r, written as operand kind `op`
 // (or fp32 for kOutF32). If gather_* is set, source row = (r / gather_rows) * gather_stride +

@@ -41,7 +41,9 @@ struct TsLayer {
 };
 
 struct TsWeights {
-  DevLinear emb_h, emb_o, emb_r;
+  // the patch embedding: hidden [4d, 2P]; output and residual as one linear over [SiLU(hidden) | tokens]:
+  // [d, 4d + 2P] = [W_out | W_res], bias b_out + b_res
+  DevLinear emb_h, emb_or;
   float* forecast_query = nullptr;
   std::vector<TsLayer> layers;
   float* out_norm = nullptr;
@@ -205,10 +207,20 @@ bool upload_weights(TimestralEngine& e, const HostTs& hw, TsDevice& dv, std::str
   const int d = e.d, p = e.P, F = e.F, Q = e.Q, op = e.op;
   DeviceMem& m = dv.weights;
   TsWeights& w = dv.w;
-  if (!upload_linear(m, op, hw.emb_hw, hw.emb_hb, 2 * p, 4 * d, &w.emb_h, err) ||
-      !upload_linear(m, op, hw.emb_ow, hw.emb_ob, 4 * d, d, &w.emb_o, err) ||
-      !upload_linear(m, op, hw.emb_rw, hw.emb_rb, 2 * p, d, &w.emb_r, err))
-    return false;
+  if (!upload_linear(m, op, hw.emb_hw, hw.emb_hb, 2 * p, 4 * d, &w.emb_h, err)) return false;
+  {
+    // output(SiLU(hidden)) + residual(tokens) as one GEMM over the concatenated K
+    const int K = 4 * d + 2 * p;
+    std::vector<float> wor(static_cast<size_t>(d) * K), bor(d);
+    for (int o = 0; o < d; ++o) {
+      std::memcpy(wor.data() + static_cast<size_t>(o) * K, hw.emb_ow + static_cast<size_t>(o) * 4 * d,
+                  sizeof(float) * 4 * d);
+      std::memcpy(wor.data() + static_cast<size_t>(o) * K + 4 * d, hw.emb_rw + static_cast<size_t>(o) * 2 * p,
+                  sizeof(float) * 2 * p);
+      bor[o] = hw.emb_ob[o] + hw.emb_rb[o];
+    }
+    if (!upload_linear(m, op, wor.data(), bor.data(), K, d, &w.emb_or, err)) return false;
+  }
   if (!(w.forecast_query = upload_f32(m, hw.fq, d, err))) return false;
   for (const auto& L : hw.layers) {
     TsLayer tl;
@@ -253,7 +265,7 @@ std::unique_ptr<TsPlan> make_plan(const TimestralEngine& e, int rows, int enc, i
                   decT = static_cast<long long>(rows) * h;
   DeviceMem& m = p->mem;
   bool ok = (p->tok_f32 = static_cast<float*>(m.alloc(sizeof(float) * encT * 2 * e.P))) &&
-            alloc_op(m, op, encT, 2 * e.P, &p->tok) && alloc_op(m, op, encT, 4 * d, &p->emb_h) &&
+            alloc_op(m, op, encT, 2 * e.P, &p->tok) && alloc_op(m, op, encT, 4 * d + 2 * e.P, &p->emb_h) &&
             (p->x = static_cast<float*>(m.alloc(sizeof(float) * T * d))) && alloc_op(m, op, T, d, &p->hn) &&
             (p->qkv = m.alloc(e.qkv_esize() * T * 3 * d)) && (p->gate = m.alloc(e.qkv_esize() * T * d)) &&
             alloc_op(m, op, T, d, &p->att) && alloc_op(m, op, T, e.F, &p->act) && alloc_op(m, op, decT, d, &p->dec) &&
@@ -401,26 +413,22 @@ cudaError_t enqueue_forward(const TimestralEngine& e, TsDevice& dv, TsPlan& p, c
     g.ep.norm_inv_d = 1.0f / static_cast<float>(d);
     g.ep.norm_eps = e.eps;
   };
+  // the tokens, in the operand format, for the hidden GEMM and as the last 2P columns of its output buffer
+  const size_t esz = op_esize(op);
   prof.begin(s, "convert", 0);
   launch_convert(op, p.tok_f32, P2, p.tok.hi, p.tok.lo, p.tok.ld, encT, P2, s);
+  launch_convert_cols(op, p.tok_f32, P2, static_cast<uint8_t*>(p.emb_h.hi) + 4 * d * esz,
+                      p.emb_h.lo ? static_cast<uint8_t*>(p.emb_h.lo) + 4 * d * esz : nullptr, p.emb_h.ld, encT, P2, s);
   prof.end(s);
-  // patch embedding: output(SiLU(hidden(tok))) + residual(tok), into the encoder rows of x. The two GEMMs of
-  // tok (hidden, and residual stored into x) run as one grouped launch; output then adds into x, the same
-  // float sum as the reference's output + residual
-  GemmArgs ge[2] = {gemm_args(op, p.tok, encT, w.emb_h), gemm_args(op, p.tok, encT, w.emb_r)};
-  ge[0].ep.act = kActSilu;
-  set_op_out(ge[0].ep, op, p.emb_h);
-  ge[1].ep.c = p.x;
-  ge[1].ep.ldc = d;
-  ge[1].ep.rg = E;
-  ge[1].ep.rg_stride = n;
-  JC_TRY(gemm_group(dv, ge, 2, s, "gemm.embed"));
-  GemmArgs g = gemm_args(op, p.emb_h, encT, w.emb_o);
+  // patch embedding: output(SiLU(hidden(tok))) + residual(tok), into the encoder rows of x: hidden into the first
+  // 4d columns of emb_h, then one GEMM over [SiLU(hidden) | tok] with [W_out | W_res] and b_out + b_res
+  GemmArgs g = gemm_args(op, p.tok, encT, w.emb_h);
+  g.ep.act = kActSilu;
+  set_op_out(g.ep, op, p.emb_h);
+  JC_TRY(gemm(dv, g, s, "gemm.embed"));
+  g = gemm_args(op, p.emb_h, encT, w.emb_or);
   g.ep.c = p.x;
   g.ep.ldc = d;
-  g.ep.cin = p.x;
-  g.ep.ldcin = d;
-  g.ep.accumulate = 1;
   g.ep.rg = E;
   g.ep.rg_stride = n;
   produce(g);

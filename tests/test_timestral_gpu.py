@@ -347,7 +347,8 @@ def test_eager_equals_graph_and_profile(jc, tiny):
     np.testing.assert_array_equal(g1, g2)
     np.testing.assert_array_equal(g1, e1)
     gemm_launches = sum(v["launches"] for k, v in prof.items() if k.startswith("gemm"))
-    # embed 2 (hidden and residual grouped, then output), per attention 2, per MLP 2, head 2 (grouped likewise)
+    # embed 2 (hidden, then output and residual as one GEMM over [SiLU(hidden) | tokens]), per attention 2, per
+    # MLP 2, head 2 (hidden and residual grouped, then output)
     assert gemm_launches == 2 + 2 * 5 + 2 * 3 + 2
     assert prof["gemm.embed"]["launches"] == 2 and prof["gemm.head"]["launches"] == 2
     assert prof["gemm.w12"]["launches"] == 3 and prof["gemm.w12"]["ms"] > 0
