@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   float l = 0.0f;  // the extra keys' share of the row sum; the tile keys' share comes from the row-sum MMA
   if (ok1) {
     float mx = -INFINITY;
-#pragma unroll
+#pragma unroll 1  // one copy of each chunk body: the unrolled chunk loops overflowed the instruction cache
     for (int c = 0; c < kTcMaxTokens / 32; ++c) {
       const uint32_t mw = allowed_word(a, bits, known, q, c);
       if (32 * c >= sh.nkm || !__any_sync(0xffffffffu, mw != 0u)) continue;
@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
         l += xs[i];
       }
     }
-#pragma unroll
+#pragma unroll 1
     for (int c = 0; c < kTcMaxTokens / 32; ++c) {
       if (32 * c >= sh.nkm) continue;
       uint32_t pk[16];
