@@ -14,6 +14,7 @@
 // cuBLAS dispatch with a separate ReLU pass (:314-409) and Chronos2Kernels; the arithmetic is
 // CpuChronos2.forward's (chronos2/cpu/CpuChronos2.java:122-173).
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -53,6 +54,7 @@ struct C2Plan {
   float* x = nullptr;
   void* qkv = nullptr;
   float* raw = nullptr;
+  float* rowsq = nullptr;  // the folded norms' Σx² per row and 64-column unit [T, d / 64]
   int *pos = nullptr, *live = nullptr, *gs = nullptr, *ge = nullptr;
   float* table = nullptr;
   GraphRunner graph;
@@ -79,6 +81,10 @@ struct Chronos2Engine : jc_engine {
   int d = 0, dkv = 0, ff = 0, layers = 0, heads = 0, inner = 0, P = 0, Q = 0, reg = 0;
   float eps = 0, theta = 0;
   int op = kOpBF16;
+  // The 16-bit modes fold the attention and MLP norms into the GEMMs around them, as the Timestral engine does:
+  // the GEMM that writes x also writes its 16-bit copy and Σx² per 64-column unit, the next GEMM (whose W carries
+  // the norm's weights) scales its rows by the norm. JC_FOLD_NORM=0 in the environment keeps the norm kernel.
+  bool fold_norms = false;
   std::vector<float> inv_freq;
   std::vector<std::unique_ptr<C2Device>> devs;
 
@@ -166,6 +172,8 @@ bool upload(Chronos2Engine& e, const HostC2& hw, C2Device& dv, std::string* err)
     std::memcpy(qkv.data(), a.q, sizeof(float) * part);
     std::memcpy(qkv.data() + part, a.k, sizeof(float) * part);
     std::memcpy(qkv.data() + 2 * part, a.v, sizeof(float) * part);
+    if (e.fold_norms)
+      for (size_t i = 0; i < qkv.size(); ++i) qkv[i] *= a.norm[i % d];
     return upload_linear(m, op, qkv.data(), nullptr, d, 3 * inner, &t->qkv, err) &&
            upload_linear(m, op, a.o, nullptr, inner, d, &t->o, err);
   };
@@ -173,7 +181,10 @@ bool upload(Chronos2Engine& e, const HostC2& hw, C2Device& dv, std::string* err)
     C2Layer cl;
     if (!attn(L.time, &cl.time) || !attn(L.group, &cl.group)) return false;
     if (!(cl.mlp_norm = upload_f32(m, L.mlp_norm, d, err))) return false;
-    if (!upload_linear(m, op, L.wi, nullptr, d, ff, &cl.wi, err) ||
+    std::vector<float> wi(L.wi, L.wi + static_cast<size_t>(ff) * d);
+    if (e.fold_norms)
+      for (size_t i = 0; i < wi.size(); ++i) wi[i] *= L.mlp_norm[i % d];
+    if (!upload_linear(m, op, wi.data(), nullptr, d, ff, &cl.wi, err) ||
         !upload_linear(m, op, L.wo, nullptr, ff, d, &cl.wo, err))
       return false;
     w.layers.push_back(std::move(cl));
@@ -196,6 +207,7 @@ std::unique_ptr<C2Plan> make_plan(const Chronos2Engine& e, int rows, int nc, int
   bool ok = (p->tok_f32 = static_cast<float*>(m.alloc(sizeof(float) * EN * 3 * e.P))) &&
             alloc_op(m, op, EN, 3 * e.P, &p->tok) && alloc_op(m, op, EN, e.ff, &p->emb_h) &&
             (p->x = static_cast<float*>(m.alloc(sizeof(float) * T * d))) && alloc_op(m, op, T, d, &p->hn) &&
+            (!e.fold_norms || (p->rowsq = static_cast<float*>(m.alloc(sizeof(float) * T * (d / 64))))) &&
             (p->qkv = m.alloc(e.qkv_esize() * T * 3 * e.inner)) && alloc_op(m, op, T, e.inner, &p->att) &&
             alloc_op(m, op, T, e.ff, &p->act) && alloc_op(m, op, decT, d, &p->dec) &&
             alloc_op(m, op, decT, e.ff, &p->head_h) &&
@@ -299,6 +311,22 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   const C2Weights& w = dv.w;
   Profiler& prof = dv.prof;
   const int out_kind = out_of_op(op);
+  // the folded norms (fold_norms): a GEMM that writes x also writes its 16-bit copy into hn and Σx² per unit; the
+  // GEMM that reads hn scales its rows by the norm
+  const bool fold = e.fold_norms;
+  auto produce = [&](GemmArgs& g) {
+    if (!fold) return;
+    set_out(g.ep, op, p.hn);
+    g.ep.rowsq = p.rowsq;
+    g.ep.rowsq_units = d / 64;
+  };
+  auto consume = [&](GemmArgs& g) {
+    if (!fold) return;
+    g.ep.norm_sq = p.rowsq;
+    g.ep.norm_units = d / 64;
+    g.ep.norm_inv_d = 1.0f / static_cast<float>(d);
+    g.ep.norm_eps = e.eps;
+  };
   cudaError_t r;
 #define JC_TRY(x)                   \
   do {                              \
@@ -328,10 +356,12 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   g.ep.rg_stride = n;
   g.ep.rg_split = nc;
   g.ep.rg_shift = reg;
+  produce(g);
   JC_TRY(gemm(dv, g, s, "gemm.embed"));
   if (reg) {
     prof.begin(s, "fill", 0);
     launch_fill_rows(p.x, d, w.reg, d, R, nc, nc + 1, n, s);
+    if (fold) launch_norm_copy_rows(p.x, d, d, out_kind, p.hn.hi, p.hn.ld, p.rowsq, R, nc, nc + 1, n, s);
     prof.end(s);
   }
   AttnArgs a{};
@@ -355,13 +385,17 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
   a.mask_mode = 1;
   a.live = p.live;
   a.err = dv.err;
-  for (const C2Layer& L : w.layers) {
+  for (size_t li = 0; li < w.layers.size(); ++li) {
+    const C2Layer& L = w.layers[li];
     for (int which = 0; which < 2; ++which) {
       const C2Attn& A = which == 0 ? L.time : L.group;
-      prof.begin(s, "rmsnorm", 0);
-      launch_rmsnorm(p.x, d, A.norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
-      prof.end(s);
+      if (!fold) {
+        prof.begin(s, "rmsnorm", 0);
+        launch_rmsnorm(p.x, d, A.norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
+        prof.end(s);
+      }
       g = gemm_args(op, p.hn, T, A.qkv);
+      consume(g);
       g.ep.mode = kEpiQKV;
       g.ep.o_kind = e.qkv_kind();
       g.ep.o_hi = p.qkv;
@@ -377,17 +411,22 @@ cudaError_t enqueue_forward(const Chronos2Engine& e, C2Device& dv, C2Plan& p, cu
       prof.end(s);
       g = gemm_args(op, p.att, T, A.o);
       residual_into(g, p.x, d);
+      produce(g);
       JC_TRY(gemm(dv, g, s, "gemm.o"));
     }
-    prof.begin(s, "rmsnorm", 0);
-    launch_rmsnorm(p.x, d, L.mlp_norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
-    prof.end(s);
+    if (!fold) {
+      prof.begin(s, "rmsnorm", 0);
+      launch_rmsnorm(p.x, d, L.mlp_norm, d, e.eps, out_kind, p.hn.hi, p.hn.lo, p.hn.ld, T, 0, 0, 0, s);
+      prof.end(s);
+    }
     g = gemm_args(op, p.hn, T, L.wi);
+    consume(g);
     g.ep.act = kActRelu;
     set_out(g.ep, op, p.act);
     JC_TRY(gemm(dv, g, s, "gemm.wi"));
     g = gemm_args(op, p.act, T, L.wo);
     residual_into(g, p.x, d);
+    if (li + 1 < w.layers.size()) produce(g);  // the last x goes to final_norm, which reads it directly
     JC_TRY(gemm(dv, g, s, "gemm.wo"));
   }
   prof.begin(s, "rmsnorm", 0);
@@ -634,6 +673,10 @@ jc_status jc_engine_create_chronos2(const jc_chronos2_desc* desc, const jc_tenso
   e->eps = c.layer_norm_eps;
   e->theta = c.rope_theta;
   e->op = op_of_precision(precision);
+  {
+    const char* v = std::getenv("JC_FOLD_NORM");
+    e->fold_norms = op_is_16bit(e->op) && !(v && v[0] == '0');
+  }
   // CpuChronos2.inverseFrequencies (chronos2/cpu/CpuChronos2.java:101-109), in float
   e->inv_freq.resize(e->dkv / 2);
   for (int i = 0; i < e->dkv / 2; ++i) {
