@@ -117,6 +117,15 @@ __device__ __forceinline__ void tail_q(const AttnArgs& a, long long row0, int hh
   }
 }
 
+// The gate values thread tid applies in a tail round (query tid / 16, dims 4·(tid % 16) .. + 3), loaded before the
+// round so that their latency is not on its path; zeros where the thread has no query or there is no gate.
+template <typename T>
+__device__ __forceinline__ uint2 tail_gate(const AttnArgs& a, long long row0, int hh, int t0, int nt, int tid) {
+  const int qg = tid >> 4, d4 = 4 * (tid & 15);
+  if (!a.gate || qg >= nt) return make_uint2(0u, 0u);
+  return __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.gate) + (row0 + t0 + qg) * a.ld_gate + hh * 64 + d4));
+}
+
 // One round of up to kTailQ queries past the MMA tile (tokens t0 .. t0 + nt), on the four warps' warp-level tensor
 // cores (mma.sync m16n8k16, FP32 accumulation): warp w owns the 16-key steps w, w + 4, .. of the row's keys. It
 // forms S = q·Kᵀ for them (B = the K tile by ldmatrix), applies the mask and publishes its per-query max; after a
@@ -129,7 +138,7 @@ template <typename T>
 __device__ __forceinline__ void tail_round(const AttnArgs& a, const TcShape& sh, const uint32_t* bits, bool known,
                                            const uint8_t* ks, const uint8_t* vs, long long row0, int hh, int t0,
                                            int nt, float sl2, int warp, int lane, int tid, const uint32_t (&qa)[4][2],
-                                           float* tmax, float* tsum, float* tpart) {
+                                           uint2 tg, float* tmax, float* tsum, float* tpart) {
   constexpr int KW = kTcMaxTokens / 64;  // k-steps per warp at most
   const int g = lane >> 2, t = lane & 3;
   const bool live = g < nt;
@@ -215,8 +224,7 @@ __device__ __forceinline__ void tail_round(const AttnArgs& a, const TcShape& sh,
     float x[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
     const long long tk = row0 + t0 + qg;
     if (a.gate) {
-      const uint2 gu = __ldg(reinterpret_cast<const uint2*>(static_cast<const T*>(a.gate) + tk * a.ld_gate + hh * 64 + d4));
-      const float2 g0 = unpack2<T>(gu.x), g1 = unpack2<T>(gu.y);
+      const float2 g0 = unpack2<T>(tg.x), g1 = unpack2<T>(tg.y);
       x[0] *= g0.x, x[1] *= g0.y, x[2] *= g1.x, x[3] *= g1.y;
     }
     if constexpr (std::is_same<T, __half>::value) {
@@ -289,7 +297,13 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   const uint32_t tmem = *tmem_slot;
   // the first tail round's q fragments (queries past the MMA tile), in flight during the TMA wait
   uint32_t tqa[4][2];
-  if (n > kTcQ) tail_q<T>(a, row0, hh, kTcQ, min(kTailQ, n - kTcQ), lane, tqa);
+  uint2 tg = make_uint2(0u, 0u);
+  if (n > kTcQ) {
+    tail_q<T>(a, row0, hh, kTcQ, min(kTailQ, n - kTcQ), lane, tqa);
+    tg = tail_gate<T>(a, row0, hh, kTcQ, min(kTailQ, n - kTcQ), tid);
+  }
+  // this thread's gate row on its way into L2 for the epilogue
+  if (a.gate && tid < n) prefetch_l2(static_cast<const T*>(a.gate) + (row0 + tid) * a.ld_gate + hh * 64);
   // this thread's query and its allowed keys as bit words
   const int q = tid;
   const bool my_row = q < n;
@@ -364,8 +378,11 @@ __global__ void __launch_bounds__(kTcThreads, 4) attention_tc_kernel(const __gri
   if (ok1) {
     for (int t0 = kTcQ; t0 < n; t0 += kTailQ) {
       const int nt = min(kTailQ, n - t0);
-      if (t0 != kTcQ) tail_q<T>(a, row0, hh, t0, nt, lane, tqa);
-      tail_round<T>(a, sh, bits, known, ks, vs, row0, hh, t0, nt, sl2, warp, lane, tid, tqa, tmax, tsum, tpart);
+      if (t0 != kTcQ) {
+        tail_q<T>(a, row0, hh, t0, nt, lane, tqa);
+        tg = tail_gate<T>(a, row0, hh, t0, nt, tid);
+      }
+      tail_round<T>(a, sh, bits, known, ks, vs, row0, hh, t0, nt, sl2, warp, lane, tid, tqa, tg, tmax, tsum, tpart);
     }
   }
 
