@@ -675,7 +675,9 @@ jc_status jc_engine_create_chronos2(const jc_chronos2_desc* desc, const jc_tenso
   e->op = op_of_precision(precision);
   {
     const char* v = std::getenv("JC_FOLD_NORM");
-    e->fold_norms = op_is_16bit(e->op) && !(v && v[0] == '0');
+    // the producing epilogues sum x² per 64-column unit of x: a d_model that is not a multiple of 64 keeps
+    // the norm kernels
+    e->fold_norms = op_is_16bit(e->op) && !(v && v[0] == '0') && e->d % 64 == 0;
   }
   // CpuChronos2.inverseFrequencies (chronos2/cpu/CpuChronos2.java:101-109), in float
   e->inv_freq.resize(e->dkv / 2);
