@@ -131,7 +131,8 @@ __device__ __forceinline__ uint2 tail_gate(const AttnArgs& a, long long row0, in
 // forms S = q·Kᵀ for them (B = the K tile by ldmatrix), applies the mask and publishes its per-query max; after a
 // barrier each warp takes the row max, forms P = 2^(S − max) as FP16 A fragments, publishes its partial sum and
 // its partial O = P·V (B = the FP16 V tile by ldmatrix.trans); after a second barrier a thread per (query, 4 dims)
-// adds the four partials, divides by the row sum, multiplies the gate and stores. Keys the query may not read get
+// adds the four partials, divides by the row sum, multiplies the gate (`tg`, from tail_gate before the round) and
+// stores. Keys the query may not read get
 // probability 0; the K/V rows staged past the row's n tokens hold finite values (the next row's tokens or TMA's
 // zero fill), so they add nothing. The caller orders the scratch against later writes to Q's tile.
 template <typename T>
